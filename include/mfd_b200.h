@@ -1,0 +1,139 @@
+/*
+ * mfd_b200.h -- C ABI of the B200-native MFD verify step (libmfd_b200.so, sm_100a).
+ *
+ * Every entry point takes plain device pointers, element counts/strides and a cudaStream_t passed as
+ * void*, launches on that stream without synchronising, allocates nothing (scratch comes from a caller
+ * workspace) and returns an mfd_status; on failure mfd_last_error() describes the problem.  Host
+ * bindings (mfd_b200/_lib.py, ctypes) raise RuntimeError on a nonzero status, as the reference's
+ * TORCH_CHECKs do.  Each declaration names the reference interface it replaces
+ * (hhhhhhy5/multi-future-drafting; "patch" = inference/sglang/patches/sglang-v0.5.22-mfd.patch).
+ */
+#ifndef MFD_B200_H
+#define MFD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mfd_status {
+    MFD_OK = 0,
+    MFD_ERR_INVALID = 1,     /* bad argument: sizes, null pointers, dtype codes */
+    MFD_ERR_UNSUPPORTED = 2, /* sizes beyond this build's limits */
+    MFD_ERR_CUDA = 3,        /* a CUDA call failed */
+    MFD_ERR_CAPACITY = 4     /* a device-side capacity check tripped (reported through a status word) */
+};
+
+enum mfd_dtype { MFD_F32 = 0, MFD_BF16 = 1, MFD_I32 = 2, MFD_I64 = 3 };
+
+/* Thread-local message of the last failed call ("" if none). */
+const char* mfd_last_error(void);
+/* ABI version of this library. */
+int mfd_abi_version(void);
+
+/*
+ * Logits step of tree construction: per row of x [rows, vocab] (row stride in elements), the top k
+ * candidates ordered by value descending, equal values by lower index first, as
+ *   top_logp[r, j] = x[r, ids[r, j]] - logsumexp(x[r, :])   (float32)
+ * plus logz[r] (optional).  One pass over the logits.  k <= min(vocab, 256).
+ * Replaces: inference/hf/ddtree.py:240-244 and 142-146 (torch.topk + torch.logsumexp),
+ *           inference/hf/tree_logits.py:34-46 (row_logsumexp, top_candidates),
+ *           patch:1472-1482 (row_logsumexp) and patch:1530-1545 (DDTreeDraftTopK.__call__ after its GEMM).
+ * Workspace: mfd_topk_logz_workspace() bytes, zero-filled before the first use; the kernel leaves it
+ * ready for the next call (calls sharing one workspace must be stream-ordered).
+ */
+size_t mfd_topk_logz_workspace(int64_t rows, int64_t vocab, int64_t k);
+int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64_t row_stride, int64_t k,
+                  float* top_logp, void* top_ids, int ids_dtype, float* logz, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/*
+ * Exact best-first tree builders, batched, one request per CTA (bit-identical pop order).
+ *   top_logp [bs, K, L, k] float32, top_ids [bs, K, L, k] int32/int64, log_prior [bs, K] (null = zeros).
+ *   single = 1 (K must be 1): the DDTree heap, float64 key -logw, ties by the rank tuple;
+ *   single = 0: the mixture heap, float32 key -(float(logw) + prior), ties by mode, parent, depth, rank,
+ *   a prefix reached again by another mode reuses its node.
+ * Outputs: tree [bs, 3, B+1] int64 (tokens, depths, parents; index 0 = root with token 0, depth 0,
+ * parent -1; tail entries 0 / 0 / -1), counts [bs] int64; optional ancestor-or-self bitsets
+ * anc_bits [bs, B+1, ceil((B+1)/64)] uint64 and/or dense visibility [bs, B+1, B+1] uint8.
+ * status (optional device int) receives MFD_ERR_CAPACITY if a heap store overflows.
+ * Limits: K <= 16, L <= 31, k <= 2047, B <= 511, K * (B + 1) <= 2046.
+ * Replaces: patch:1375-1407 (build_trees / build_trees_cpu, SGLang);
+ *           inference/hf/tree_build_ext.py:118-203 (build_single, build_mixture, finish);
+ *           inference/hf/ddtree.py:161-211 and 259-314 (the Python heaps and the visibility loop).
+ */
+int mfd_build_trees(const float* top_logp, const void* top_ids, int ids_dtype, const float* log_prior, int64_t bs,
+                    int64_t num_modes, int64_t depth_limit, int64_t topk, int64_t budget, int single, int64_t* tree,
+                    int64_t* counts, uint64_t* anc_bits, uint8_t* visibility, int* status, void* stream);
+
+/*
+ * Target token per node and the verified-path walk in one launch.  logits: bf16 rows, row b*width + i
+ * (row stride in elements).  temperature < 1e-5: argmax (first index of the maximum); otherwise one sample
+ * per node by the reproducible rule documented in mfd_b200/csrc/accept.cu, with uniforms [bs*width].
+ * The walk starts at node 0 and follows the child whose token equals the posterior (at most max_steps
+ * edges; < 0 = unbounded).  Outputs (any may be null except posterior): posterior [bs*width];
+ * accept_len [bs] (edges), commit_lens [bs] (= accept_len + 1), bonus [bs], out_tokens [bs, out_len]
+ * (posterior along the path, then the bonus), accepted [bs, out_len] (node indices, -1 past the path),
+ * new_seq_lens [bs] (= prefix + accept_len + 1), move_src/move_tgt [bs, out_len] (window slots),
+ * hidden_index [bs, out_len] (= b*width + node).
+ * Replaces: inference/hf/model/utils.py:28-35 (sample) + inference/hf/ddtree.py:368-382
+ *           (follow_verified_tree) / tree_build_ext.py:70-83 (Tree.follow);
+ *           patch:2986-3010 (_target_tokens) + patch:1844-1885 (ddtree_follow).
+ * Workspace: mfd_accept_workspace(bs) bytes, zero-filled before first use.
+ */
+size_t mfd_accept_workspace(int64_t bs);
+int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab, int64_t bs, int64_t width,
+               const int64_t* tokens, int64_t tokens_stride, const int64_t* parents, int64_t parents_stride,
+               float temperature, const double* uniforms, int64_t max_steps, const int64_t* window,
+               const int64_t* prefix_lens, int64_t out_len, int64_t* posterior, int32_t* accept_len,
+               int32_t* commit_lens, int64_t* bonus, int64_t* out_tokens, int64_t* accepted, int64_t* new_seq_lens,
+               int64_t* move_src, int64_t* move_tgt, int64_t* hidden_index, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* Target token per row only (argmax or the reproducible sample).
+ * Replaces: inference/hf/model/utils.py:28-35 (sample); patch:2986-3010 (_target_tokens). */
+int mfd_sample_tokens(const void* logits, int64_t row_stride, int64_t vocab, int64_t rows, float temperature,
+                      const double* uniforms, int64_t* posterior, void* stream);
+
+/* The walk alone, posterior given [bs, width].  Replaces: patch:1844-1885 (ddtree_follow). */
+int mfd_follow(const int64_t* posterior, const int64_t* tokens, int64_t tokens_stride, const int64_t* parents,
+               int64_t parents_stride, int64_t bs, int64_t width, int64_t max_steps, const int64_t* window,
+               const int64_t* prefix_lens, int64_t out_len, int32_t* accept_len, int32_t* commit_lens,
+               int64_t* bonus, int64_t* out_tokens, int64_t* accepted, int64_t* new_seq_lens, int64_t* move_src,
+               int64_t* move_tgt, int64_t* hidden_index, void* stream);
+
+/*
+ * Verify inputs of a batch of trees: ids [bs, W] (root token at node 0), positions [bs, W] = prefix + depth,
+ * and the flat int8 mask, request b's rows [W, prefix_b + W] at byte offset mask_offsets[b].
+ * Replaces: patch:1625-1703 (_ddtree_verify_inputs_kernel / ddtree_verify_inputs).
+ */
+int mfd_verify_inputs(const int64_t* root_tokens, const int64_t* prefix_lens, const int64_t* tokens,
+                      const int64_t* depths, const int64_t* parents, int64_t tree_stride, const int64_t* mask_offsets,
+                      int64_t bs, int64_t width, int64_t max_depth, int64_t* ids_out, int64_t* positions_out,
+                      int8_t* mask_out, void* stream);
+
+/*
+ * Tree-masked GQA verify attention.  q, out [bs, n, H, 128] bf16 (strides in elements, last dim
+ * contiguous); k, v [bs, Hkv, S, 128] bf16 holding each request's prefix keys followed by its n tree keys;
+ * prefix_lens [bs] int32 on the device (or null: every request uses prefix_len); anc_bits [bs, n, words]
+ * ancestor-or-self bitsets (mfd_build_trees).  Row i sees all prefix keys and the tree keys of its
+ * ancestors and itself.  Flash-decoding over `splits` key ranges, merged by log-sum-exp.
+ * Replaces: the target's SDPA call with the compile_ddtree_tree mask (inference/hf/ddtree.py:352-356,
+ *           598-605); SGLang's flashinfer custom-mask prefill (patch:86-142, 558-592).
+ * Workspace: mfd_tree_attention_workspace(bs, n, H, splits) bytes.
+ */
+size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t splits);
+int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int64_t sq_h, const void* k, int64_t sk_b,
+                       int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
+                       const int32_t* prefix_lens, int64_t prefix_len, const uint64_t* anc_bits, int64_t anc_words,
+                       int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, float scale,
+                       int64_t splits, void* out, int64_t so_b, int64_t so_n, int64_t so_h, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MFD_B200_H */

@@ -1,0 +1,116 @@
+// common.cuh -- shared device helpers for the MFD verify-step kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mfd_b200.h"
+
+#define MFD_FULL_MASK 0xffffffffu
+
+namespace mfd {
+
+// Records a human-readable message for mfd_last_error(); defined in capi.cu.
+void set_error(const char* fmt, ...);
+
+// ------------------------------------------------------------------ orderable keys
+// A float mapped to a uint32 whose unsigned order equals the float order (-inf < ... < +inf < NaN);
+// NaN is canonicalised to the positive quiet NaN first, so every NaN sorts above +inf as torch.topk has it,
+// and -0.0 to +0.0, which compare equal as values (ties between them fall to the index).
+__device__ __forceinline__ uint32_t ord_f32(float v) {
+    uint32_t b = __float_as_uint(v);
+    if ((b & 0x7fffffffu) > 0x7f800000u) b = 0x7fc00000u;
+    if (b == 0x80000000u) b = 0u;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float unord_f32(uint32_t o) {
+    uint32_t b = (o & 0x80000000u) ? (o & 0x7fffffffu) : ~o;
+    return __uint_as_float(b);
+}
+// Top-k key: larger value first, equal values by lower index first.
+__device__ __forceinline__ uint64_t topk_key(float v, uint32_t idx) {
+    return ((uint64_t)ord_f32(v) << 32) | (uint64_t)(~idx);
+}
+__device__ __forceinline__ float key_value(uint64_t k) { return unord_f32((uint32_t)(k >> 32)); }
+__device__ __forceinline__ uint32_t key_index(uint64_t k) { return ~(uint32_t)k; }
+
+// double -> uint64 with the same order (finite and infinite values)
+__device__ __forceinline__ uint64_t ord_f64(double v) {
+    uint64_t b = (uint64_t)__double_as_longlong(v);
+    return (b & 0x8000000000000000ull) ? ~b : (b | 0x8000000000000000ull);
+}
+
+// ------------------------------------------------------------------ loads
+__device__ __forceinline__ float4 ldg_stream_f4(const void* p) {
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf16_at(const uint16_t* p) { return __uint_as_float((uint32_t)(*p) << 16); }
+
+// hardware base-2 exponential (MUFU); relative error about 2^-22
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ------------------------------------------------------------------ warp helpers
+__device__ __forceinline__ uint64_t shfl_u64(uint64_t v, int src) {
+    uint32_t lo = __shfl_sync(MFD_FULL_MASK, (uint32_t)v, src);
+    uint32_t hi = __shfl_sync(MFD_FULL_MASK, (uint32_t)(v >> 32), src);
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) {
+    uint32_t lo = __shfl_xor_sync(MFD_FULL_MASK, (uint32_t)v, m);
+    uint32_t hi = __shfl_xor_sync(MFD_FULL_MASK, (uint32_t)(v >> 32), m);
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ double shfl_f64(double v, int src) {
+    return __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(v), src));
+}
+
+// Warp min of a 64-bit key (all lanes receive it).
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+    uint32_t hi = __reduce_min_sync(MFD_FULL_MASK, (uint32_t)(v >> 32));
+    uint32_t lo = __reduce_min_sync(MFD_FULL_MASK, ((uint32_t)(v >> 32) == hi) ? (uint32_t)v : 0xffffffffu);
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+    uint32_t hi = __reduce_max_sync(MFD_FULL_MASK, (uint32_t)(v >> 32));
+    uint32_t lo = __reduce_max_sync(MFD_FULL_MASK, ((uint32_t)(v >> 32) == hi) ? (uint32_t)v : 0u);
+    return ((uint64_t)hi << 32) | lo;
+}
+
+// online (max, sum of exp(x - max)) pair merge; -inf maxima carry a zero sum
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+    float mn = fmaxf(m, m2);
+    if (mn == -INFINITY) { m = mn; s = 0.f; return; }
+    s = s * fast_exp2((m - mn) * kLog2e) + s2 * fast_exp2((m2 - mn) * kLog2e);
+    m = mn;
+}
+
+}  // namespace mfd
+
+#define MFD_CHECK_LAUNCH(name)                                                  \
+    do {                                                                        \
+        cudaError_t _e = cudaGetLastError();                                    \
+        if (_e != cudaSuccess) {                                                \
+            mfd::set_error("%s: launch failed: %s", name, cudaGetErrorString(_e)); \
+            return MFD_ERR_CUDA;                                                \
+        }                                                                       \
+    } while (0)

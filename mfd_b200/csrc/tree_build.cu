@@ -1,0 +1,462 @@
+// tree_build.cu -- exact best-first tree builders on the GPU, one warp per request.
+//
+// Reproduces the pop order of the reference heaps bit for bit:
+//   mixture (K modes): key = -(float(logw) + prior[mode]) in float32, ties by mode, parent, depth, rank
+//     (inference/hf/tree_build_ext.py:48-62, 158-203; sglang-v0.5.22-mfd.patch:1330-1373);
+//   single mode: key = -logw in float64, ties by the rank tuple (lexicographic), parent, depth, rank
+//     (inference/hf/tree_build_ext.py:31-46, 118-156; patch:1295-1327; inference/hf/ddtree.py:161-192).
+// logw is accumulated in float64 with the reference's operation order: a sibling is
+// (logw - lp[rank]) + lp[rank+1], a child logw + lp[depth][0].  A prefix popped again by another mode
+// reuses its node (dedup by (parent, token) in a shared-memory hash table).
+//
+// Heap representation: the live entries sit in shared memory, each lane of the warp owning the slots
+// lane + 32*j.  The comparator is packed into one 64-bit key (mixture: orderable float32 key in the high
+// word, mode|parent|depth|rank in the low word -- unique per entry, so no further tie-break is ever reached;
+// single mode: the orderable float64 key), each lane caches the minimum of its slots, and a pop is a
+// warp-wide min (two redux.sync) over the cached minima.  Single-mode entries whose float64 keys tie exactly
+// are ordered by rank tuple on a slow path that walks parent pointers.
+//
+// Outputs: the SGLang layout tree[bs, 3, B+1] (tokens, depths, parents; index 0 = root; tail entries
+// tokens 0 / depths 0 / parents -1), counts[bs], and optionally each node's ancestor-or-self set as a
+// bitset anc[bs, B+1, words] and/or a dense uint8 visibility matrix vis[bs, B+1, B+1]
+// (inference/hf/tree_build_ext.py:92-114, ddtree.py:297-305).
+#include "common.cuh"
+
+namespace mfd {
+namespace tree {
+
+constexpr int kThreads = 128;
+constexpr uint64_t kEmptyHash = ~0ull;
+
+struct Params {
+    const float* lp;      // [bs, K, L, k]
+    const void* ids;      // [bs, K, L, k] int32 / int64
+    int ids_i64;
+    const float* prior;   // [bs, K] or null (zeros)
+    int64_t bs;
+    int K, L, k, B;
+    int single;           // single-mode heap (K must be 1)
+    int ks;               // ranks staged in shared memory per (mode, depth) row
+    int S;                // entry slots per lane
+    int hcap;             // hash capacity (power of two)
+    int words;            // 64-bit words per ancestor row
+    int64_t* tree;        // [bs, 3, B+1]
+    int64_t* counts;      // [bs]
+    uint64_t* anc;        // [bs, B+1, words] or null
+    uint8_t* vis;         // [bs, B+1, B+1] or null
+    int* status;          // device status word or null: set to MFD_ERR_CAPACITY on overflow
+};
+
+__device__ __forceinline__ uint32_t pack_aux(int mode, int parent, int depth, int rank) {
+    return ((uint32_t)mode << 28) | ((uint32_t)parent << 16) | ((uint32_t)depth << 11) | (uint32_t)rank;
+}
+
+struct Smem {
+    float* lp;        // [K][L][ks]
+    int32_t* ids;     // [K][L][ks]
+    uint64_t* comp;   // [32*S]
+    double* logw;     // [32*S]
+    uint32_t* aux;    // [32*S]
+    int32_t* ntok;    // [B+1]
+    int16_t* npar;    // [B+1]
+    uint8_t* ndep;    // [B+1]
+    int16_t* nrank;   // [B+1]
+    uint64_t* hash;   // [hcap]
+    float* prior;     // [K]
+};
+
+__device__ __forceinline__ float lp_at(const Params& p, const Smem& s, const float* glp, int m, int d, int r) {
+    if (r < p.ks) return s.lp[(m * p.L + d) * p.ks + r];
+    return glp[((size_t)m * p.L + d) * p.k + r];
+}
+__device__ __forceinline__ int64_t id_at(const Params& p, const Smem& s, const void* gids, int m, int d, int r) {
+    if (r < p.ks) return s.ids[(m * p.L + d) * p.ks + r];
+    const size_t o = ((size_t)m * p.L + d) * p.k + r;
+    return p.ids_i64 ? ((const int64_t*)gids)[o] : (int64_t)((const int32_t*)gids)[o];
+}
+
+// rank tuple of a prospective node (parent `par`, own rank `rk`, depth `dep`), root-first, into t[0..dep)
+__device__ __forceinline__ void rank_tuple(const Smem& s, int par, int rk, int dep, int16_t* t) {
+    t[dep - 1] = (int16_t)rk;
+    int node = par;
+    for (int d = dep - 2; d >= 0; --d) {
+        t[d] = s.nrank[node];
+        node = s.npar[node];
+    }
+}
+// lexicographic comparison of rank tuples (shorter first when one is a prefix), as Python tuples compare
+__device__ __forceinline__ int tuple_cmp(const int16_t* a, int na, const int16_t* b, int nb) {
+    const int n = na < nb ? na : nb;
+    for (int i = 0; i < n; ++i)
+        if (a[i] != b[i]) return a[i] < b[i] ? -1 : 1;
+    return na == nb ? 0 : (na < nb ? -1 : 1);
+}
+
+__global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int b = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int K = p.K, L = p.L, k = p.k, B = p.B, S = p.S, W = B + 1;
+    const int cap = 32 * S;
+
+    // ---- carve shared memory
+    Smem s;
+    {
+        unsigned char* q = smem_raw;
+        auto take = [&](size_t bytes) {
+            unsigned char* r = q;
+            q += (bytes + 15) & ~(size_t)15;
+            return r;
+        };
+        s.comp = (uint64_t*)take(sizeof(uint64_t) * cap);
+        s.logw = (double*)take(sizeof(double) * cap);
+        s.hash = (uint64_t*)take(sizeof(uint64_t) * p.hcap);
+        s.aux = (uint32_t*)take(sizeof(uint32_t) * cap);
+        s.lp = (float*)take(sizeof(float) * K * L * p.ks);
+        s.ids = (int32_t*)take(sizeof(int32_t) * K * L * p.ks);
+        s.ntok = (int32_t*)take(sizeof(int32_t) * W);
+        s.npar = (int16_t*)take(sizeof(int16_t) * W);
+        s.nrank = (int16_t*)take(sizeof(int16_t) * W);
+        s.ndep = (uint8_t*)take(sizeof(uint8_t) * W);
+        s.prior = (float*)take(sizeof(float) * (K > 0 ? K : 1));
+    }
+    const float* glp = p.lp + (size_t)b * K * L * k;
+    const void* gids = p.ids_i64 ? (const void*)((const int64_t*)p.ids + (size_t)b * K * L * k)
+                                 : (const void*)((const int32_t*)p.ids + (size_t)b * K * L * k);
+
+    // ---- stage the candidate tables (all warps)
+    const int rows = K * L;
+    for (int i = threadIdx.x; i < rows * p.ks; i += kThreads) {
+        const int row = i / p.ks, r = i % p.ks;
+        const size_t o = (size_t)row * k + r;
+        s.lp[i] = glp[o];
+        s.ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[o] : ((const int32_t*)gids)[o];
+    }
+    for (int i = threadIdx.x; i < p.hcap; i += kThreads) s.hash[i] = kEmptyHash;
+    for (int i = threadIdx.x; i < cap; i += kThreads) {
+        s.comp[i] = ~0ull;
+        s.aux[i] = 0xffffffffu;
+    }
+    for (int i = threadIdx.x; i < K; i += kThreads) s.prior[i] = p.prior ? p.prior[(size_t)b * K + i] : 0.f;
+    if (threadIdx.x == 0) {
+        s.ntok[0] = 0;
+        s.npar[0] = -1;
+        s.ndep[0] = 0;
+        s.nrank[0] = 0;
+    }
+    __syncthreads();
+
+    __shared__ int sh_count, sh_fail;
+    if (warp == 0) {
+        int count = 0;
+        int fail = 0;
+        // lane-owned slot sets
+        uint64_t occ = 0;             // occupied slots of this lane (bit j = slot lane + 32 j)
+        uint64_t lmin = ~0ull;        // this lane's minimum key
+        int lslot = -1;               // its slot
+        int lcnt = 0;                 // how many of this lane's entries equal lmin (single-mode ties)
+        int live = 0;                 // warp-uniform number of live entries
+        int rr = 0;                   // round-robin insertion lane
+
+        auto rescan = [&]() {
+            lmin = ~0ull;
+            lslot = -1;
+            lcnt = 0;
+            uint64_t o = occ;
+            while (o) {
+                const int j = __ffsll((long long)o) - 1;
+                o &= o - 1;
+                const int slot = lane + 32 * j;
+                const uint64_t c = s.comp[slot];
+                if (c < lmin) { lmin = c; lslot = slot; lcnt = 1; }
+                else if (c == lmin) { ++lcnt; }
+            }
+        };
+        // insert (comp, logw, aux) into lane `dst`'s free slot; warp-uniform call
+        auto insert = [&](int dst, uint64_t c, double lw, uint32_t ax) {
+            // pick a lane with room, preferring dst
+            uint32_t room = __ballot_sync(MFD_FULL_MASK, (S >= 64) ? (occ != ~0ull) : (occ != ((1ull << S) - 1ull)));
+            if (!room) { fail = 1; return; }
+            if (!((room >> dst) & 1u)) dst = __ffs(room) - 1;
+            if (lane == dst) {
+                const int j = __ffsll((long long)~occ) - 1;
+                const int slot = lane + 32 * j;
+                occ |= 1ull << j;
+                s.comp[slot] = c;
+                s.logw[slot] = lw;
+                s.aux[slot] = ax;
+                if (c < lmin) { lmin = c; lslot = slot; lcnt = 1; }
+                else if (c == lmin) { ++lcnt; }
+            }
+            ++live;
+        };
+        auto mix_comp = [&](double lw, int m, uint32_t ax) -> uint64_t {
+            float key = -(__double2float_rn(lw) + s.prior[m]);
+            key = key + 0.0f;  // -0.0 and +0.0 compare equal in the reference: fold them
+            return ((uint64_t)ord_f32(key) << 32) | ax;
+        };
+
+        // initial entries: one per mode at (parent 0, depth 1, rank 0)
+        if (B > 0 && L > 0) {
+            if (p.single) {
+                const double lw = (double)lp_at(p, s, glp, 0, 0, 0);
+                insert(0, ord_f64(-lw), lw, pack_aux(0, 0, 1, 0));
+            } else {
+                for (int m = 0; m < K; ++m) {
+                    const double lw = (double)lp_at(p, s, glp, m, 0, 0);
+                    const uint32_t ax = pack_aux(m, 0, 1, 0);
+                    insert(m & 31, mix_comp(lw, m, ax), lw, ax);
+                }
+            }
+        }
+
+        while (live > 0 && count < B && !fail) {
+            // ---- pop the minimum
+            const uint64_t M = warp_min_u64(lmin);
+            const bool eq = (lmin == M) && lslot >= 0;
+            int slot;
+            const int tot = p.single ? __reduce_add_sync(MFD_FULL_MASK, eq ? lcnt : 0) : 1;
+            if (tot == 1) {
+                const int w = __ffs(__ballot_sync(MFD_FULL_MASK, eq)) - 1;
+                slot = __shfl_sync(MFD_FULL_MASK, lslot, w);
+            } else {
+                // single-mode exact float64 tie: order the tied entries by rank tuple (lane 0, rare)
+                __syncwarp();
+                int best = -1;
+                if (lane == 0) {
+                    int16_t tb[32], tc[32];
+                    int nb = 0;
+                    for (int sl = 0; sl < cap; ++sl) {
+                        if (!((s.comp[sl] == M) && (s.aux[sl] != 0xffffffffu))) continue;
+                        const uint32_t ax = s.aux[sl];
+                        const int par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
+                        if (best < 0) {
+                            rank_tuple(s, par, rk, dep, tb);
+                            nb = dep;
+                            best = sl;
+                        } else {
+                            rank_tuple(s, par, rk, dep, tc);
+                            if (tuple_cmp(tc, dep, tb, nb) < 0) {
+                                for (int i = 0; i < dep; ++i) tb[i] = tc[i];
+                                nb = dep;
+                                best = sl;
+                            }
+                        }
+                    }
+                }
+                slot = __shfl_sync(MFD_FULL_MASK, best, 0);
+            }
+            const double lw = s.logw[slot];
+            const uint32_t ax = s.aux[slot];
+            const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
+            const int owner = slot & 31;
+            const int64_t token = id_at(p, s, gids, m, dep - 1, rk);
+
+            // ---- node: new, or an existing prefix reached by another mode
+            int current;
+            if (p.single) {
+                current = count + 1;
+            } else {
+                const uint64_t want = ((uint64_t)(uint32_t)token << 32) | ((uint64_t)(uint32_t)par << 16);
+                uint32_t h = (uint32_t)(((uint64_t)(uint32_t)token * 0x9E3779B1u) ^ ((uint32_t)par * 0x85EBCA77u));
+                h &= (uint32_t)(p.hcap - 1);
+                current = -1;
+                for (int base = 0; base < p.hcap && current < 0; base += 32) {
+                    const int hs = (int)((h + (uint32_t)base + (uint32_t)lane) & (uint32_t)(p.hcap - 1));
+                    const uint64_t v = s.hash[hs];
+                    const uint32_t hit = __ballot_sync(MFD_FULL_MASK, v != kEmptyHash && (v & ~0xffffull) == want);
+                    const uint32_t emp = __ballot_sync(MFD_FULL_MASK, v == kEmptyHash);
+                    // probe order = lane order; the first match before the first empty slot wins
+                    const uint32_t before = emp ? ((emp & (0u - emp)) - 1u) : 0xffffffffu;
+                    if (hit & before) {
+                        const int hl = __ffs(hit & before) - 1;
+                        current = (int)(__shfl_sync(MFD_FULL_MASK, (uint32_t)(v & 0xffffu), hl));
+                    } else if (emp) {
+                        const int el = __ffs(emp) - 1;
+                        current = count + 1;
+                        if (lane == el) s.hash[hs] = want | (uint64_t)(uint32_t)current;
+                    }
+                }
+                __syncwarp();
+                if (current < 0) { fail = 1; break; }
+            }
+            if (current == count + 1) {
+                if (lane == 0) {
+                    s.ntok[current] = (int32_t)token;
+                    s.npar[current] = (int16_t)par;
+                    s.ndep[current] = (uint8_t)dep;
+                    s.nrank[current] = (int16_t)rk;
+                }
+                ++count;
+            }
+
+            // ---- successors: the sibling replaces the popped slot, the child takes a free slot
+            const bool has_sib = rk + 1 < k;
+            const bool has_child = dep < L;
+            if (lane == owner) {
+                if (has_sib) {
+                    const double slw = (lw - (double)lp_at(p, s, glp, m, dep - 1, rk))
+                                       + (double)lp_at(p, s, glp, m, dep - 1, rk + 1);
+                    const uint32_t sax = pack_aux(m, par, dep, rk + 1);
+                    s.comp[slot] = p.single ? ord_f64(-slw) : mix_comp(slw, m, sax);
+                    s.logw[slot] = slw;
+                    s.aux[slot] = sax;
+                } else {
+                    occ &= ~(1ull << (slot >> 5));
+                    s.aux[slot] = 0xffffffffu;
+                    s.comp[slot] = ~0ull;
+                }
+                rescan();
+            }
+            if (!has_sib) --live;
+            if (has_child) {
+                const double clw = lw + (double)lp_at(p, s, glp, m, dep, 0);
+                const uint32_t cax = pack_aux(m, current, dep + 1, 0);
+                const uint64_t cc = p.single ? ord_f64(-clw) : mix_comp(clw, m, cax);
+                __syncwarp();
+                insert(rr, cc, clw, cax);
+                rr = (rr + 1) & 31;
+            }
+            __syncwarp();
+        }
+        if (lane == 0) {
+            sh_count = count;
+            sh_fail = fail;
+        }
+    }
+    __syncthreads();
+    const int n = sh_count;
+    if (sh_fail && threadIdx.x == 0 && p.status) atomicExch(p.status, (int)MFD_ERR_CAPACITY);
+
+    // ---- outputs
+    int64_t* t = p.tree + (size_t)b * 3 * W;
+    int64_t* d = t + W;
+    int64_t* pa = d + W;
+    for (int i = threadIdx.x; i < W; i += kThreads) {
+        const bool live_node = i <= n;
+        t[i] = (live_node && i > 0) ? (int64_t)s.ntok[i] : 0;
+        d[i] = live_node ? (int64_t)s.ndep[i] : 0;
+        pa[i] = live_node ? (int64_t)s.npar[i] : -1;
+    }
+    if (threadIdx.x == 0) p.counts[b] = n;
+    if (p.anc || p.vis) {
+        const int words = p.words;
+        for (int i = threadIdx.x; i < W; i += kThreads) {
+            uint64_t bits[8];  // words <= 8 (B < 512)
+#pragma unroll
+            for (int w = 0; w < 8; ++w) bits[w] = 0;
+            if (i <= n) {
+                int node = i;
+                while (node >= 0) {
+                    bits[node >> 6] |= 1ull << (node & 63);
+                    node = node == 0 ? -1 : s.npar[node];
+                }
+            }
+            if (p.anc) {
+                uint64_t* row = p.anc + ((size_t)b * W + i) * words;
+#pragma unroll
+                for (int w = 0; w < 8; ++w)
+                    if (w < words) row[w] = bits[w];
+            }
+            if (p.vis) {
+                uint8_t* row = p.vis + ((size_t)b * W + i) * W;
+                for (int j = 0; j < W; ++j) row[j] = (uint8_t)((bits[j >> 6] >> (j & 63)) & 1ull);
+            }
+        }
+    }
+}
+
+struct Plan {
+    int ks, S, hcap, words;
+    size_t smem;
+};
+
+static Plan plan(int K, int L, int k, int B) {
+    Plan pl;
+    const int W = B + 1;
+    const int64_t live_max = (int64_t)K + (int64_t)K * B + 2;  // pops <= K*B, each adds at most one entry
+    pl.S = (int)((live_max + 31) / 32);
+    if (pl.S < 2) pl.S = 2;
+    pl.hcap = 64;
+    while (pl.hcap < 4 * W) pl.hcap <<= 1;
+    pl.words = (W + 63) / 64;
+    const size_t fixed = (size_t)32 * pl.S * (8 + 8 + 4) + (size_t)pl.hcap * 8 + (size_t)W * (4 + 2 + 2 + 1) +
+                         (size_t)K * 4 + 16 * 12;
+    const size_t budget = 200 * 1024;
+    const size_t per_rank = (size_t)K * L * 8;
+    int ks = k;
+    if (fixed + per_rank * ks > budget) ks = (int)((budget - fixed) / per_rank);
+    if (ks < 1) ks = 1;
+    pl.ks = ks;
+    pl.smem = fixed + per_rank * ks + 64;
+    return pl;
+}
+
+}  // namespace tree
+}  // namespace mfd
+
+using namespace mfd;
+
+extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int ids_dtype, const float* log_prior,
+                               int64_t bs, int64_t num_modes, int64_t depth_limit, int64_t topk, int64_t budget,
+                               int single, int64_t* tree, int64_t* counts, uint64_t* anc_bits, uint8_t* visibility,
+                               int* status, void* stream) {
+    if (bs < 0 || num_modes < 1 || depth_limit < 0 || topk < 1 || budget < 0) {
+        set_error("mfd_build_trees: invalid sizes bs=%lld K=%lld L=%lld k=%lld B=%lld", (long long)bs,
+                  (long long)num_modes, (long long)depth_limit, (long long)topk, (long long)budget);
+        return MFD_ERR_INVALID;
+    }
+    if (num_modes > 16 || depth_limit > 31 || topk > 2047 || budget > 511) {
+        set_error("mfd_build_trees: limits K<=16, L<=31, k<=2047, B<=511 (got K=%lld L=%lld k=%lld B=%lld)",
+                  (long long)num_modes, (long long)depth_limit, (long long)topk, (long long)budget);
+        return MFD_ERR_UNSUPPORTED;
+    }
+    if (single && num_modes != 1) {
+        set_error("mfd_build_trees: the single-mode heap needs num_modes == 1");
+        return MFD_ERR_INVALID;
+    }
+    if (ids_dtype != MFD_I32 && ids_dtype != MFD_I64) {
+        set_error("mfd_build_trees: ids_dtype must be MFD_I32 or MFD_I64");
+        return MFD_ERR_INVALID;
+    }
+    if (bs == 0) return MFD_OK;
+    if (!tree || !counts || ((!top_logp || !top_ids) && depth_limit > 0 && budget > 0)) {
+        set_error("mfd_build_trees: null pointer");
+        return MFD_ERR_INVALID;
+    }
+    tree::Plan pl = tree::plan((int)num_modes, (int)depth_limit, (int)topk, (int)budget);
+    if ((int64_t)num_modes + num_modes * budget + 2 > 32 * 64) {
+        set_error("mfd_build_trees: K*(B+1) too large for the entry store (K=%lld B=%lld)", (long long)num_modes,
+                  (long long)budget);
+        return MFD_ERR_UNSUPPORTED;
+    }
+    tree::Params p;
+    p.lp = top_logp;
+    p.ids = top_ids;
+    p.ids_i64 = ids_dtype == MFD_I64;
+    p.prior = log_prior;
+    p.bs = bs;
+    p.K = (int)num_modes;
+    p.L = (int)depth_limit;
+    p.k = (int)topk;
+    p.B = (int)budget;
+    p.single = single ? 1 : 0;
+    p.ks = depth_limit > 0 ? pl.ks : 1;
+    p.S = pl.S;
+    p.hcap = pl.hcap;
+    p.words = pl.words;
+    p.tree = tree;
+    p.counts = counts;
+    p.anc = anc_bits;
+    p.vis = visibility;
+    p.status = status;
+    cudaError_t e = cudaFuncSetAttribute(tree::build_trees_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)pl.smem);
+    if (e != cudaSuccess) {
+        set_error("mfd_build_trees: %s", cudaGetErrorString(e));
+        return MFD_ERR_CUDA;
+    }
+    tree::build_trees_kernel<<<(unsigned)bs, tree::kThreads, pl.smem, (cudaStream_t)stream>>>(p);
+    MFD_CHECK_LAUNCH("mfd_build_trees");
+    return MFD_OK;
+}

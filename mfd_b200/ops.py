@@ -1,0 +1,239 @@
+"""Torch-facing wrappers of the C ABI: device tensors in, device tensors out, launches on the current stream.
+
+These are the building blocks; the reference-shaped entry points live in ddtree.py, tree_build_ext.py,
+tree_logits.py, ddtree_utils.py (SGLang), mode_attention.py, tree_gdn_kernel.py and qwen35_tree.py.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import MFD_BF16, MFD_F32, MFD_I32, MFD_I64, Workspace, check, ptr, require_cuda, stream_ptr
+
+
+def _ids_code(dtype: torch.dtype) -> int:
+    if dtype == torch.int32:
+        return MFD_I32
+    if dtype == torch.int64:
+        return MFD_I64
+    raise RuntimeError(f"ids must be int32 or int64, got {dtype}")
+
+
+# ----------------------------------------------------------------------------------------------- logits step
+
+def topk_logz(x: torch.Tensor, k: int, ids_dtype: torch.dtype = torch.int64, out=None):
+    """x [..., V] float32/bf16 (CUDA, last dim contiguous) -> (top_logp f32 [..., k], ids [..., k], logz f32 [...]).
+
+    top_logp = top - logsumexp(row); ids ordered by value descending, equal values by lower index first."""
+    dev = require_cuda(x)
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError(f"topk_logz: x must be float32 or bfloat16, got {x.dtype}")
+    V = x.shape[-1]
+    rows2d = x.reshape(-1, V)
+    if rows2d.stride(-1) != 1:
+        rows2d = rows2d.contiguous()
+    R = rows2d.shape[0]
+    if out is None:
+        top = torch.empty(R, k, dtype=torch.float32, device=dev)
+        ids = torch.empty(R, k, dtype=ids_dtype, device=dev)
+        logz = torch.empty(R, dtype=torch.float32, device=dev)
+    else:
+        top, ids, logz = out
+    L = _lib.lib()
+    ws_bytes = L.mfd_topk_logz_workspace(R, V, k)
+    ws = Workspace.get(dev, "topk", ws_bytes)
+    rc = L.mfd_topk_logz(rows2d.data_ptr(), MFD_BF16 if x.dtype == torch.bfloat16 else MFD_F32, R, V,
+                         rows2d.stride(0), k, top.data_ptr(), ids.data_ptr(), _ids_code(ids.dtype),
+                         ptr(logz), ws.data_ptr(), ws.numel(), stream_ptr(dev))
+    check(rc, "mfd_topk_logz")
+    lead = x.shape[:-1]
+    return top.view(*lead, k), ids.view(*lead, k), logz.view(*lead)
+
+
+# ----------------------------------------------------------------------------------------------- builders
+
+def build_trees(top_logp: torch.Tensor, top_ids: torch.Tensor, log_prior: torch.Tensor | None, budget: int,
+                single: bool = False, tree: torch.Tensor | None = None, counts: torch.Tensor | None = None,
+                want_anc: bool = True, want_vis: bool = False, status: torch.Tensor | None = None):
+    """top_logp [bs, K, L, k] f32, top_ids [bs, K, L, k] i32/i64, log_prior [bs, K] or None.
+
+    Returns (tree [bs, 3, B+1] i64, counts [bs] i64, anc [bs, B+1, words] u64 as int64 or None,
+    vis [bs, B+1, B+1] u8 or None)."""
+    dev = require_cuda(top_logp, top_ids, log_prior)
+    bs, K, L, k = top_logp.shape
+    W = budget + 1
+    if top_logp.dtype != torch.float32:
+        raise RuntimeError("build_trees: top_logp must be float32")
+    top_logp = top_logp.contiguous()
+    top_ids = top_ids.contiguous()
+    if log_prior is not None:
+        log_prior = log_prior.to(torch.float32).contiguous()
+    if tree is None:
+        tree = torch.empty(bs, 3, W, dtype=torch.int64, device=dev)
+    if counts is None:
+        counts = torch.empty(bs, dtype=torch.int64, device=dev)
+    words = (W + 63) // 64
+    anc = torch.empty(bs, W, words, dtype=torch.int64, device=dev) if want_anc else None
+    vis = torch.empty(bs, W, W, dtype=torch.uint8, device=dev) if want_vis else None
+    rc = _lib.lib().mfd_build_trees(top_logp.data_ptr(), top_ids.data_ptr(), _ids_code(top_ids.dtype),
+                                    ptr(log_prior), bs, K, L, k, budget, 1 if single else 0, tree.data_ptr(),
+                                    counts.data_ptr(), ptr(anc), ptr(vis), ptr(status), stream_ptr(dev))
+    check(rc, "mfd_build_trees")
+    return tree, counts, anc, vis
+
+
+# ----------------------------------------------------------------------------------------------- acceptance
+
+def accept(logits: torch.Tensor, tokens: torch.Tensor, parents: torch.Tensor, temperature: float = 0.0,
+           uniforms: torch.Tensor | None = None, max_steps: int = -1, out_len: int | None = None,
+           window: torch.Tensor | None = None, prefix_lens: torch.Tensor | None = None):
+    """logits [bs, W, V] bf16 (rows contiguous), tokens/parents [bs, W] i64 -> dict of device outputs."""
+    dev = require_cuda(logits, tokens, parents, uniforms, window, prefix_lens)
+    if logits.dtype != torch.bfloat16:
+        raise RuntimeError("accept: logits must be bfloat16")
+    bs, W, V = logits.shape
+    rows = logits.reshape(bs * W, V)
+    if rows.stride(-1) != 1:
+        rows = rows.contiguous()
+    if out_len is None:
+        out_len = W if max_steps < 0 else max_steps + 1
+    if tokens.stride(-1) != 1 or parents.stride(-1) != 1:
+        raise RuntimeError("accept: tokens/parents need a contiguous last dim")
+    if uniforms is not None:
+        uniforms = uniforms.to(torch.float64).contiguous()
+    o = {
+        "posterior": torch.empty(bs, W, dtype=torch.int64, device=dev),
+        "accept_len": torch.empty(bs, dtype=torch.int32, device=dev),
+        "commit_lens": torch.empty(bs, dtype=torch.int32, device=dev),
+        "bonus": torch.empty(bs, dtype=torch.int64, device=dev),
+        "out_tokens": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+        "accepted": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+        "new_seq_lens": torch.empty(bs, dtype=torch.int64, device=dev),
+        "hidden_index": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+    }
+    if window is not None:
+        o["move_src"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
+        o["move_tgt"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
+    L = _lib.lib()
+    ws = Workspace.get(dev, "accept", L.mfd_accept_workspace(bs))
+    rc = L.mfd_accept(rows.data_ptr(), rows.stride(0), V, bs, W, tokens.data_ptr(), tokens.stride(0),
+                      parents.data_ptr(), parents.stride(0), float(temperature), ptr(uniforms), max_steps,
+                      ptr(window), ptr(prefix_lens), out_len, o["posterior"].data_ptr(), o["accept_len"].data_ptr(),
+                      o["commit_lens"].data_ptr(), o["bonus"].data_ptr(), o["out_tokens"].data_ptr(),
+                      o["accepted"].data_ptr(), o["new_seq_lens"].data_ptr(), ptr(o.get("move_src")),
+                      ptr(o.get("move_tgt")), o["hidden_index"].data_ptr(), ws.data_ptr(), ws.numel(),
+                      stream_ptr(dev))
+    check(rc, "mfd_accept")
+    return o
+
+
+def sample_tokens(logits: torch.Tensor, temperature: float = 0.0, uniforms: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """logits [..., V] bf16 -> int64 [...]: argmax (temperature < 1e-5) or the reproducible sample."""
+    dev = require_cuda(logits, uniforms)
+    if logits.dtype != torch.bfloat16:
+        raise RuntimeError("sample_tokens: logits must be bfloat16")
+    V = logits.shape[-1]
+    rows = logits.reshape(-1, V)
+    if rows.stride(-1) != 1:
+        rows = rows.contiguous()
+    R = rows.shape[0]
+    if out is None:
+        out = torch.empty(R, dtype=torch.int64, device=dev)
+    if uniforms is not None:
+        uniforms = uniforms.to(torch.float64).reshape(-1).contiguous()
+    rc = _lib.lib().mfd_sample_tokens(rows.data_ptr(), rows.stride(0), V, R, float(temperature), ptr(uniforms),
+                                      out.data_ptr(), stream_ptr(dev))
+    check(rc, "mfd_sample_tokens")
+    return out.view(logits.shape[:-1])
+
+
+def follow(posterior: torch.Tensor, tokens: torch.Tensor, parents: torch.Tensor, max_steps: int = -1,
+           out_len: int | None = None, window: torch.Tensor | None = None, prefix_lens: torch.Tensor | None = None,
+           outs: dict | None = None):
+    """Walk only: posterior/tokens/parents [bs, W] i64 (CUDA)."""
+    dev = require_cuda(posterior, tokens, parents, window, prefix_lens)
+    bs, W = posterior.shape
+    if out_len is None:
+        out_len = W if max_steps < 0 else max_steps + 1
+    posterior = posterior.contiguous()
+    if outs is None:
+        outs = {
+            "accept_len": torch.empty(bs, dtype=torch.int32, device=dev),
+            "commit_lens": torch.empty(bs, dtype=torch.int32, device=dev),
+            "bonus": torch.empty(bs, dtype=torch.int64, device=dev),
+            "out_tokens": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+            "accepted": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+            "new_seq_lens": torch.empty(bs, dtype=torch.int64, device=dev),
+            "hidden_index": torch.empty(bs, out_len, dtype=torch.int64, device=dev),
+        }
+        if window is not None:
+            outs["move_src"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
+            outs["move_tgt"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
+    rc = _lib.lib().mfd_follow(posterior.data_ptr(), tokens.data_ptr(), tokens.stride(0), parents.data_ptr(),
+                               parents.stride(0), bs, W, max_steps, ptr(window), ptr(prefix_lens), out_len,
+                               ptr(outs.get("accept_len")), ptr(outs.get("commit_lens")), ptr(outs.get("bonus")),
+                               ptr(outs.get("out_tokens")), ptr(outs.get("accepted")), ptr(outs.get("new_seq_lens")),
+                               ptr(outs.get("move_src")), ptr(outs.get("move_tgt")), ptr(outs.get("hidden_index")),
+                               stream_ptr(dev))
+    check(rc, "mfd_follow")
+    return outs
+
+
+# ----------------------------------------------------------------------------------------------- verify inputs
+
+def verify_inputs(root_tokens, prefix_lens, tokens, depths, parents, mask_offsets, ids_out, positions_out,
+                  mask_out, max_depth: int) -> None:
+    dev = require_cuda(root_tokens, prefix_lens, tokens, depths, parents, mask_offsets, ids_out, positions_out,
+                       mask_out)
+    bs, W = tokens.shape
+    if not (tokens.stride() == depths.stride() == parents.stride() and tokens.stride(1) == 1):
+        raise RuntimeError("verify_inputs: tokens/depths/parents must share a row-contiguous layout")
+    rc = _lib.lib().mfd_verify_inputs(root_tokens.data_ptr(), prefix_lens.data_ptr(), tokens.data_ptr(),
+                                      depths.data_ptr(), parents.data_ptr(), tokens.stride(0),
+                                      mask_offsets.data_ptr(), bs, W, max_depth, ids_out.data_ptr(),
+                                      positions_out.data_ptr(), mask_out.data_ptr(), stream_ptr(dev))
+    check(rc, "mfd_verify_inputs")
+
+
+# ----------------------------------------------------------------------------------------------- attention
+
+def default_splits(bs: int, n: int, num_heads: int, num_kv_heads: int, keys: int) -> int:
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    row_blocks = (n * (num_heads // num_kv_heads) + 63) // 64
+    base = bs * num_kv_heads * row_blocks
+    want = max(1, (2 * sms + base - 1) // base)
+    return int(max(1, min(want, (keys + 63) // 64)))
+
+
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch.Tensor, prefix_lens,
+                   scale: float, splits: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """q [bs, n, H, D], k/v [bs, Hkv, S, D] bf16 (prefix keys then the n tree keys), anc [bs, n, words] i64,
+    prefix_lens: int (same for all) or int32 [bs] CUDA tensor.  Returns [bs, n, H, D] bf16."""
+    dev = require_cuda(q, k, v, anc)
+    bs, n, H, D = q.shape
+    Hkv = k.shape[1]
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError("tree_attention: q, k, v must be bfloat16")
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise RuntimeError("tree_attention: the head dim must be contiguous")
+    if out is None:
+        out = torch.empty(bs, n, H, D, dtype=torch.bfloat16, device=dev)
+    if isinstance(prefix_lens, torch.Tensor):
+        pl_t, pl_c = prefix_lens.to(torch.int32).contiguous(), 0
+        max_keys = k.shape[2]
+    else:
+        pl_t, pl_c = None, int(prefix_lens)
+        max_keys = pl_c + n
+    if splits is None:
+        splits = default_splits(bs, n, H, Hkv, max_keys)
+    L = _lib.lib()
+    ws = Workspace.get(dev, "attn", L.mfd_tree_attention_workspace(bs, n, H, splits))
+    rc = L.mfd_tree_attention(q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(), k.stride(0),
+                              k.stride(1), k.stride(2), v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
+                              ptr(pl_t), pl_c, anc.data_ptr(), anc.shape[-1], bs, n, H, Hkv, D, float(scale), splits,
+                              out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), ws.data_ptr(), ws.numel(),
+                              stream_ptr(dev))
+    check(rc, "mfd_tree_attention")
+    return out

@@ -1,0 +1,314 @@
+"""CPU oracle for the MFD verify step -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference legs import
+this module, and only as the checker.  The product package (mfd_b200) never imports it.
+
+Integer and index work (tree builders, visibility, walk, sampling rule, argmax) runs in the plain-C
+restatement oracle/mfd_oracle.c through ctypes.  Floating-point paths are restated with numpy:
+
+  topk_logz          hf/ddtree.py:240-244 (float32 top-k and logsumexp); ties ordered by lower index
+                     first (this build's contract; torch's CPU top-k leaves tie order unspecified)
+  tree_attention     hf/ddtree.py:352-356 (mask: prefix visible, tree block ancestor-only, the
+                     compile_ddtree_tree mask) + SDPA with GQA head repetition
+  mode_attention     hf/mode_attention.py:216-227 (`reference`: whole context + own mode block)
+  tree_gdn           tests/test_gdn_tree_math.py:29-60 (chunk form with ancestor mask, one
+                     triangular solve) with the GQA key-head map of hf/tree_gdn_kernel.py:71, 101,
+                     per-node states by the commit formula hf/qwen35_tree.py:134-137
+
+Parity pins: tests/golden/ holds fixtures made by tests/golden/make_golden.py from the reference
+itself (its Python builders, compiled C++ builders, walk, mode-attention reference and verify mask);
+tests/test_oracle_golden.py checks this oracle against them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libmfd_oracle.so")
+_LIB = None
+
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_f64p = ctypes.POINTER(ctypes.c_double)
+
+
+def build() -> str:
+    """Compile oracle/mfd_oracle.c (gcc) into oracle/_build/libmfd_oracle.so."""
+    src = os.path.join(_HERE, "mfd_oracle.c")
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-C", _HERE, "-s"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oracle_build_mixture.restype = ctypes.c_int64
+        L.oracle_build_mixture.argtypes = [_f32p, _i64p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, _i64p, _i64p, _i64p, _i64p]
+        L.oracle_build_single.restype = ctypes.c_int64
+        L.oracle_build_single.argtypes = [_f32p, _i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                          _i64p, _i64p, _i64p, _i64p]
+        L.oracle_build_trees.restype = None
+        L.oracle_build_trees.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int64, _i64p, _i64p]
+        L.oracle_visibility.restype = None
+        L.oracle_visibility.argtypes = [_i64p, ctypes.c_int64, _u8p]
+        L.oracle_follow.restype = ctypes.c_int64
+        L.oracle_follow.argtypes = [_i64p, _i64p, ctypes.c_int64, _i64p, ctypes.c_int64, _i64p, _i64p]
+        L.oracle_sample_rows.restype = None
+        L.oracle_sample_rows.argtypes = [_u16p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _f64p, _i64p]
+        L.oracle_argmax_rows.restype = None
+        L.oracle_argmax_rows.argtypes = [_u16p, ctypes.c_int64, ctypes.c_int64, _i64p]
+        L.oracle_exp32.restype = ctypes.c_float
+        L.oracle_exp32.argtypes = [ctypes.c_float]
+        _LIB = L
+    return _LIB
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+# ------------------------------------------------------------------------------------------ builders
+
+def build_mixture(top_logp: np.ndarray, top_ids: np.ndarray, prior: np.ndarray, budget: int, stats=None):
+    """[K, L, k] float32 / int64, [K] float32 -> (tokens [n], depths [n], parents [n+1]) int64."""
+    lp = np.ascontiguousarray(top_logp, dtype=np.float32)
+    ids = np.ascontiguousarray(top_ids, dtype=np.int64)
+    pr = np.ascontiguousarray(prior, dtype=np.float32)
+    K, L, k = lp.shape
+    tok = np.empty(max(budget, 1), np.int64)
+    dep = np.empty(max(budget, 1), np.int64)
+    par = np.empty(max(budget, 0) + 1, np.int64)
+    pops = np.zeros(1, np.int64)
+    n = lib().oracle_build_mixture(_p(lp, _f32p), _p(ids, _i64p), _p(pr, _f32p), K, L, k, budget,
+                                   _p(tok, _i64p), _p(dep, _i64p), _p(par, _i64p), _p(pops, _i64p))
+    if stats is not None:
+        stats["pops"] = int(pops[0])
+    return tok[:n].copy(), dep[:n].copy(), par[:n + 1].copy()
+
+
+def build_single(top_logp: np.ndarray, top_ids: np.ndarray, budget: int, stats=None):
+    """[L, k] float32 / int64 -> (tokens [n], depths [n], parents [n+1]) int64."""
+    lp = np.ascontiguousarray(top_logp, dtype=np.float32)
+    ids = np.ascontiguousarray(top_ids, dtype=np.int64)
+    L, k = lp.shape
+    tok = np.empty(max(budget, 1), np.int64)
+    dep = np.empty(max(budget, 1), np.int64)
+    par = np.empty(max(budget, 0) + 1, np.int64)
+    pops = np.zeros(1, np.int64)
+    n = lib().oracle_build_single(_p(lp, _f32p), _p(ids, _i64p), L, k, budget, _p(tok, _i64p), _p(dep, _i64p),
+                                  _p(par, _i64p), _p(pops, _i64p))
+    if stats is not None:
+        stats["pops"] = int(pops[0])
+    return tok[:n].copy(), dep[:n].copy(), par[:n + 1].copy()
+
+
+def build_trees(top_logp: np.ndarray, top_ids: np.ndarray, prior: np.ndarray, budget: int):
+    """SGLang layout: [bs, K, L, k] float32 / int32, [bs, K] -> tree [bs, 3, B+1] int64, counts [bs]."""
+    lp = np.ascontiguousarray(top_logp, dtype=np.float32)
+    ids = np.ascontiguousarray(top_ids, dtype=np.int32)
+    pr = np.ascontiguousarray(prior, dtype=np.float32)
+    bs, K, L, k = lp.shape
+    tree = np.empty((bs, 3, budget + 1), np.int64)
+    counts = np.empty(bs, np.int64)
+    lib().oracle_build_trees(_p(lp, _f32p), _p(ids, _i32p), _p(pr, _f32p), bs, K, L, k, budget,
+                             _p(tree, _i64p), _p(counts, _i64p))
+    return tree, counts
+
+
+def visibility(parents) -> np.ndarray:
+    par = np.ascontiguousarray(parents, dtype=np.int64)
+    m = par.shape[0]
+    vis = np.empty((m, m), np.uint8)
+    lib().oracle_visibility(_p(par, _i64p), m, _p(vis, _u8p))
+    return vis.astype(bool)
+
+
+def follow(tokens_with_root, parents, posterior, max_steps: int = -1):
+    """tokens_with_root [m] (index 0 unused), parents [m], posterior [m] -> (accepted list, bonus)."""
+    tok = np.ascontiguousarray(tokens_with_root, dtype=np.int64)
+    par = np.ascontiguousarray(parents, dtype=np.int64)
+    post = np.ascontiguousarray(posterior, dtype=np.int64)
+    m = par.shape[0]
+    acc = np.empty(m + 1, np.int64)
+    bonus = np.zeros(1, np.int64)
+    n = lib().oracle_follow(_p(tok, _i64p), _p(par, _i64p), m, _p(post, _i64p), max_steps, _p(acc, _i64p),
+                            _p(bonus, _i64p))
+    return acc[:n].tolist(), int(bonus[0])
+
+
+def sample_rows(rows_bf16_u16: np.ndarray, inv_temp: float, u: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(rows_bf16_u16, dtype=np.uint16)
+    R, V = x.shape
+    uu = np.ascontiguousarray(u, dtype=np.float64)
+    out = np.empty(R, np.int64)
+    lib().oracle_sample_rows(_p(x, _u16p), R, V, ctypes.c_float(inv_temp), _p(uu, _f64p), _p(out, _i64p))
+    return out
+
+
+def argmax_rows(rows_bf16_u16: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(rows_bf16_u16, dtype=np.uint16)
+    R, V = x.shape
+    out = np.empty(R, np.int64)
+    lib().oracle_argmax_rows(_p(x, _u16p), R, V, _p(out, _i64p))
+    return out
+
+
+def exp32(y: float) -> float:
+    return float(lib().oracle_exp32(ctypes.c_float(y)))
+
+
+# ------------------------------------------------------------------------------------------ float paths
+
+def bf16_bits_to_f32(u16: np.ndarray) -> np.ndarray:
+    return (np.asarray(u16, dtype=np.uint32) << 16).view(np.float32)
+
+
+def topk_logz(x: np.ndarray, k: int):
+    """x [R, V] float32 -> (top_logp [R, k] float32, ids [R, k] int64, logz [R] float32).
+
+    logz is the float64 logsumexp rounded once to float32; top_logp = float32(top) - logz in float32, as
+    hf/ddtree.py:243 subtracts.  Order: value descending, equal values by lower index first."""
+    x = np.asarray(x, dtype=np.float32)
+    R, V = x.shape
+    xd = x.astype(np.float64)
+    m = xd.max(axis=1, keepdims=True)
+    logz = (m[:, 0] + np.log(np.exp(xd - m).sum(axis=1))).astype(np.float32)
+    ids = np.empty((R, k), np.int64)
+    top = np.empty((R, k), np.float32)
+    idx = np.arange(V)
+    for r in range(R):
+        order = np.lexsort((idx, -x[r].astype(np.float64)))[:k]
+        ids[r] = order
+        top[r] = x[r, order]
+    return (top - logz[:, None]).astype(np.float32), ids, logz
+
+
+def tree_attention(q, k_prefix, v_prefix, k_tree, v_tree, parents, scale):
+    """q [n, H, D], prefix K/V [P, Hkv, D], tree K/V [n, Hkv, D] (float arrays), parents [n] (parents[0] = -1).
+    Row i sees every prefix key and the tree keys of its ancestors and itself.  Returns [n, H, D] float32."""
+    q = np.asarray(q, np.float32)
+    n, H, D = q.shape
+    Hkv = k_tree.shape[1]
+    G = H // Hkv
+    vis = visibility(parents)
+    kk = np.concatenate([np.asarray(k_prefix, np.float32), np.asarray(k_tree, np.float32)], 0)
+    vv = np.concatenate([np.asarray(v_prefix, np.float32), np.asarray(v_tree, np.float32)], 0)
+    P = k_prefix.shape[0]
+    mask = np.zeros((n, P + n), bool)
+    mask[:, :P] = True
+    mask[:, P:] = vis
+    out = np.empty((n, H, D), np.float32)
+    for h in range(H):
+        kv = h // G
+        s = (q[:, h, :].astype(np.float64) @ kk[:, kv, :].astype(np.float64).T) * scale
+        s = np.where(mask, s, -np.inf)
+        s = s - s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, h, :] = (p @ vv[:, kv, :].astype(np.float64)).astype(np.float32)
+    return out
+
+
+def mode_attention(q, k, v, num_modes, block_size, scale):
+    """hf/mode_attention.py reference: q [H, K*bs, D], k/v [Hkv, ctx + K*bs, D] -> [K*bs, H, D] float32."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    H, T, D = q.shape
+    Hkv, total, _ = k.shape
+    G = H // Hkv
+    ctx = total - num_modes * block_size
+    qb = np.arange(T) // block_size
+    mask = np.ones((T, total), bool)
+    mask[:, ctx:] = qb[:, None] == qb[None, :]
+    out = np.empty((T, H, D), np.float32)
+    for h in range(H):
+        s = (q[h] @ k[h // G].T) * scale
+        s = np.where(mask, s, -np.inf)
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, h, :] = (p @ v[h // G]).astype(np.float32)
+    return out
+
+
+def tree_gdn(q, k, v, g_cum, beta, s0, parents, emit_states=False):
+    """Chunk form of the tree gated delta rule in float64.
+
+    q, k [n, HK, Dk] (q already l2-normalised and scaled, k l2-normalised), v [n, H, Dv], g_cum/beta [n, H]
+    (g_cum = log decay summed along the root path), s0 [H, Dk, Dv] (fla layout, o = S^T q), parents [n]
+    (-1 = the committed state).  Returns u, o [n, H, Dv] and, if asked, per-node states [n, H, Dk, Dv]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    G = np.asarray(g_cum, np.float64)
+    beta = np.asarray(beta, np.float64)
+    s0 = np.asarray(s0, np.float64)
+    n, HK, Dk = k.shape
+    H, Dv = v.shape[1], v.shape[2]
+    anc = np.zeros((n, n), bool)
+    for i in range(n):
+        p = int(parents[i])
+        if p >= 0:
+            anc[i] = anc[p]
+        anc[i, i] = True
+    strict = anc & ~np.eye(n, dtype=bool)
+    u = np.empty((n, H, Dv))
+    o = np.empty((n, H, Dv))
+    states = np.empty((n, H, Dk, Dv)) if emit_states else None
+    for h in range(H):
+        hk = h // (H // HK)
+        kh, qh, Gh = k[:, hk], q[:, hk], G[:, h]
+        gamma = np.where(anc, np.exp(np.where(anc, Gh[:, None] - Gh[None, :], 0.0)), 0.0)
+        lower = beta[:, h, None] * gamma * (kh @ kh.T) * strict
+        rhs = beta[:, h, None] * (v[:, h] - np.exp(Gh)[:, None] * (kh @ s0[h]))
+        A = np.eye(n) + lower
+        uh = np.zeros((n, Dv))
+        for i in range(n):  # forward substitution (unit lower triangular)
+            uh[i] = rhs[i] - A[i, :i] @ uh[:i]
+        u[:, h] = uh
+        o[:, h] = np.exp(Gh)[:, None] * (qh @ s0[h]) + (gamma * (qh @ kh.T) * anc) @ uh
+        if emit_states:
+            for i in range(n):
+                w = gamma[i] * anc[i]
+                states[i, h] = np.exp(Gh[i]) * s0[h] + (kh * w[:, None]).T @ uh
+    return u, o, states
+
+
+def gdn_recurrence(q, k, v, g, beta, s0, parents):
+    """Node-by-node gated delta rule (tests/test_gdn_tree_math.py:38-44, fla layout S [Dk, Dv]):
+    S_i = exp(g_i) S_p (I - beta_i k_i k_i^T)... written as S_i = e^{g_i}(S_p - beta_i k_i (k_i^T S_p)) +
+    beta_i k_i v_i^T, o_i = S_i^T q_i.  float64; returns o [n, H, Dv] and states [n, H, Dk, Dv]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    g = np.asarray(g, np.float64)
+    beta = np.asarray(beta, np.float64)
+    s0 = np.asarray(s0, np.float64)
+    n, HK, Dk = k.shape
+    H, Dv = v.shape[1], v.shape[2]
+    states = np.empty((n, H, Dk, Dv))
+    o = np.empty((n, H, Dv))
+    for i in range(n):
+        p = int(parents[i])
+        for h in range(H):
+            hk = h // (H // HK)
+            sp = s0[h] if p < 0 else states[p, h]
+            ki = k[i, hk]
+            s = np.exp(g[i, h]) * (sp - beta[i, h] * np.outer(ki, ki @ sp)) + beta[i, h] * np.outer(ki, v[i, h])
+            states[i, h] = s
+            o[i, h] = s.T @ q[i, hk]
+    return o, states

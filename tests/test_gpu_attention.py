@@ -1,0 +1,82 @@
+"""GPU parity: tree-masked GQA verify attention vs the oracle / the reference mask + SDPA.
+bf16 inputs, float32 accumulation; tolerance max |err| <= 2e-2 (the reference's kernel checks use 2e-2,
+inference/hf/mode_attention.py:242)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._golden import bf16_from_i16, load
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-2
+
+
+def anc_bits(parents, words):
+    n = len(parents)
+    a = np.zeros((n, words), np.uint64)
+    for i in range(n):
+        j = i
+        while j >= 0:
+            a[i, j >> 6] |= np.uint64(1) << np.uint64(j & 63)
+            j = parents[j]
+    return torch.from_numpy(a.view(np.int64))
+
+
+def test_verify_attention_vs_reference_fixture():
+    from mfd_b200 import ops
+    z = load("verify_attention.npz")
+    q = torch.from_numpy(bf16_from_i16(z["q"])).to(torch.bfloat16)  # [1, H, n, D]
+    k = torch.from_numpy(bf16_from_i16(z["k"])).to(torch.bfloat16)  # [1, Hkv, P+n, D]
+    v = torch.from_numpy(bf16_from_i16(z["v"])).to(torch.bfloat16)
+    parents = z["parents"].tolist()
+    n = len(parents)
+    P = int(z["prefix"])
+    anc = anc_bits(parents, 1)[None].to(DEV)
+    out = ops.tree_attention(q.transpose(1, 2).contiguous().to(DEV), k.to(DEV), v.to(DEV), anc, P, 128 ** -0.5)
+    ref = torch.from_numpy(z["out"]).transpose(1, 2)  # [1, n, H, D]
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("P,n,H,Hkv,splits", [(4096, 65, 32, 8, None), (100, 65, 32, 8, 3), (0, 17, 8, 8, 1),
+                                              (1000, 64, 32, 8, 7), (77, 257, 16, 4, 2)])
+def test_tree_attention_vs_oracle(P, n, H, Hkv, splits):
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(P + n + H)
+    parents = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)]
+    D = 128
+    q = torch.randn(1, n, H, D, generator=g).to(torch.bfloat16)
+    k = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5).to(torch.bfloat16)
+    words = (n + 63) // 64
+    anc = anc_bits(parents, words)[None].to(DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, P, D ** -0.5, splits=splits)
+    kk = k[0].transpose(0, 1).float().numpy()
+    vv = v[0].transpose(0, 1).float().numpy()
+    ref = oracle.tree_attention(q[0].float().numpy(), kk[:P], vv[:P], kk[P:], vv[P:], parents, D ** -0.5)
+    err = np.abs(out[0].float().cpu().numpy() - ref).max()
+    assert err <= TOL, err
+
+
+def test_tree_attention_batched_variable_prefix():
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(9)
+    bs, n, H, Hkv, D, S = 3, 33, 16, 4, 128, 700
+    prefixes = [10, 300, 667]
+    q = torch.randn(bs, n, H, D, generator=g).to(torch.bfloat16)
+    k = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    trees = [[-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)] for _ in range(bs)]
+    anc = torch.stack([anc_bits(t, 1) for t in trees]).to(DEV)
+    pl = torch.tensor(prefixes, dtype=torch.int32, device=DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, pl, D ** -0.5, splits=4)
+    for b in range(bs):
+        P = prefixes[b]
+        kk = k[b].transpose(0, 1).float().numpy()
+        vv = v[b].transpose(0, 1).float().numpy()
+        ref = oracle.tree_attention(q[b].float().numpy(), kk[:P], vv[:P], kk[P:P + n], vv[P:P + n], trees[b],
+                                    D ** -0.5)
+        err = np.abs(out[b].float().cpu().numpy() - ref).max()
+        assert err <= TOL, (b, err)

@@ -1,0 +1,152 @@
+"""GPU parity: logits step (mfd_topk_logz) and exact tree builders (mfd_build_trees) vs the oracle and the
+reference fixtures.  Integer outputs are compared bit for bit; log-probabilities within 2e-6 absolute
+(the reference's own check allows 1e-4, inference/hf/tree_logits.py:58)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._golden import cases
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+V0, K0, L0, B0 = 151936, 8, 16, 64
+
+
+def config0_logits(seed, K=K0, L=L0, V=V0, sharp=False):
+    """N(0,1) logits, 4 ids per (mode, position) boosted by U(4,10) (sharp: 1 id by U(12,16))."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(K, L, V, generator=g)
+    nb = 1 if sharp else 4
+    ids = torch.randint(0, V, (K, L, nb), generator=g)
+    boost = torch.rand(K, L, nb, generator=g) * 4 + 12 if sharp else torch.rand(K, L, nb, generator=g) * 6 + 4
+    x.scatter_add_(2, ids, boost)
+    return x
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("R,V,k", [(1, 64, 64), (3, 1000, 8), (5, 4099, 100), (2, 70000, 256), (128, V0, 64), (7, 333, 1)])
+def test_topk_logz_vs_oracle(dtype, R, V, k):
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(R * 1000 + V + k)
+    x = (torch.randn(R, V, generator=g) * 3).to(dtype)
+    if dtype == torch.bfloat16 and V < 5000:
+        x = ((x.float() * 2).round() / 2).to(dtype)  # many exact ties
+    top, ids, lz = ops.topk_logz(x.to(DEV), k)
+    xo = x.float().numpy()
+    ref_lp, ref_ids, ref_lz = oracle.topk_logz(xo, k)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    np.testing.assert_allclose(lz.cpu().numpy(), ref_lz, rtol=0, atol=4e-6 * max(1.0, float(np.abs(ref_lz).max()) / 8))
+    np.testing.assert_allclose(top.cpu().numpy(), ref_lp, rtol=0, atol=8e-6)
+
+
+def test_topk_strided_rows_and_int32_ids():
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(3)
+    base = torch.randn(6, 5003, generator=g)
+    x = base.to(DEV)[:, 1:5001]  # misaligned starts, stride 5003
+    top, ids, lz = ops.topk_logz(x, 33, ids_dtype=torch.int32)
+    ref_lp, ref_ids, _ = oracle.topk_logz(base[:, 1:5001].numpy(), 33)
+    assert ids.dtype == torch.int32 and np.array_equal(ids.cpu().numpy(), ref_ids)
+    np.testing.assert_allclose(top.cpu().numpy(), ref_lp, rtol=0, atol=8e-6)
+
+
+def test_builders_on_reference_tie_cases():
+    from mfd_b200 import ops
+    for i, c in enumerate(cases("candidates_ties.npz")):
+        B = int(c["budget"])
+        lp = torch.from_numpy(c["lp"]).to(DEV)[None]
+        ids = torch.from_numpy(c["ids"]).to(DEV)[None]
+        pr = torch.from_numpy(c["prior"]).to(DEV)[None]
+        tree, counts, anc, vis = ops.build_trees(lp, ids, pr, B, single=bool(int(c["single"])), want_vis=True)
+        n = int(counts[0])
+        t = tree[0].cpu().numpy()
+        assert n == len(c["tokens"]), f"case {i}"
+        assert np.array_equal(t[0, 1:n + 1], c["tokens"]), f"case {i}"
+        assert np.array_equal(t[1, 1:n + 1], c["depths"]), f"case {i}"
+        assert np.array_equal(t[2, :n + 1], c["parents"]), f"case {i}"
+        assert np.array_equal(vis[0, :n + 1, :n + 1].cpu().numpy().astype(bool), c["vis"]), f"case {i}"
+
+
+def test_batched_builder_matches_reference_sglang_layout():
+    from mfd_b200 import ddtree_utils
+    for i, c in enumerate(cases("sglang_build_trees.npz")):
+        bs = c["lp"].shape[0]
+        B = int(c["budget"])
+        tree = torch.empty((bs, 3, B + 1), dtype=torch.long, device=DEV)
+        counts = torch.empty((bs,), dtype=torch.long, device=DEV)
+        ddtree_utils.build_trees(top_log_probs=torch.from_numpy(c["lp"]).to(DEV),
+                                 top_ids=torch.from_numpy(c["ids"]).to(DEV),
+                                 log_prior=torch.from_numpy(c["prior"]).to(DEV), bs=bs, budget=B, tree=tree,
+                                 counts=counts)
+        assert np.array_equal(tree.cpu().numpy(), c["tree"]), f"case {i}"
+        assert np.array_equal(counts.cpu().numpy(), c["counts"]), f"case {i}"
+        # the host-signature variant writes into CPU tensors
+        tcpu = torch.empty((bs, 3, B + 1), dtype=torch.long)
+        ccpu = torch.empty((bs,), dtype=torch.long)
+        ddtree_utils.build_trees_cpu(top_log_probs=torch.from_numpy(c["lp"]), top_ids=torch.from_numpy(c["ids"]),
+                                     log_prior=torch.from_numpy(c["prior"]), bs=bs, budget=B, tree=tcpu, counts=ccpu)
+        assert np.array_equal(tcpu.numpy(), c["tree"]), f"case {i} (cpu signature)"
+
+
+def test_hf_build_mixture_tree_end_to_end_vs_reference():
+    from mfd_b200 import ddtree
+    for i, c in enumerate(cases("mixture_e2e.npz")):
+        logits = torch.from_numpy(c["logits"]).to(DEV)
+        B = int(c["budget"])
+        if int(c["single"]):
+            out = ddtree.build_ddtree_tree(logits[0], B)
+        else:
+            out = ddtree.build_mixture_tree(logits, torch.from_numpy(c["prior"]).to(DEV), B)
+        assert np.array_equal(out[0].numpy(), c["tokens"]), f"case {i}"
+        assert np.array_equal(out[1].numpy(), c["depths"]), f"case {i}"
+        assert out[2] == c["parents"].tolist(), f"case {i}"
+        assert np.array_equal(out[4].numpy(), c["vis"]), f"case {i}"
+        acc, bonus = ddtree.follow_verified_tree(out[3], torch.from_numpy(c["post"]).view(1, -1))
+        assert acc == c["accepted"].tolist() and bonus == int(c["bonus"]), f"case {i} walk"
+
+
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("sharp", [False, True])
+def test_config0_tree_vs_oracle(seed, sharp):
+    """Full config-0 size: GPU top-k/logZ + GPU heap == oracle heap fed with the GPU's candidates (bit-exact),
+    and == the oracle's own candidates unless a score near-tie below 1e-5 separates them."""
+    from mfd_b200 import ops
+    x = config0_logits(seed, sharp=sharp)
+    xd = x.to(DEV)
+    top, ids, _ = ops.topk_logz(xd.view(K0 * L0, V0), B0, ids_dtype=torch.int32)
+    prior = torch.zeros(1, K0, device=DEV)
+    tree, counts, anc, _ = ops.build_trees(top.view(1, K0, L0, B0), ids.view(1, K0, L0, B0), prior, B0)
+    n = int(counts[0])
+    t = tree[0].cpu().numpy()
+    lp_np = top.view(K0, L0, B0).cpu().numpy()
+    ids_np = ids.view(K0, L0, B0).cpu().numpy().astype(np.int64)
+    tok, dep, par = oracle.build_mixture(lp_np, ids_np, np.zeros(K0, np.float32), B0)
+    assert n == len(tok)
+    assert np.array_equal(t[0, 1:n + 1], tok) and np.array_equal(t[1, 1:n + 1], dep)
+    assert np.array_equal(t[2, :n + 1], par)
+    # ancestor bitsets equal the oracle visibility
+    vis = oracle.visibility(par)
+    a = anc[0].cpu().numpy().view(np.uint64)
+    for i in range(n + 1):
+        bits = [(int(a[i, j >> 6]) >> (j & 63)) & 1 for j in range(n + 1)]
+        assert bits == vis[i].astype(int).tolist()
+    # against the oracle's own candidates (float64 log Z)
+    ref_lp, ref_ids, _ = oracle.topk_logz(x.view(K0 * L0, V0).numpy(), B0)
+    assert np.array_equal(ref_ids.reshape(K0, L0, B0), ids_np)
+    assert np.abs(ref_lp.reshape(K0, L0, B0) - lp_np).max() < 1e-5
+
+
+def test_single_mode_heap_matches_reference_on_ties():
+    from mfd_b200 import tree_build_ext
+    g = torch.Generator().manual_seed(5)
+    for trial in range(20):
+        L = 1 + trial % 9
+        logits = ((torch.randn(L, 40, generator=g) * 3 * 2).round() / 2).to(torch.bfloat16).float()
+        top, ids = torch.topk(logits, 16, dim=-1)
+        lp = (top - torch.logsumexp(logits, -1, keepdim=True)).float()
+        got = tree_build_ext.build_single(lp, ids, 16)
+        tok, dep, par = oracle.build_single(lp.numpy(), ids.numpy(), 16)
+        assert np.array_equal(got[0].numpy(), tok) and np.array_equal(got[1].numpy(), dep)
+        assert list(got[2]) == par.tolist()
