@@ -1,0 +1,472 @@
+"""Verify-step benchmark (tree build + tree verify attention + acceptance), B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests R]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
+
+Workload (synthetic, seeded per global request id so any partition computes the same
+requests): 256 requests per step, each with drafter logits float32 [K=8, L=16, V=151936] (N(0,1), 4 ids per
+(mode, position) boosted by U(4,10)), an exact mixture tree of B=64 nodes, tree-masked GQA verify attention
+(32/8 heads, head_dim 128, prefix U(1024, 8192)), and stochastic acceptance at T=1 over target logits bf16
+[65, V] N(0, 1.5) with seeded uniforms.  Requests are partitioned across ranks (sorted by prefix, dealt
+round-robin); there is no collective on the data path (only the timing max-reduce), so scaling is strong:
+the total work is fixed.  Inputs (~30 GB) are far larger than L2.
+
+Printed by rank 0: one JSON line (metric trees/s, whole job), with
+  north_star: BASELINE's headline verify step -- batch 1, greedy, prefix 4096, configs 0 + 1 + acceptance --
+              in microseconds per step (L2 flushed between steps), rank 0 only;
+  roofline:   the dominant kernel (the fused logits step) against the measured HBM copy bandwidth;
+  e2e:        the same metric through the public API with inputs copied from pinned host memory each step;
+  cpu_baseline: the reference's CPU path (its compiled C++ builder, torch's CPU top-k / logsumexp / SDPA /
+              softmax sampling, its walk) on a bounded sample, rank 0 at N=1.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_MODES, L_BLOCK, VOCAB, BUDGET = 8, 16, 151936, 64
+W = BUDGET + 1
+H, HKV, D = 32, 8, 128
+TOTAL_REQUESTS = 256
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+# ------------------------------------------------------------------------------------------------ setup
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+    except Exception:
+        return dict(PEAKS_FALLBACK, source="fallback")
+
+
+def dist_setup(n_gpus: int):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(ws, value: float) -> float:
+    if ws == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prefix_lengths(total: int, seed: int = 4321):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(1024, 8193, (total,), generator=g).tolist()
+
+
+def partition(total: int, ws: int, rank: int, prefixes):
+    order = sorted(range(total), key=lambda r: prefixes[r])
+    return order[rank::ws]
+
+
+def gen_draft_logits(req: int, dev, out: torch.Tensor):
+    g = torch.Generator(device=dev).manual_seed(1_000_003 * (req + 1))
+    out.normal_(generator=g)
+    ids = torch.randint(0, VOCAB, (K_MODES, L_BLOCK, 4), generator=g, device=dev)
+    boost = torch.rand(K_MODES, L_BLOCK, 4, generator=g, device=dev) * 6 + 4
+    out.scatter_add_(2, ids, boost)
+
+
+class Batch:
+    """Device-resident inputs and outputs of one rank's requests."""
+
+    def __init__(self, reqs, prefixes, dev, temperature=1.0, target_std=1.5, uniform_prefix=None):
+        self.reqs = reqs
+        bs = len(reqs)
+        self.bs = bs
+        self.temperature = temperature
+        self.prefix = [uniform_prefix or prefixes[r] for r in reqs]
+        smax = max(self.prefix) + W
+        self.draft = torch.empty(bs, K_MODES, L_BLOCK, VOCAB, dtype=torch.float32, device=dev)
+        self.q = torch.empty(bs, W, H, D, dtype=torch.bfloat16, device=dev)
+        self.k = torch.empty(bs, HKV, smax, D, dtype=torch.bfloat16, device=dev)
+        self.v = torch.empty(bs, HKV, smax, D, dtype=torch.bfloat16, device=dev)
+        self.target = torch.empty(bs, W, VOCAB, dtype=torch.bfloat16, device=dev)
+        self.u = torch.empty(bs, W, dtype=torch.float64, device=dev)
+        for i, r in enumerate(reqs):
+            gen_draft_logits(r, dev, self.draft[i])
+            g = torch.Generator(device=dev).manual_seed(7_000_001 * (r + 1))
+            self.q[i].copy_(torch.randn(W, H, D, generator=g, device=dev))
+            self.k[i].copy_(torch.randn(HKV, smax, D, generator=g, device=dev) * 0.5)
+            self.v[i].copy_(torch.randn(HKV, smax, D, generator=g, device=dev) * 0.5)
+            self.target[i].copy_(torch.randn(W, VOCAB, generator=g, device=dev) * target_std)
+            self.u[i].copy_(torch.rand(W, generator=g, device=dev, dtype=torch.float64))
+        self.prefix_t = torch.tensor(self.prefix, dtype=torch.int32, device=dev)
+        # outputs / intermediates
+        R = bs * K_MODES * L_BLOCK
+        self.top = torch.empty(R, BUDGET, dtype=torch.float32, device=dev)
+        self.ids = torch.empty(R, BUDGET, dtype=torch.int32, device=dev)
+        self.logz = torch.empty(R, dtype=torch.float32, device=dev)
+        self.tree = torch.empty(bs, 3, W, dtype=torch.int64, device=dev)
+        self.counts = torch.empty(bs, dtype=torch.int64, device=dev)
+        self.attn_out = torch.empty(bs, W, H, D, dtype=torch.bfloat16, device=dev)
+
+    def input_bytes(self):
+        kv = sum(2 * HKV * (p + W) * D * 2 for p in self.prefix)
+        return self.draft.numel() * 4 + self.q.numel() * 2 + kv + self.target.numel() * 2 + self.u.numel() * 8
+
+
+# ------------------------------------------------------------------------------------------------ the step
+
+class Step:
+    """One verify step over a Batch: 5 kernel launches (logits step, tree build, attention + merge, accept)."""
+
+    LAUNCHES = 5
+
+    def __init__(self, batch: Batch, splits=None):
+        from mfd_b200 import ops
+
+        self.ops = ops
+        self.b = batch
+        self.splits = splits or ops.default_splits(batch.bs, W, H, HKV, batch.k.shape[2])
+
+    def run(self, ev=None):
+        b, ops = self.b, self.ops
+        if ev is not None:
+            ev[0].record()
+        ops.topk_logz(b.draft.view(-1, VOCAB), BUDGET, ids_dtype=torch.int32, out=(b.top, b.ids, b.logz))
+        if ev is not None:
+            ev[1].record()
+        _, _, anc, _ = ops.build_trees(b.top.view(b.bs, K_MODES, L_BLOCK, BUDGET),
+                                       b.ids.view(b.bs, K_MODES, L_BLOCK, BUDGET), None, BUDGET, tree=b.tree,
+                                       counts=b.counts)
+        if ev is not None:
+            ev[2].record()
+        ops.tree_attention(b.q, b.k, b.v, anc, b.prefix_t, D ** -0.5, splits=self.splits, out=b.attn_out)
+        if ev is not None:
+            ev[3].record()
+        o = ops.accept(b.target, b.tree[:, 0], b.tree[:, 2], temperature=b.temperature,
+                       uniforms=b.u if b.temperature > 0 else None, max_steps=L_BLOCK - 1, out_len=L_BLOCK)
+        if ev is not None:
+            ev[4].record()
+        return o
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                vals = [v.strip() for v in out.stdout.strip().split(",")]
+                if len(vals) == 7:
+                    self.samples.append(vals)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._loop, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------ measurements
+
+def time_steps(step: Step, steps: int, warmup: int, ws: int, dev_index: int):
+    for _ in range(warmup):
+        step.run()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(steps)]
+    barrier(ws)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev_index) as clocks:
+        start.record()
+        for i in range(steps):
+            step.run(evs[i])
+        end.record()
+        torch.cuda.synchronize()
+    barrier(ws)
+    total_ms = start.elapsed_time(end)
+    per_kernel = {name: statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) * 1e3
+                  for j, name in enumerate(["logits_step", "tree_build", "attention", "accept"])}
+    return total_ms, per_kernel, clocks.summary()
+
+
+def north_star(dev, steps: int, warmup: int):
+    """Batch 1, greedy, prefix 4096: BASELINE's headline verify step; L2 flushed between timed steps."""
+    prefixes = [4096]
+    batch = Batch([0], prefixes, dev, temperature=0.0, target_std=1.0, uniform_prefix=4096)
+    step = Step(batch)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(max(warmup, 3)):
+        step.run()
+    times, parts = [], {"logits_step": [], "tree_build": [], "attention": [], "accept": []}
+    for _ in range(steps):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        step.run(ev)
+        torch.cuda.synchronize()
+        times.append(ev[0].elapsed_time(ev[4]) * 1e3)
+        for j, name in enumerate(parts):
+            parts[name].append(ev[j].elapsed_time(ev[j + 1]) * 1e3)
+    alg_bytes = batch.input_bytes()
+    us = statistics.mean(times)
+    pk = peaks()
+    roof_us = alg_bytes / (pk["hbm_gbs"] * 1e9) * 1e6
+    return {
+        "us_per_step": round(us, 2), "us_median": round(statistics.median(times), 2),
+        "parts_us": {k: round(statistics.mean(v), 2) for k, v in parts.items()},
+        "algorithmic_bytes": alg_bytes, "roofline_us": round(roof_us, 2),
+        "frac_of_hbm_roofline": round(roof_us / us, 4),
+        "config": "batch 1, K=8 L=16 V=151936 fp32 draft logits, B=64, prefix 4096, 32/8 heads d128, greedy",
+        "l2": "flushed (256 MB write) before every timed step",
+    }
+
+
+def e2e(dev, reqs, prefixes, steps: int, chunk: int = 16):
+    """The public API end to end: every step copies the requests' inputs from pinned host memory to the device,
+    runs the verify step, and reads the accepted lengths / tokens back."""
+    sample = reqs[:chunk]
+    batch = Batch(sample, prefixes, dev)
+    host = {name: getattr(batch, name).cpu().pin_memory() for name in ("draft", "q", "k", "v", "target", "u")}
+    host["prefix_t"] = batch.prefix_t.cpu().pin_memory()
+    step = Step(batch)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    out_bytes = 0
+
+    def one():
+        nonlocal out_bytes
+        for name, t in host.items():
+            getattr(batch, name).copy_(t, non_blocking=True)
+        o = step.run()
+        res = (o["accept_len"].cpu(), o["out_tokens"].cpu(), batch.tree.cpu())
+        out_bytes = sum(r.numel() * r.element_size() for r in res)
+        return res
+
+    one()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    return {"value": round(len(sample) / (ms / 1e3), 3), "unit": "trees/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": out_bytes, "requests_per_step": len(sample), "ms_per_step": round(ms, 3)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU reference
+
+def cpu_reference_request(req: int, prefix: int, temperature: float, ext):
+    """The reference's CPU path for one request: float32 top-k + logsumexp (hf/ddtree.py:240-245), its C++ mixture
+    builder (tree_build_ext.build_mixture), the compile_ddtree_tree mask + float32 SDPA with GQA repeat, the
+    `sample` rule (argmax / softmax + multinomial, hf/model/utils.py:28-35) and its C++ walk."""
+    g = torch.Generator().manual_seed(1_000_003 * (req + 1))
+    x = torch.randn(K_MODES, L_BLOCK, VOCAB, generator=g)
+    ids = torch.randint(0, VOCAB, (K_MODES, L_BLOCK, 4), generator=g)
+    x.scatter_add_(2, ids, torch.rand(K_MODES, L_BLOCK, 4, generator=g) * 6 + 4)
+    q = torch.randn(1, H, W, D).to(torch.bfloat16)
+    kv = (torch.randn(2, 1, HKV, prefix + W, D) * 0.5).to(torch.bfloat16)
+    target = (torch.randn(1, W, VOCAB) * 1.5).to(torch.bfloat16)
+    t0 = time.perf_counter()
+    top, tid = torch.topk(x, k=BUDGET, dim=-1)
+    lz = torch.logsumexp(x, dim=-1, keepdim=True)
+    lp = (top - lz).float()
+    if ext is not None:
+        tok, dep, parents, tree, vis = ext.build_mixture(lp.contiguous(), tid.contiguous(), torch.zeros(K_MODES), BUDGET)
+    else:
+        from oracle import oracle
+
+        tok_np, dep_np, par_np = oracle.build_mixture(lp.numpy(), tid.numpy(), torch.zeros(K_MODES).numpy(), BUDGET)
+        vis = torch.from_numpy(oracle.visibility(par_np))
+        tree = None
+    n = vis.shape[0]
+    mask = torch.zeros(1, 1, n, prefix + n)
+    blk = mask[0, 0, :, prefix:]
+    blk.fill_(torch.finfo(torch.float32).min)
+    blk.masked_fill_(vis, 0)
+    G = H // HKV
+    out = torch.nn.functional.scaled_dot_product_attention(
+        q[:, :, :n].float(), kv[0].float().repeat_interleave(G, 1)[:, :, : prefix + n],
+        kv[1].float().repeat_interleave(G, 1)[:, :, : prefix + n], attn_mask=mask, scale=D ** -0.5)
+    logits = target[:, :n].float()
+    if temperature < 1e-5:
+        post = torch.argmax(logits, dim=-1)
+    else:
+        probs = torch.softmax(logits.view(-1, VOCAB) / temperature, dim=-1)
+        post = torch.multinomial(probs, num_samples=1).view(1, n)
+    if tree is not None:
+        tree.follow(post[0].to(torch.long))
+    del out
+    return time.perf_counter() - t0
+
+
+def reference_ext():
+    try:
+        from oracle import build_ref
+
+        if build_ref.available():
+            return build_ref.load("hf"), "reference"
+    except Exception:
+        pass
+    return None, "port"
+
+
+def cpu_baseline(sample_requests: int = 3, temperature: float = 1.0):
+    torch.set_num_threads(os.cpu_count() or 1)
+    ext, kind = reference_ext()
+    prefixes = prefix_lengths(TOTAL_REQUESTS)
+    cpu_reference_request(0, 1024, temperature, ext)  # warm-up
+    secs = [cpu_reference_request(r, prefixes[r], temperature, ext) for r in range(sample_requests)]
+    per = statistics.mean(secs)
+    return {"value": round(1.0 / per, 4), "unit": "trees/s", "cores": torch.get_num_threads(), "kind": kind,
+            "sample": f"{sample_requests} requests of the benchmark workload (prefixes {prefixes[:sample_requests]}), "
+                      f"mean {per * 1e3:.1f} ms per request, host {os.cpu_count()} cpus"}
+
+
+# ------------------------------------------------------------------------------------------------ main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mfd", choices=["mfd", "reference"])
+    ap.add_argument("--requests", type=int, default=TOTAL_REQUESTS)
+    ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return
+        torch.set_num_threads(os.cpu_count() or 1)
+        ext, kind = reference_ext()
+        prefixes = prefix_lengths(TOTAL_REQUESTS)
+        per_step = 1
+        for i in range(args.warmup):
+            cpu_reference_request(i, prefixes[i], 1.0, ext)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            cpu_reference_request(i % TOTAL_REQUESTS, prefixes[i % TOTAL_REQUESTS], 1.0, ext)
+        secs = (time.perf_counter() - t0) / args.steps
+        value = per_step / secs
+        line = {"impl": "reference", "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
+                "value": round(value, 4), "unit": "trees/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "configs[4] batched verify step, one request per step (CPU)",
+                           "budget": BUDGET, "modes": K_MODES, "block": L_BLOCK, "vocab": VOCAB},
+                "cpu_baseline": {"value": round(value, 4), "unit": "trees/s", "cores": torch.get_num_threads(),
+                                 "kind": kind, "sample": "one request of the workload per step"},
+                "e2e": {"value": round(value, 4), "unit": "trees/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    ws, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local if ws > 1 else 0)
+    from mfd_b200 import _lib
+
+    _lib.load()
+    prefixes = prefix_lengths(args.requests)
+    reqs = partition(args.requests, ws, rank, prefixes)
+    batch = Batch(reqs, prefixes, dev)
+    step = Step(batch)
+    torch.cuda.synchronize()
+    total_ms, per_kernel, clocks = time_steps(step, args.steps, args.warmup, ws, dev.index or 0)
+    total_ms = max_over_ranks(ws, total_ms)
+    ms_per_step = total_ms / args.steps
+    value = args.requests / (ms_per_step / 1e3)
+
+    pk = peaks()
+    # roofline of the dominant kernel: the logits step reads each request's float32 [8, 16, V] logits once
+    logits_bytes = len(reqs) * K_MODES * L_BLOCK * VOCAB * 4
+    achieved = logits_bytes / (per_kernel["logits_step"] * 1e-6) / 1e9
+    line = {
+        "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
+        "value": round(value, 3), "unit": "trees/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 logits / bf16 attention", "data": "synthetic",
+        "config": {"workload": "configs[4]: batched verify step, 256 requests split across GPUs, T=1",
+                   "requests": args.requests, "requests_per_gpu": len(reqs), "budget": BUDGET, "modes": K_MODES,
+                   "block": L_BLOCK, "vocab": VOCAB, "heads": H, "kv_heads": HKV, "head_dim": D,
+                   "prefix": "U(1024, 8192)", "l2": "inputs (~117 MB per request) far larger than L2",
+                   "parallelism": f"requests partitioned over {ws} GPU(s), no collective"},
+        "kernels_us_per_step": {k: round(v, 2) for k, v in per_kernel.items()},
+        "roofline": {"kernel": "mfd_topk_logz (logits step)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "peak_source": pk["source"], "traffic": None,
+                     "algorithmic_bytes_per_launch": logits_bytes},
+        "clocks": clocks,
+        "gpu_launches": Step.LAUNCHES * args.steps,
+    }
+    if rank == 0 and not args.no_extras:
+        line["north_star"] = north_star(dev, steps=20, warmup=args.warmup)
+        line["e2e"] = e2e(dev, reqs, prefixes, steps=3)
+        if ws == 1:
+            line["cpu_baseline"] = cpu_baseline()
+    if ws > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        print(json.dumps(line))
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -41,13 +41,14 @@ int mfd_abi_version(void);
  * Replaces: inference/hf/ddtree.py:240-244 and 142-146 (torch.topk + torch.logsumexp),
  *           inference/hf/tree_logits.py:34-46 (row_logsumexp, top_candidates),
  *           patch:1472-1482 (row_logsumexp) and patch:1530-1545 (DDTreeDraftTopK.__call__ after its GEMM).
- * Workspace: mfd_topk_logz_workspace() bytes, zero-filled before the first use; the kernel leaves it
- * ready for the next call (calls sharing one workspace must be stream-ordered).
+ * Scratch: mfd_topk_logz_workspace() bytes (no initialisation needed).  Tickets: `rows` uint32 words of a
+ * buffer used only for tickets, zero before the first call; every kernel leaves its tickets zero again, so
+ * one ticket buffer serves all calls that are stream-ordered with each other.
  */
 size_t mfd_topk_logz_workspace(int64_t rows, int64_t vocab, int64_t k);
 int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64_t row_stride, int64_t k,
                   float* top_logp, void* top_ids, int ids_dtype, float* logz, void* workspace,
-                  size_t workspace_bytes, void* stream);
+                  size_t workspace_bytes, unsigned int* tickets, int64_t tickets_len, void* stream);
 
 /*
  * Exact best-first tree builders, batched, one request per CTA (bit-identical pop order).
@@ -59,7 +60,7 @@ int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64
  * parent -1; tail entries 0 / 0 / -1), counts [bs] int64; optional ancestor-or-self bitsets
  * anc_bits [bs, B+1, ceil((B+1)/64)] uint64 and/or dense visibility [bs, B+1, B+1] uint8.
  * status (optional device int) receives MFD_ERR_CAPACITY if a heap store overflows.
- * Limits: K <= 16, L <= 31, k <= 2047, B <= 511, K * (B + 1) <= 2046.
+ * Limits: K <= 16, L <= 31, k <= 2047, B <= 511, K * (B + 1) <= 2048.
  * Replaces: patch:1375-1407 (build_trees / build_trees_cpu, SGLang);
  *           inference/hf/tree_build_ext.py:118-203 (build_single, build_mixture, finish);
  *           inference/hf/ddtree.py:161-211 and 259-314 (the Python heaps and the visibility loop).
@@ -81,21 +82,26 @@ int mfd_build_trees(const float* top_logp, const void* top_ids, int ids_dtype, c
  * Replaces: inference/hf/model/utils.py:28-35 (sample) + inference/hf/ddtree.py:368-382
  *           (follow_verified_tree) / tree_build_ext.py:70-83 (Tree.follow);
  *           patch:2986-3010 (_target_tokens) + patch:1844-1885 (ddtree_follow).
- * Workspace: mfd_accept_workspace(bs) bytes, zero-filled before first use.
+ * Scratch: mfd_accept_workspace(bs, width) bytes; tickets: mfd_accept_tickets(bs, width) zeroed words of a
+ * ticket-only buffer (left zero again, as for mfd_topk_logz).
  */
-size_t mfd_accept_workspace(int64_t bs);
+size_t mfd_accept_workspace(int64_t bs, int64_t width);
+int64_t mfd_accept_tickets(int64_t bs, int64_t width);
 int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab, int64_t bs, int64_t width,
                const int64_t* tokens, int64_t tokens_stride, const int64_t* parents, int64_t parents_stride,
                float temperature, const double* uniforms, int64_t max_steps, const int64_t* window,
                const int64_t* prefix_lens, int64_t out_len, int64_t* posterior, int32_t* accept_len,
                int32_t* commit_lens, int64_t* bonus, int64_t* out_tokens, int64_t* accepted, int64_t* new_seq_lens,
                int64_t* move_src, int64_t* move_tgt, int64_t* hidden_index, void* workspace,
-               size_t workspace_bytes, void* stream);
+               size_t workspace_bytes, unsigned int* tickets, int64_t tickets_len, void* stream);
 
-/* Target token per row only (argmax or the reproducible sample).
+/* Target token per row only (argmax or the reproducible sample).  Scratch: mfd_sample_tokens_workspace(rows)
+ * bytes; tickets: rows + 1 zeroed words of a ticket-only buffer.
  * Replaces: inference/hf/model/utils.py:28-35 (sample); patch:2986-3010 (_target_tokens). */
+size_t mfd_sample_tokens_workspace(int64_t rows);
 int mfd_sample_tokens(const void* logits, int64_t row_stride, int64_t vocab, int64_t rows, float temperature,
-                      const double* uniforms, int64_t* posterior, void* stream);
+                      const double* uniforms, int64_t* posterior, void* workspace, size_t workspace_bytes,
+                      unsigned int* tickets, int64_t tickets_len, void* stream);
 
 /* The walk alone, posterior given [bs, width].  Replaces: patch:1844-1885 (ddtree_follow). */
 int mfd_follow(const int64_t* posterior, const int64_t* tokens, int64_t tokens_stride, const int64_t* parents,

@@ -29,13 +29,17 @@ _SIGS = {
     "mfd_last_error": (ctypes.c_char_p, []),
     "mfd_abi_version": (c_int, []),
     "mfd_topk_logz_workspace": (c_size, [c_i64, c_i64, c_i64]),
-    "mfd_topk_logz": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_size, c_vp]),
+    "mfd_topk_logz": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_size, c_vp,
+                              c_i64, c_vp]),
     "mfd_build_trees": (c_int, [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp,
                                 c_vp, c_vp, c_vp]),
-    "mfd_accept_workspace": (c_size, [c_i64]),
+    "mfd_accept_workspace": (c_size, [c_i64, c_i64]),
+    "mfd_accept_tickets": (c_i64, [c_i64, c_i64]),
     "mfd_accept": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_f32, c_vp, c_i64, c_vp, c_vp,
-                           c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_vp]),
-    "mfd_sample_tokens": (c_int, [c_vp, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp]),
+                           c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_vp, c_i64,
+                           c_vp]),
+    "mfd_sample_tokens_workspace": (c_size, [c_i64]),
+    "mfd_sample_tokens": (c_int, [c_vp, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp, c_vp, c_size, c_vp, c_i64, c_vp]),
     "mfd_follow": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp,
                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mfd_verify_inputs": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
@@ -109,10 +113,23 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 class Workspace:
-    """Per-device, per-purpose zero-initialised scratch, grown on demand.  The kernels that keep tickets in it
-    leave it zeroed; the others overwrite what they read."""
+    """Per-device, per-purpose scratch, grown on demand, plus one per-device ticket buffer.  Tickets live only in
+    the ticket buffer, which starts zeroed and which every ticketed kernel leaves zeroed; scratch needs no
+    initialisation.  Calls that share them must be ordered on one stream (as the current-stream launches are)."""
 
     _cache: dict = {}
+
+    @classmethod
+    def tickets(cls, device: torch.device, n: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), "__tickets__")
+        buf = cls._cache.get(key)
+        if buf is None or buf.numel() < n:
+            size = max(int(n), 1024)
+            if buf is not None:
+                size = max(size, 2 * buf.numel())
+            buf = torch.zeros(size, dtype=torch.int32, device=device)
+            cls._cache[key] = buf
+        return buf
 
     @classmethod
     def get(cls, device: torch.device, purpose: str, nbytes: int) -> torch.Tensor:

@@ -12,20 +12,20 @@
 //   tree_build_ext.py:70-83; SGLang _ddtree_follow_kernel patch:1706-1766 and its outputs: accepted length,
 //   commit length, bonus, emitted tokens, KV move lists, hidden-row indices, new sequence lengths).
 //
-// One CTA per logits row; the last CTA to finish a request's rows (an atomic ticket per request, no
-// waiting) walks that request's tree.  Tickets reset themselves.
+// Greedy: the rows are split over several CTAs when there are few of them; the last CTA of a row merges its
+// parts.  Sampling: one CTA per row.  In both, the last CTA to finish a request's rows (an atomic ticket per
+// request, no waiting) walks that request's tree.  Tickets reset themselves.
 #include "common.cuh"
 
 namespace mfd {
 namespace accept {
 
-constexpr int kThreads = 512;
-constexpr int kWarps = kThreads / 32;
 
 // exp(y), y <= 0, float32: Cody & Waite range reduction (ln 2 = 0.693359375 - 2.12194440e-4) and the
 // degree-7 Taylor polynomial of exp evaluated by Horner's rule; every operation individually rounded.
 __device__ __forceinline__ float exp32_rule(float y) {
-    if (!(y > -87.0f)) return 0.0f;
+    const bool ok = y > -87.0f;  // also false for NaN
+    y = ok ? y : 0.0f;
     const float n = rintf(__fmul_rn(y, 1.44269504088896341f));
     float r = __fmaf_rn(n, -0.693359375f, y);
     r = __fmaf_rn(n, 2.12194440e-4f, r);
@@ -38,7 +38,7 @@ __device__ __forceinline__ float exp32_rule(float y) {
     q = __fmaf_rn(q, r, 1.0f);
     q = __fmaf_rn(q, r, 1.0f);
     const int ni = (int)n;
-    return __uint_as_float(__float_as_uint(q) + ((uint32_t)ni << 23));
+    return ok ? __uint_as_float(__float_as_uint(q) + ((uint32_t)ni << 23)) : 0.0f;
 }
 __device__ __forceinline__ uint64_t fixed40(float x, float m, float inv_t) {
     const float e = exp32_rule(__fmul_rn(__fsub_rn(x, m), inv_t));
@@ -53,6 +53,9 @@ struct Params {
     float temperature;       // < 1e-5: greedy
     const double* uniforms;  // [bs * width]
     int64_t* posterior;      // [bs * width]
+    int parts;               // greedy: CTAs per row
+    uint64_t* part_keys;     // [rows, parts] (greedy, parts > 1)
+    unsigned int* row_tickets;  // [rows] (greedy, parts > 1)
     // walk (optional)
     int walk;
     const int64_t* tokens;   // [bs, width] stride tokens_stride
@@ -74,28 +77,6 @@ struct Params {
     int64_t* hidden_index;
     unsigned int* tickets;   // [bs]
 };
-
-__device__ __forceinline__ uint64_t block_reduce_max_u64(uint64_t v, uint64_t* red) {
-    v = warp_max_u64(v);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    uint64_t r = (lane < kWarps) ? red[lane] : 0ull;
-    return warp_max_u64(r);
-}
-__device__ __forceinline__ uint64_t block_reduce_sum_u64(uint64_t v, uint64_t* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += shfl_xor_u64(v, o);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    uint64_t r = (lane < kWarps) ? red[lane] : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) r += shfl_xor_u64(r, o);
-    return r;
-}
 
 // walk request b along its verified path (one warp); SGLang follow-kernel outputs
 __device__ void walk_request(const Params& p, int64_t b) {
@@ -149,91 +130,210 @@ __device__ void walk_request(const Params& p, int64_t b) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads) accept_kernel(Params p) {
-    __shared__ uint64_t red[kWarps];
+template <int NT>
+__device__ __forceinline__ uint64_t block_reduce_max_u64(uint64_t v, uint64_t* red) {
+    constexpr int NW = NT / 32;
+    v = warp_max_u64(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    uint64_t r = (lane < NW) ? red[lane] : 0ull;
+    return warp_max_u64(r);
+}
+
+// Best (value, first index) key over columns [c0, c1) of row x, one thread's share (vector loads when aligned).
+template <int NT>
+__device__ __forceinline__ uint64_t argmax_share(const uint16_t* x, int64_t c0, int64_t c1) {
+    float bv = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    const bool vec = ((((uintptr_t)(x + c0)) & 15u) == 0);
+    int64_t c = c0;
+    if (vec) {
+        const int64_t nv = (c1 - c0) / 8;
+        const uint16_t* xv = x + c0;
+        for (int64_t v0 = 0; v0 < nv; v0 += 4 * NT) {
+            uint4 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t vi = v0 + (int64_t)u * NT + threadIdx.x;
+                w[u] = vi < nv ? ldg_stream_u4(xv + vi * 8) : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t vi = v0 + (int64_t)u * NT + threadIdx.x;
+                const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float a = bf16lo(ws[q]), b = bf16hi(ws[q]);
+                    const uint32_t ia = (uint32_t)(c0 + vi * 8 + 2 * q);
+                    if (vi < nv && (a > bv || bi == 0xffffffffu)) { bv = a; bi = ia; }
+                    if (vi < nv && b > bv) { bv = b; bi = ia + 1; }
+                }
+            }
+        }
+        c = c0 + nv * 8;
+    }
+    for (int64_t cc = c + threadIdx.x; cc < c1; cc += NT) {
+        const float a = bf16_at(x + cc);
+        if (a > bv || bi == 0xffffffffu) { bv = a; bi = (uint32_t)cc; }
+    }
+    return bi == 0xffffffffu ? 0ull : topk_key(bv, bi);
+}
+
+constexpr int kGreedyThreads = 256;
+
+// greedy: CTA (row, part) reduces its part; the last part of a row reduces the parts; the last row of a
+// request walks the tree
+__global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
+    __shared__ uint64_t red[kGreedyThreads / 32];
     __shared__ int flag;
+    const int64_t row = blockIdx.x / p.parts;
+    const int part = blockIdx.x % p.parts;
+    const int64_t b = row / p.width;
+    const uint16_t* x = p.logits + row * p.row_stride;
+    const int64_t V = p.vocab;
+    int64_t chunk = (V + p.parts - 1) / p.parts;
+    chunk = (chunk + 7) / 8 * 8;
+    const int64_t c0 = min(V, (int64_t)part * chunk), c1 = min(V, c0 + chunk);
+    const uint64_t best = block_reduce_max_u64<kGreedyThreads>(argmax_share<kGreedyThreads>(x, c0, c1), red);
+    if (p.parts > 1) {
+        if (threadIdx.x == 0) {
+            p.part_keys[row * p.parts + part] = best;
+            __threadfence();
+            const unsigned int t = atomicAdd(p.row_tickets + row, 1u);
+            flag = (t == (unsigned int)(p.parts - 1));
+        }
+        __syncthreads();
+        if (!flag) return;
+        if (threadIdx.x < 32) {
+            __threadfence();
+            uint64_t k = 0;
+            for (int i = threadIdx.x; i < p.parts; i += 32) {
+                const uint64_t v = __ldcg(p.part_keys + row * p.parts + i);
+                k = v > k ? v : k;
+            }
+            k = warp_max_u64(k);
+            if (threadIdx.x == 0) {
+                p.posterior[row] = (int64_t)key_index(k);
+                p.row_tickets[row] = 0u;
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        p.posterior[row] = (int64_t)key_index(best);
+    }
+    if (!p.walk) return;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned int t = atomicAdd(p.tickets + b, 1u);
+        flag = (t == (unsigned int)(p.width - 1));
+    }
+    __syncthreads();
+    if (!flag) return;
+    __threadfence();
+    if (threadIdx.x < 32) walk_request(p, b);
+    if (threadIdx.x == 0) p.tickets[b] = 0u;
+}
+
+// sum of the fixed-point weights of x[c0, c1) (one thread, sequential, vector loads when aligned)
+__device__ __forceinline__ uint64_t weight_sum(const uint16_t* x, int64_t c0, int64_t c1, float m, float inv_t) {
+    uint64_t z = 0;
+    int64_t c = c0;
+    if ((((uintptr_t)(x + c)) & 15u) == 0) {
+        for (; c + 8 <= c1; c += 8) {
+            const uint4 w = *reinterpret_cast<const uint4*>(x + c);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) z += fixed40(bf16lo(ws[q]), m, inv_t) + fixed40(bf16hi(ws[q]), m, inv_t);
+        }
+    }
+    for (; c < c1; ++c) z += fixed40(bf16_at(x + c), m, inv_t);
+    return z;
+}
+
+constexpr int kSampleThreads = 512;
+
+// stochastic: one CTA per row.  Pass 1: the row max (coalesced).  Pass 2: thread t sums the weights of its
+// contiguous segment; a block scan turns the sums into prefix offsets and Z.  Pass 3: warp 0 finds the crossing
+// inside the one segment that holds floor(u * Z).  All sums are integers, so no order changes the result.
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(Params p) {
+    __shared__ uint64_t red[kSampleThreads / 32];
+    __shared__ uint64_t seg_sum[kSampleThreads];
+    __shared__ int flag;
+    __shared__ int64_t s_token;
     const int64_t row = blockIdx.x;
     const int64_t b = row / p.width;
     const uint16_t* x = p.logits + row * p.row_stride;
     const int64_t V = p.vocab;
-    const bool vec = ((((uintptr_t)x) & 15u) == 0) && (V % 8 == 0);
-    const int64_t nv = vec ? V / 8 : 0;
-
-    // pass 1: max (and first index of it)
-    float bv = -INFINITY;
-    uint32_t bi = 0xffffffffu;
-    for (int64_t v = threadIdx.x; v < nv; v += kThreads) {
-        const uint4 w = ldg_stream_u4(x + v * 8);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float a = bf16lo(ws[q]), c = bf16hi(ws[q]);
-            if (a > bv || bi == 0xffffffffu) { bv = a; bi = (uint32_t)(v * 8 + 2 * q); }
-            if (c > bv) { bv = c; bi = (uint32_t)(v * 8 + 2 * q + 1); }
-        }
-    }
-    for (int64_t c = nv * 8 + threadIdx.x; c < V; c += kThreads) {
-        const float a = bf16_at(x + c);
-        if (a > bv || bi == 0xffffffffu) { bv = a; bi = (uint32_t)c; }
-    }
-    const uint64_t mine = (bi == 0xffffffffu) ? 0ull : topk_key(bv, bi);
-    const uint64_t best = block_reduce_max_u64(mine, red);
-    int64_t token = (int64_t)key_index(best);
-
-    if (p.temperature >= 1e-5f) {
-        // stochastic: pass 2 (Z), pass 3 (the crossing), both from L2
-        const float m = key_value(best);
-        const float inv_t = __frcp_rn(p.temperature);
-        uint64_t z = 0;
-        for (int64_t c = threadIdx.x; c < V; c += kThreads) z += fixed40(bf16_at(x + c), m, inv_t);
-        const uint64_t Z = block_reduce_sum_u64(z, red);
-        const double u = p.uniforms[row];
-        const uint64_t target = (uint64_t)floor(u * (double)Z);
-        // scan tiles of kThreads consecutive elements in order; thread t holds element tile*kThreads + t
-        uint64_t acc = 0;
-        token = V - 1;
-        for (int64_t t0 = 0; t0 < V; t0 += kThreads) {
-            const int64_t c = t0 + threadIdx.x;
-            const uint64_t e = c < V ? fixed40(bf16_at(x + c), m, inv_t) : 0ull;
-            // inclusive scan over the tile in thread order
-            uint64_t incl = e;
-            const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint64_t y = shfl_u64(incl, lane >= o ? lane - o : lane);
-                if (lane >= o) incl += y;
-            }
-            __syncthreads();
-            if (lane == 31) red[warp] = incl;
-            __syncthreads();
-            uint64_t before = 0, tile = 0;
-            for (int w2 = 0; w2 < kWarps; ++w2) {
-                const uint64_t s = red[w2];
-                if (w2 < warp) before += s;
-                tile += s;
-            }
-            const uint64_t cum = acc + before + incl;
-            const bool cross = c < V && cum > target;
-            // first crossing element in the tile
-            const uint32_t bal = __ballot_sync(MFD_FULL_MASK, cross);
-            __syncthreads();
-            if (lane == 0) red[warp] = bal ? (uint64_t)(warp * 32 + __ffs(bal) - 1) : ~0ull;
-            __syncthreads();
-            uint64_t first = ~0ull;
-            for (int w2 = 0; w2 < kWarps; ++w2) first = red[w2] < first ? red[w2] : first;
-            if (first != ~0ull) {
-                token = t0 + (int64_t)first;
-                break;
-            }
-            acc += tile;
-        }
-    }
-    if (threadIdx.x == 0) p.posterior[row] = token;
-
-    if (!p.walk) return;
-    __threadfence();
+    const uint64_t best = block_reduce_max_u64<kSampleThreads>(argmax_share<kSampleThreads>(x, 0, V), red);
+    const float m = key_value(best);
+    const float inv_t = __frcp_rn(p.temperature);
+    int64_t seg = (V + kSampleThreads - 1) / kSampleThreads;
+    seg = (seg + 7) / 8 * 8;
+    const int64_t a0 = min(V, (int64_t)threadIdx.x * seg), a1 = min(V, a0 + seg);
+    const uint64_t mine = weight_sum(x, a0, a1, m, inv_t);
+    seg_sum[threadIdx.x] = mine;
     __syncthreads();
+    if (threadIdx.x < 32) {
+        // warp 0: exclusive prefix over the 512 segment sums (16 per lane, in order)
+        const int lane = threadIdx.x;
+        uint64_t loc[16];
+        uint64_t tot = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            loc[i] = seg_sum[lane * 16 + i];
+            tot += loc[i];
+        }
+        uint64_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = shfl_u64(incl, lane >= o ? lane - o : lane);
+            if (lane >= o) incl += y;
+        }
+        const uint64_t Z = shfl_u64(incl, 31);
+        const uint64_t target = (uint64_t)floor(p.uniforms[row] * (double)Z);
+        uint64_t run = incl - tot;  // exclusive prefix of this lane's first segment
+        int hit = -1;
+        uint64_t before = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            if (hit < 0 && run + loc[i] > target) { hit = lane * 16 + i; before = run; }
+            run += loc[i];
+        }
+        const uint32_t bal = __ballot_sync(MFD_FULL_MASK, hit >= 0);
+        const int src = __ffs(bal) - 1;  // segments are in lane order: the first lane with a hit holds the crossing
+        const int segi = __shfl_sync(MFD_FULL_MASK, hit, src);
+        const uint64_t base = shfl_u64(before, src);
+        // pass 3 over segment segi: lane l takes elements [s0 + l*sub, ...)
+        const int64_t s0 = min(V, (int64_t)segi * seg), s1 = min(V, s0 + seg);
+        const int64_t sub = (s1 - s0 + 31) / 32;
+        const int64_t l0 = min(s1, s0 + lane * sub), l1 = min(s1, l0 + sub);
+        const uint64_t ls = weight_sum(x, l0, l1, m, inv_t);
+        uint64_t li = ls;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = shfl_u64(li, lane >= o ? lane - o : lane);
+            if (lane >= o) li += y;
+        }
+        const uint64_t lex = base + li - ls;
+        const bool in_me = (lex <= target) && (target < lex + ls);
+        const uint32_t b2 = __ballot_sync(MFD_FULL_MASK, in_me && ls > 0);
+        if (b2 && lane == __ffs(b2) - 1) {
+            uint64_t c = lex;
+            int64_t tok = l1 - 1;
+            for (int64_t j = l0; j < l1; ++j) {
+                c += fixed40(bf16_at(x + j), m, inv_t);
+                if (c > target) { tok = j; break; }
+            }
+            s_token = tok;
+        }
+        if (!b2 && lane == 0) s_token = V - 1;  // unreachable when Z > 0
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) p.posterior[row] = s_token;
+    if (!p.walk) return;
     if (threadIdx.x == 0) {
+        __threadfence();
         const unsigned int t = atomicAdd(p.tickets + b, 1u);
         flag = (t == (unsigned int)(p.width - 1));
     }
@@ -269,7 +369,38 @@ static int accept_common_checks(const char* fn, int64_t bs, int64_t width, const
     return MFD_OK;
 }
 
-extern "C" size_t mfd_accept_workspace(int64_t bs) { return (size_t)(bs > 0 ? bs : 1) * sizeof(unsigned int); }
+static int greedy_parts(int64_t rows) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = 4LL * sms;
+    int64_t parts = (want + rows - 1) / rows;
+    return (int)(parts < 1 ? 1 : (parts > 32 ? 32 : parts));
+}
+
+// scratch: part keys [rows * 32]; tickets (a buffer that is only ever used for tickets and is left zeroed):
+// request tickets [bs] then row tickets [rows]
+static size_t accept_scratch(int64_t rows) { return (size_t)(rows > 0 ? rows : 1) * 32 * 8; }
+
+static int launch_accept(accept::Params& p, int64_t rows, void* scratch, unsigned int* tickets, cudaStream_t stream,
+                         const char* fn) {
+    p.tickets = tickets;
+    p.row_tickets = tickets + (p.bs > 0 ? p.bs : 1);
+    p.part_keys = (uint64_t*)scratch;
+    if (p.temperature < 1e-5f) {
+        p.parts = greedy_parts(rows);
+        accept::greedy_kernel<<<(unsigned)(rows * p.parts), accept::kGreedyThreads, 0, stream>>>(p);
+    } else {
+        p.parts = 1;
+        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
+    }
+    MFD_CHECK_LAUNCH(fn);
+    return MFD_OK;
+}
+
+extern "C" size_t mfd_accept_workspace(int64_t bs, int64_t width) { return accept_scratch(bs * width); }
+
+extern "C" int64_t mfd_accept_tickets(int64_t bs, int64_t width) { return (bs > 0 ? bs : 1) + bs * width; }
 
 extern "C" int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab, int64_t bs, int64_t width,
                           const int64_t* tokens, int64_t tokens_stride, const int64_t* parents,
@@ -277,7 +408,8 @@ extern "C" int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab,
                           const int64_t* window, const int64_t* prefix_lens, int64_t out_len, int64_t* posterior,
                           int32_t* accept_len, int32_t* commit_lens, int64_t* bonus, int64_t* out_tokens,
                           int64_t* accepted, int64_t* new_seq_lens, int64_t* move_src, int64_t* move_tgt,
-                          int64_t* hidden_index, void* workspace, size_t workspace_bytes, void* stream) {
+                          int64_t* hidden_index, void* workspace, size_t workspace_bytes, unsigned int* tickets,
+                          int64_t tickets_len, void* stream) {
     int rc = accept_common_checks("mfd_accept", bs, width, tokens, parents, out_len);
     if (rc) return rc;
     if (vocab < 1 || vocab >= 0x7fffffff || row_stride < vocab) {
@@ -293,8 +425,10 @@ extern "C" int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab,
         set_error("mfd_accept: temperature > 0 needs uniforms");
         return MFD_ERR_INVALID;
     }
-    if (!workspace || workspace_bytes < mfd_accept_workspace(bs)) {
-        set_error("mfd_accept: workspace of %zu bytes needed", mfd_accept_workspace(bs));
+    if (!workspace || workspace_bytes < mfd_accept_workspace(bs, width) || !tickets ||
+        tickets_len < mfd_accept_tickets(bs, width)) {
+        set_error("mfd_accept: workspace of %zu bytes and %lld zeroed tickets needed", mfd_accept_workspace(bs, width),
+                  (long long)mfd_accept_tickets(bs, width));
         return MFD_ERR_INVALID;
     }
     accept::Params p = {};
@@ -324,15 +458,14 @@ extern "C" int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab,
     p.move_src = move_src;
     p.move_tgt = move_tgt;
     p.hidden_index = hidden_index;
-    p.tickets = (unsigned int*)workspace;
-    const int64_t rows = bs * width;
-    accept::accept_kernel<<<(unsigned)rows, accept::kThreads, 0, (cudaStream_t)stream>>>(p);
-    MFD_CHECK_LAUNCH("mfd_accept");
-    return MFD_OK;
+    return launch_accept(p, bs * width, workspace, tickets, (cudaStream_t)stream, "mfd_accept");
 }
 
+extern "C" size_t mfd_sample_tokens_workspace(int64_t rows) { return accept_scratch(rows); }
+
 extern "C" int mfd_sample_tokens(const void* logits, int64_t row_stride, int64_t vocab, int64_t rows,
-                                 float temperature, const double* uniforms, int64_t* posterior, void* stream) {
+                                 float temperature, const double* uniforms, int64_t* posterior, void* workspace,
+                                 size_t workspace_bytes, unsigned int* tickets, int64_t tickets_len, void* stream) {
     if (rows < 0 || vocab < 1 || vocab >= 0x7fffffff || row_stride < vocab) {
         set_error("mfd_sample_tokens: invalid sizes rows=%lld vocab=%lld", (long long)rows, (long long)vocab);
         return MFD_ERR_INVALID;
@@ -352,9 +485,12 @@ extern "C" int mfd_sample_tokens(const void* logits, int64_t row_stride, int64_t
     p.uniforms = uniforms;
     p.posterior = posterior;
     p.walk = 0;
-    accept::accept_kernel<<<(unsigned)rows, accept::kThreads, 0, (cudaStream_t)stream>>>(p);
-    MFD_CHECK_LAUNCH("mfd_sample_tokens");
-    return MFD_OK;
+    if (!workspace || workspace_bytes < mfd_sample_tokens_workspace(rows) || !tickets || tickets_len < rows + 1) {
+        set_error("mfd_sample_tokens: workspace of %zu bytes and %lld zeroed tickets needed",
+                  mfd_sample_tokens_workspace(rows), (long long)(rows + 1));
+        return MFD_ERR_INVALID;
+    }
+    return launch_accept(p, rows, workspace, tickets, (cudaStream_t)stream, "mfd_sample_tokens");
 }
 
 extern "C" int mfd_follow(const int64_t* posterior, const int64_t* tokens, int64_t tokens_stride,

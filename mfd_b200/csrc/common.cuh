@@ -96,6 +96,41 @@ __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
     return ((uint64_t)hi << 32) | lo;
 }
 
+// ------------------------------------------------------------------ mbarrier + bulk async copy (no multicast)
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+// global -> this CTA's shared memory, completion counted on `bar`; src, dst 16-byte aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+// order this thread's earlier generic-proxy shared-memory accesses before later async-proxy (bulk copy) ones
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Wait for phase `parity` of `bar` to complete, at most `max_tries` polls; false on timeout (the caller records
+// an error status and stops instead of spinning forever).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_tries = (1u << 26)) {
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t i = 0; i < max_tries; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // online (max, sum of exp(x - max)) pair merge; -inf maxima carry a zero sum
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
     float mn = fmaxf(m, m2);

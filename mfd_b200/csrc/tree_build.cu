@@ -124,13 +124,38 @@ __global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
     const void* gids = p.ids_i64 ? (const void*)((const int64_t*)p.ids + (size_t)b * K * L * k)
                                  : (const void*)((const int32_t*)p.ids + (size_t)b * K * L * k);
 
-    // ---- stage the candidate tables (all warps)
+    // ---- stage the candidate tables (all warps): 16-byte asynchronous copies when the tables are whole and
+    // aligned, so every thread has many copies in flight; element copies otherwise
     const int rows = K * L;
-    for (int i = threadIdx.x; i < rows * p.ks; i += kThreads) {
-        const int row = i / p.ks, r = i % p.ks;
-        const size_t o = (size_t)row * k + r;
-        s.lp[i] = glp[o];
-        s.ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[o] : ((const int32_t*)gids)[o];
+    const int n_el = rows * p.ks;
+    const bool whole = p.ks == k && (n_el % 4) == 0 && (((uintptr_t)glp) & 15u) == 0 &&
+                       (((uintptr_t)gids) & 15u) == 0;
+    if (whole) {
+        for (int c = threadIdx.x; c < n_el / 4; c += kThreads) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s.lp + 4 * c)),
+                         "l"(glp + 4 * c));
+            if (!p.ids_i64)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s.ids + 4 * c)),
+                             "l"((const int32_t*)gids + 4 * c));
+        }
+        asm volatile("cp.async.commit_group;");
+        if (p.ids_i64) {
+            const longlong2* g2 = (const longlong2*)gids;
+#pragma unroll 4
+            for (int c = threadIdx.x; c < n_el / 2; c += kThreads) {
+                const longlong2 v = __ldg(g2 + c);
+                s.ids[2 * c] = (int32_t)v.x;
+                s.ids[2 * c + 1] = (int32_t)v.y;
+            }
+        }
+        asm volatile("cp.async.wait_all;");
+    } else {
+        for (int i = threadIdx.x; i < n_el; i += kThreads) {
+            const int row = i / p.ks, r = i % p.ks;
+            const size_t o = (size_t)row * k + r;
+            s.lp[i] = glp[o];
+            s.ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[o] : ((const int32_t*)gids)[o];
+        }
     }
     for (int i = threadIdx.x; i < p.hcap; i += kThreads) s.hash[i] = kEmptyHash;
     for (int i = threadIdx.x; i < cap; i += kThreads) {
@@ -374,7 +399,7 @@ struct Plan {
 static Plan plan(int K, int L, int k, int B) {
     Plan pl;
     const int W = B + 1;
-    const int64_t live_max = (int64_t)K + (int64_t)K * B + 2;  // pops <= K*B, each adds at most one entry
+    const int64_t live_max = (int64_t)K * (B + 1);  // K initial entries; pops <= K*B, each adds at most one
     pl.S = (int)((live_max + 31) / 32);
     if (pl.S < 2) pl.S = 2;
     pl.hcap = 64;
@@ -425,7 +450,7 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
         return MFD_ERR_INVALID;
     }
     tree::Plan pl = tree::plan((int)num_modes, (int)depth_limit, (int)topk, (int)budget);
-    if ((int64_t)num_modes + num_modes * budget + 2 > 32 * 64) {
+    if (num_modes * (budget + 1) > 32 * 64) {
         set_error("mfd_build_trees: K*(B+1) too large for the entry store (K=%lld B=%lld)", (long long)num_modes,
                   (long long)budget);
         return MFD_ERR_UNSUPPORTED;

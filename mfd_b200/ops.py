@@ -43,9 +43,10 @@ def topk_logz(x: torch.Tensor, k: int, ids_dtype: torch.dtype = torch.int64, out
     L = _lib.lib()
     ws_bytes = L.mfd_topk_logz_workspace(R, V, k)
     ws = Workspace.get(dev, "topk", ws_bytes)
+    tk = Workspace.tickets(dev, R)
     rc = L.mfd_topk_logz(rows2d.data_ptr(), MFD_BF16 if x.dtype == torch.bfloat16 else MFD_F32, R, V,
                          rows2d.stride(0), k, top.data_ptr(), ids.data_ptr(), _ids_code(ids.dtype),
-                         ptr(logz), ws.data_ptr(), ws.numel(), stream_ptr(dev))
+                         ptr(logz), ws.data_ptr(), ws.numel(), tk.data_ptr(), tk.numel(), stream_ptr(dev))
     check(rc, "mfd_topk_logz")
     lead = x.shape[:-1]
     return top.view(*lead, k), ids.view(*lead, k), logz.view(*lead)
@@ -116,14 +117,15 @@ def accept(logits: torch.Tensor, tokens: torch.Tensor, parents: torch.Tensor, te
         o["move_src"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
         o["move_tgt"] = torch.empty(bs, out_len, dtype=torch.int64, device=dev)
     L = _lib.lib()
-    ws = Workspace.get(dev, "accept", L.mfd_accept_workspace(bs))
+    ws = Workspace.get(dev, "accept", L.mfd_accept_workspace(bs, W))
+    tk = Workspace.tickets(dev, L.mfd_accept_tickets(bs, W))
     rc = L.mfd_accept(rows.data_ptr(), rows.stride(0), V, bs, W, tokens.data_ptr(), tokens.stride(0),
                       parents.data_ptr(), parents.stride(0), float(temperature), ptr(uniforms), max_steps,
                       ptr(window), ptr(prefix_lens), out_len, o["posterior"].data_ptr(), o["accept_len"].data_ptr(),
                       o["commit_lens"].data_ptr(), o["bonus"].data_ptr(), o["out_tokens"].data_ptr(),
                       o["accepted"].data_ptr(), o["new_seq_lens"].data_ptr(), ptr(o.get("move_src")),
                       ptr(o.get("move_tgt")), o["hidden_index"].data_ptr(), ws.data_ptr(), ws.numel(),
-                      stream_ptr(dev))
+                      tk.data_ptr(), tk.numel(), stream_ptr(dev))
     check(rc, "mfd_accept")
     return o
 
@@ -143,8 +145,11 @@ def sample_tokens(logits: torch.Tensor, temperature: float = 0.0, uniforms: torc
         out = torch.empty(R, dtype=torch.int64, device=dev)
     if uniforms is not None:
         uniforms = uniforms.to(torch.float64).reshape(-1).contiguous()
-    rc = _lib.lib().mfd_sample_tokens(rows.data_ptr(), rows.stride(0), V, R, float(temperature), ptr(uniforms),
-                                      out.data_ptr(), stream_ptr(dev))
+    L = _lib.lib()
+    ws = Workspace.get(dev, "accept", L.mfd_sample_tokens_workspace(R))
+    tk = Workspace.tickets(dev, R + 1)
+    rc = L.mfd_sample_tokens(rows.data_ptr(), rows.stride(0), V, R, float(temperature), ptr(uniforms),
+                             out.data_ptr(), ws.data_ptr(), ws.numel(), tk.data_ptr(), tk.numel(), stream_ptr(dev))
     check(rc, "mfd_sample_tokens")
     return out.view(logits.shape[:-1])
 

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 def test_error_path_without_gpu_reports_status():
     lib = _lib.load()
     # invalid sizes are rejected on the host before any CUDA call
-    rc = lib.mfd_topk_logz(None, 0, 1, 10, 10, 0, None, None, 3, None, None, 0, None)
+    rc = lib.mfd_topk_logz(None, 0, 1, 10, 10, 0, None, None, 3, None, None, 0, None, 0, None)
     assert rc == 1
     assert b"invalid sizes" in lib.mfd_last_error()
     rc = lib.mfd_build_trees(None, None, 2, None, 1, 32, 4, 4, 4, 0, None, None, None, None, None, None)
