@@ -51,6 +51,21 @@ int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64
                   size_t workspace_bytes, unsigned int* tickets, int64_t tickets_len, void* stream);
 
 /*
+ * mfd_topk_logz for callers that may not allocate device memory at call time (a host whose memory pool owns
+ * the whole GPU, a serving path where cudaMalloc's implicit synchronisation is not allowed, a plugin interface
+ * that passes only inputs and outputs).  Same arguments, results and errors as mfd_topk_logz, without the
+ * workspace and tickets: the scratch is one static device array in the library (4 MiB of partial records plus
+ * tickets for 16384 rows; every GPU that loads the library holds it until the process exits).  Calls needing
+ * more (mfd_topk_logz_workspace(rows, vocab, k) > 4 MiB, or rows > 16384) fail with MFD_ERR_UNSUPPORTED.
+ * The first call on each device resolves the array's device address (make it before any stream capture).
+ * All calls share the array: calls that may run at the same time on the GPU (other streams, other threads)
+ * race; stream-ordered calls do not.  Allocates nothing.
+ * Replaces: nothing in the reference (no counterpart; an allocation-free form of the entry point above).
+ */
+int mfd_topk_logz_static(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64_t row_stride, int64_t k,
+                         float* top_logp, void* top_ids, int ids_dtype, float* logz, void* stream);
+
+/*
  * Exact best-first tree builders, batched, one request per CTA (bit-identical pop order).
  *   top_logp [bs, K, L, k] float32, top_ids [bs, K, L, k] int32/int64, log_prior [bs, K] (null = zeros).
  *   single = 1 (K must be 1): the DDTree heap, float64 key -logw, ties by the rank tuple;

@@ -31,6 +31,7 @@ _SIGS = {
     "mfd_topk_logz_workspace": (c_size, [c_i64, c_i64, c_i64]),
     "mfd_topk_logz": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_size, c_vp,
                               c_i64, c_vp]),
+    "mfd_topk_logz_static": (c_int, [c_vp, c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_int, c_vp, c_vp]),
     "mfd_build_trees": (c_int, [c_vp, c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp,
                                 c_vp, c_vp, c_vp]),
     "mfd_accept_workspace": (c_size, [c_i64, c_i64]),
