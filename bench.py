@@ -28,7 +28,6 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
 import time
 
 import torch
@@ -180,6 +179,9 @@ class Step:
 # ------------------------------------------------------------------------------------------------ clocks
 
 class ClockSampler:
+    """nvidia-smi sampling SM clocks and throttle reasons every 200 ms, started (one fork) before the timed region
+    and stopped after it, so that no process is spawned while kernels are being launched."""
+
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -187,30 +189,32 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.samples = []
-        self._stop = threading.Event()
-        self._t = None
-
-    def _loop(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                vals = [v.strip() for v in out.stdout.strip().split(",")]
-                if len(vals) == 7:
-                    self.samples.append(vals)
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+        self._proc = None
 
     def __enter__(self):
-        self._t = threading.Thread(target=self._loop, daemon=True)
-        self._t.start()
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                           "--format=csv,noheader,nounits", "-lms", "200"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)  # let the first sample land before timing starts
+        except Exception:
+            self._proc = None
         return self
 
     def __exit__(self, *a):
-        self._stop.set()
-        if self._t:
-            self._t.join(timeout=10)
+        if self._proc is None:
+            return
+        time.sleep(0.25)  # one more sample after the timed region
+        self._proc.terminate()
+        try:
+            out, _ = self._proc.communicate(timeout=10)
+        except Exception:
+            self._proc.kill()
+            out, _ = self._proc.communicate()
+        for line in out.splitlines():
+            vals = [v.strip() for v in line.split(",")]
+            if len(vals) == 7:
+                self.samples.append(vals)
 
     def summary(self):
         if not self.samples:

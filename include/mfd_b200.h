@@ -153,6 +153,38 @@ int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int64_t sq_h, 
                        int64_t splits, void* out, int64_t so_b, int64_t so_n, int64_t so_h, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/*
+ * Tree verification of one gated-delta-rule layer from the committed state S0 (fla layout, o = S^T q):
+ *   u_i + sum_{j strict ancestor of i} beta_i e^{G_i-G_j} (k_i.k_j) u_j = beta_i (v_i - e^{G_i} S0^T k_i)
+ *   o_i = e^{G_i} S0^T q_i + sum_{j ancestor of i or i} e^{G_i-G_j} (q_i.k_j) u_j
+ *   states_i = e^{G_i} S0 + sum_{j ancestor of i or i} e^{G_i-G_j} k_j u_j^T      (only if states != null)
+ * q, k [n, HK, Dk] bf16 (node strides sq, sk; q already l2-normalised and scaled, k l2-normalised); v [n, H, Dv]
+ * bf16 (node stride sv); g_cum, beta [n, H] float32 (node strides sg, sb; g_cum = log decay summed along the root
+ * path); s0 [H, Dk, Dv] float32; anc [n, n] int8 (row stride sa), row i = ancestors of i and i, nodes in
+ * topological order.  Value head h reads key head h / (H / HK).  Outputs u, o [n, H, Dv] float32 and, if
+ * states != null, states [n, H, Dk, Dv] float32.  status (optional, device int): 0, or 1 when anc is not the
+ * ancestor matrix of a topologically ordered tree (outputs then unspecified).
+ * Limits: n <= 128, Dk, Dv <= 128 and multiples of 4.
+ * Replaces: inference/hf/tree_gdn_kernel.py:153-171 (tree_gdn: _tree_kkt, fla solve_tril, _tree_u), and the
+ *           state formula of inference/hf/qwen35_tree.py:134-137 evaluated for every node.
+ */
+int mfd_tree_gdn(const void* q, int64_t sq, const void* k, int64_t sk, const void* v, int64_t sv,
+                 const float* g_cum, int64_t sg, const float* beta, int64_t sb, const float* s0, const int8_t* anc,
+                 int64_t sa, int64_t n, int64_t num_heads, int64_t num_k_heads, int64_t dk, int64_t dv, float* u,
+                 float* o, float* states, int* status, void* stream);
+
+/*
+ * Inputs of mfd_tree_gdn from the pre-convolution projections: per node i and channel c,
+ *   y = bf16(silu(sum_t w[c][t] * X[conv_index[i][t]][c]))  with X = [conv_state^T ; x] (window oldest first),
+ * then q, k heads l2-normalised (y / sqrt(sum y^2 + 1e-6)), q times scale.  x [n, conv_dim] bf16 with
+ * conv_dim = (2 HK + H) D (channels: q heads, k heads, v heads); conv_state, conv_w [conv_dim, kernel] bf16;
+ * conv_index [n, kernel] int32.  Outputs q, k [n, HK, D], v [n, H, D] bf16 (contiguous).  D <= 128.
+ * Replaces: inference/hf/tree_gdn_kernel.py:135-150 (tree_prep, the _tree_prep kernel at 27-56).
+ */
+int mfd_tree_prep(const void* x, const void* conv_state, const int32_t* conv_index, const void* conv_w, int64_t n,
+                  int64_t conv_dim, int64_t kernel, int64_t num_k_heads, int64_t num_heads, int64_t head_dim,
+                  float scale, void* q, void* k, void* v, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -242,3 +242,63 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch
                               stream_ptr(dev))
     check(rc, "mfd_tree_attention")
     return out
+
+
+# ----------------------------------------------------------------------------------------------- tree GDN
+
+def tree_gdn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_cum: torch.Tensor, beta: torch.Tensor,
+             s0: torch.Tensor, anc8: torch.Tensor, emit_states: bool = False, out=None, status=None):
+    """q, k [n, HK, Dk] bf16, v [n, H, Dv] bf16, g_cum/beta [n, H] f32, s0 [H, Dk, Dv] f32, anc8 [n, n] int8.
+
+    Returns (u, o) float32 [n, H, Dv], plus the per-node states float32 [n, H, Dk, Dv] when emit_states."""
+    dev = require_cuda(q, k, v, g_cum, beta, s0, anc8)
+    n, HK, Dk = k.shape
+    H, Dv = v.shape[1], v.shape[2]
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError("tree_gdn: q, k, v must be bfloat16")
+    if q.shape != k.shape or v.shape[0] != n or tuple(anc8.shape) != (n, n):
+        raise RuntimeError("tree_gdn: inconsistent shapes")
+    q = q if q.stride(2) == 1 and q.stride(1) == Dk else q.contiguous()
+    k = k if k.stride(2) == 1 and k.stride(1) == Dk else k.contiguous()
+    v = v if v.stride(2) == 1 and v.stride(1) == Dv else v.contiguous()
+    g_cum = g_cum.float()
+    beta = beta.float()
+    g_cum = g_cum if g_cum.stride(1) == 1 else g_cum.contiguous()
+    beta = beta if beta.stride(1) == 1 else beta.contiguous()
+    s0 = s0.float().contiguous()
+    anc8 = anc8.to(torch.int8)
+    anc8 = anc8 if anc8.stride(1) == 1 else anc8.contiguous()
+    if out is None:
+        u = torch.empty(n, H, Dv, dtype=torch.float32, device=dev)
+        o = torch.empty(n, H, Dv, dtype=torch.float32, device=dev)
+        st = torch.empty(n, H, Dk, Dv, dtype=torch.float32, device=dev) if emit_states else None
+    else:
+        u, o, st = out
+    rc = _lib.lib().mfd_tree_gdn(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                                 g_cum.data_ptr(), g_cum.stride(0), beta.data_ptr(), beta.stride(0), s0.data_ptr(),
+                                 anc8.data_ptr(), anc8.stride(0), n, H, HK, Dk, Dv, u.data_ptr(), o.data_ptr(),
+                                 ptr(st), ptr(status), stream_ptr(dev))
+    check(rc, "mfd_tree_gdn")
+    return (u, o, st) if emit_states else (u, o)
+
+
+def tree_prep(x: torch.Tensor, conv_state: torch.Tensor, conv_index: torch.Tensor, conv_w: torch.Tensor,
+              num_k_heads: int, num_v_heads: int, head_dim: int):
+    """x [n, conv_dim] bf16, conv_state [conv_dim, KC] bf16, conv_index [n, KC] int32, conv_w [conv_dim, KC] bf16.
+
+    Returns q (l2-normalised, scaled by head_dim^-0.5), k (l2-normalised) [n, H_k, D] and v [n, H, D], bf16."""
+    dev = require_cuda(x, conv_state, conv_index, conv_w)
+    n, cd = x.shape
+    kc = conv_w.shape[1]
+    x = x.to(torch.bfloat16).contiguous()
+    conv_state = conv_state.to(torch.bfloat16).contiguous()
+    conv_w = conv_w.to(torch.bfloat16).contiguous()
+    conv_index = conv_index.to(torch.int32).contiguous()
+    q = torch.empty(n, num_k_heads, head_dim, dtype=torch.bfloat16, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(n, num_v_heads, head_dim, dtype=torch.bfloat16, device=dev)
+    rc = _lib.lib().mfd_tree_prep(x.data_ptr(), conv_state.data_ptr(), conv_index.data_ptr(), conv_w.data_ptr(), n,
+                                  cd, kc, num_k_heads, num_v_heads, head_dim, float(head_dim ** -0.5), q.data_ptr(),
+                                  k.data_ptr(), v.data_ptr(), stream_ptr(dev))
+    check(rc, "mfd_tree_prep")
+    return q, k, v

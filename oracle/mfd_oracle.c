@@ -323,13 +323,12 @@ void oracle_build_trees(const float* lp, const int32_t* ids32, const float* prio
 
 /* ------------------------------------------------------------------ visibility and walk */
 
-/* parents [m] (parents[0] = -1) -> vis [m, m] uint8, row i = ancestors of i and i. */
+/* parents [m] (parents[i] < i; -1 marks a root, as node 0 of a draft tree or any node of a forest hanging off
+ * the committed state) -> vis [m, m] uint8, row i = ancestors of i and i. */
 void oracle_visibility(const int64_t* parents, int64_t m, uint8_t* vis) {
     memset(vis, 0, (size_t)(m * m));
-    if (m == 0) return;
-    vis[0] = 1;
-    for (int64_t i = 1; i < m; ++i) {
-        memcpy(vis + i * m, vis + parents[i] * m, (size_t)i);
+    for (int64_t i = 0; i < m; ++i) {
+        if (parents[i] >= 0 && parents[i] < i) memcpy(vis + i * m, vis + parents[i] * m, (size_t)i);
         vis[i * m + i] = 1;
     }
 }

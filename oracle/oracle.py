@@ -14,6 +14,8 @@ restatement oracle/mfd_oracle.c through ctypes.  Floating-point paths are restat
   tree_gdn           tests/test_gdn_tree_math.py:29-60 (chunk form with ancestor mask, one
                      triangular solve) with the GQA key-head map of hf/tree_gdn_kernel.py:71, 101,
                      per-node states by the commit formula hf/qwen35_tree.py:134-137
+  tree_prep          hf/tree_gdn_kernel.py:27-56 (_tree_prep: windowed conv through parent pointers,
+                     SiLU rounded to bf16, l2norm + q scale); pinned against torch's causal conv1d on chains
 
 Parity pins: tests/golden/ holds fixtures made by tests/golden/make_golden.py from the reference
 itself (its Python builders, compiled C++ builders, walk, mode-attention reference and verify mask);
@@ -312,3 +314,36 @@ def gdn_recurrence(q, k, v, g, beta, s0, parents):
             states[i, h] = s
             o[i, h] = s.T @ q[i, hk]
     return o, states
+
+
+def bf16_round(x) -> np.ndarray:
+    """float32 -> nearest bfloat16 (ties to even), returned as float32."""
+    b = np.ascontiguousarray(np.asarray(x, np.float32)).view(np.uint32).astype(np.uint64)
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def tree_prep(x, conv_state, conv_index, conv_w, num_k_heads, num_v_heads, head_dim, scale):
+    """hf/tree_gdn_kernel.py:27-56 in float32.  x [n, CD], conv_state [CD, KC], conv_index [n, KC] (indices into
+    [conv_state columns ; nodes]), conv_w [CD, KC], all bf16-valued.  Returns q, k [n, HK, D], v [n, H, D] as
+    bf16-valued float32 arrays."""
+    x = np.asarray(x, np.float32)
+    cs = np.asarray(conv_state, np.float32)
+    w = np.asarray(conv_w, np.float32)
+    idx = np.asarray(conv_index, np.int64)
+    n, cd = x.shape
+    kc = w.shape[1]
+    X = np.concatenate([cs.T, x], axis=0)  # [KC + n, CD]: cached inputs then the nodes
+    acc = np.zeros((n, cd), np.float32)
+    for t in range(kc):  # sequential fp32 accumulation over the window, oldest first
+        acc = (acc + X[idx[:, t]] * w[None, :, t]).astype(np.float32)
+    y = bf16_round(acc / (np.float32(1) + np.exp(-acc, dtype=np.float32)))
+    HK, H, D = num_k_heads, num_v_heads, head_dim
+    q = y[:, : HK * D].reshape(n, HK, D)
+    k = y[:, HK * D: 2 * HK * D].reshape(n, HK, D)
+    v = y[:, 2 * HK * D:].reshape(n, H, D)
+
+    def l2n(a):
+        return a / np.sqrt((a * a).sum(-1, keepdims=True, dtype=np.float32) + np.float32(1e-6), dtype=np.float32)
+
+    return bf16_round(l2n(q) * np.float32(scale)), bf16_round(l2n(k)), bf16_round(v)
