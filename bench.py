@@ -1,15 +1,16 @@
 """Verify-step benchmark (tree build + tree verify attention + acceptance), B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests R]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests-per-gpu R]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
+    python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
 
 Workload (synthetic, seeded per global request id so any partition computes the same
-requests): 256 requests per step, each with drafter logits float32 [K=8, L=16, V=151936] (N(0,1), 4 ids per
-(mode, position) boosted by U(4,10)), an exact mixture tree of B=64 nodes, tree-masked GQA verify attention
-(32/8 heads, head_dim 128, prefix U(1024, 8192)), and stochastic acceptance at T=1 over target logits bf16
-[65, V] N(0, 1.5) with seeded uniforms.  Requests are partitioned across ranks (sorted by prefix, dealt
-round-robin); there is no collective on the data path (only the timing max-reduce), so scaling is strong:
-the total work is fixed.  Inputs (~30 GB) are far larger than L2.
+requests): 32 requests per GPU per step (32/64/128/256 requests at 1/2/4/8 GPUs), each with drafter logits
+float32 [K=8, L=16, V=151936] (N(0,1), 4 ids per (mode, position) boosted by U(4,10)), an exact mixture tree of
+B=64 nodes, tree-masked GQA verify attention (32/8 heads, head_dim 128, prefix U(1024, 8192)), and stochastic
+acceptance at T=1 over target logits bf16 [65, V] N(0, 1.5) with seeded uniforms.  Requests are partitioned
+across ranks (sorted by prefix, dealt round-robin); there is no collective on the data path (only the timing
+max-reduce), so scaling is weak: the work per GPU is fixed.  Inputs (~3.8 GB per GPU) are far larger than L2.
 
 Printed by rank 0: one JSON line (metric trees/s, whole job), with
   north_star: BASELINE's headline verify step -- batch 1, greedy, prefix 4096, configs 0 + 1 + acceptance --
@@ -38,7 +39,10 @@ sys.path.insert(0, ROOT)
 K_MODES, L_BLOCK, VOCAB, BUDGET = 8, 16, 151936, 64
 W = BUDGET + 1
 H, HKV, D = 32, 8, 128
-TOTAL_REQUESTS = 256
+REQUESTS_PER_GPU = 32
+# Logits-step DRAM traffic per row (read + write) from an ncu capture of 256 rows x 151936 fp32, k = 64:
+# 155.75 MB read + 5.15 MB written.  Traffic grows with the rows, so a launch of R rows moves R times this.
+TOPK_TRAFFIC_PER_ROW = (155.754496e6 + 5.148672e6) / 256
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -84,8 +88,9 @@ def max_over_ranks(ws, value: float) -> float:
 
 
 def prefix_lengths(total: int, seed: int = 4321):
+    """Prefix length of every request id: U(1024, 8192), the same for a request whatever the job size."""
     g = torch.Generator().manual_seed(seed)
-    return torch.randint(1024, 8193, (total,), generator=g).tolist()
+    return torch.randint(1024, 8193, (max(total, 256),), generator=g).tolist()[:total]
 
 
 def partition(total: int, ws: int, rank: int, prefixes):
@@ -230,12 +235,12 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------ measurements
 
 def time_steps(step: Step, steps: int, warmup: int, ws: int, dev_index: int):
-    for _ in range(warmup):
-        step.run()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(steps)]
-    barrier(ws)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev_index) as clocks:
+    with ClockSampler(dev_index) as clocks:  # sampling spans the warm-up and the timed steps
+        for _ in range(warmup):
+            step.run()
+        barrier(ws)
         start.record()
         for i in range(steps):
             step.run(evs[i])
@@ -279,9 +284,10 @@ def north_star(dev, steps: int, warmup: int):
     }
 
 
-def e2e(dev, reqs, prefixes, steps: int, chunk: int = 16):
-    """The public API end to end: every step copies the requests' inputs from pinned host memory to the device,
-    runs the verify step, and reads the accepted lengths / tokens back."""
+def e2e(dev, reqs, prefixes, steps: int, ws: int, chunk: int = 8):
+    """The public API end to end on every rank: each step copies its requests' inputs from pinned host memory to
+    the device, runs the verify step, and reads the accepted lengths / tokens and the trees back.  Timed on the
+    device (CUDA events), max over ranks; value = requests of all ranks per second."""
     sample = reqs[:chunk]
     batch = Batch(sample, prefixes, dev)
     host = {name: getattr(batch, name).cpu().pin_memory() for name in ("draft", "q", "k", "v", "target", "u")}
@@ -300,16 +306,16 @@ def e2e(dev, reqs, prefixes, steps: int, chunk: int = 16):
         return res
 
     one()
-    torch.cuda.synchronize()
+    barrier(ws)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
         one()
     e.record()
     torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
-    return {"value": round(len(sample) / (ms / 1e3), 3), "unit": "trees/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": out_bytes, "requests_per_step": len(sample), "ms_per_step": round(ms, 3)}
+    ms = max_over_ranks(ws, s.elapsed_time(e) / steps)
+    return {"value": round(len(sample) * ws / (ms / 1e3), 3), "unit": "trees/s", "h2d_bytes_per_step": h2d * ws,
+            "d2h_bytes_per_step": out_bytes * ws, "requests_per_step": len(sample) * ws, "ms_per_step": round(ms, 3)}
 
 
 # ------------------------------------------------------------------------------------------------ CPU reference
@@ -372,7 +378,7 @@ def reference_ext():
 def cpu_baseline(sample_requests: int = 3, temperature: float = 1.0):
     torch.set_num_threads(os.cpu_count() or 1)
     ext, kind = reference_ext()
-    prefixes = prefix_lengths(TOTAL_REQUESTS)
+    prefixes = prefix_lengths(REQUESTS_PER_GPU)
     cpu_reference_request(0, 1024, temperature, ext)  # warm-up
     secs = [cpu_reference_request(r, prefixes[r], temperature, ext) for r in range(sample_requests)]
     per = statistics.mean(secs)
@@ -383,13 +389,109 @@ def cpu_baseline(sample_requests: int = 3, temperature: float = 1.0):
 
 # ------------------------------------------------------------------------------------------------ main
 
+def timed_us(fn, steps: int, warmup: int, flush: torch.Tensor):
+    """Mean device time of fn() in microseconds: warm-up, then each timed call after an L2 flush, bracketed by CUDA
+    events on the current stream (a long device sleep first so host launch overhead is not measured)."""
+    for _ in range(max(warmup, 3)):
+        fn()
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2_000_000)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e) * 1e3)
+    return statistics.mean(times)
+
+
+def config_line(config: int, steps: int, warmup: int):
+    """One BASELINE config's kernels alone (batch 1), against the roofline of that config's algorithmic work."""
+    from mfd_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    pk = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    line = {"config": config, "peak_hbm_gbs": pk["hbm_gbs"], "peak_bf16_tflops": pk["bf16_tflops"],
+            "peak_source": pk["source"]}
+    if config in (0, 1):
+        batch = Batch([0], [4096], dev, temperature=0.0, target_std=1.0, uniform_prefix=4096)
+        step = Step(batch)
+        step.run()
+        if config == 0:
+            def fn():
+                ops.topk_logz(batch.draft.view(-1, VOCAB), BUDGET, ids_dtype=torch.int32,
+                              out=(batch.top, batch.ids, batch.logz))
+                ops.build_trees(batch.top.view(1, K_MODES, L_BLOCK, BUDGET), batch.ids.view(1, K_MODES, L_BLOCK, BUDGET),
+                                None, BUDGET, tree=batch.tree, counts=batch.counts)
+            nbytes, flops = K_MODES * L_BLOCK * VOCAB * 4, 0
+            line["workload"] = "configs[0]: logits step + mixture tree, fp32 [8, 16, 151936], B=64"
+        else:
+            _, _, anc, _ = ops.build_trees(batch.top.view(1, K_MODES, L_BLOCK, BUDGET),
+                                           batch.ids.view(1, K_MODES, L_BLOCK, BUDGET), None, BUDGET)
+            def fn():
+                ops.tree_attention(batch.q, batch.k, batch.v, anc, 4096, D ** -0.5, out=batch.attn_out)
+            nbytes = (W * H * D * 2) * 2 + 2 * HKV * (4096 + W) * D * 2
+            flops = 4 * W * H * (4096 + W) * D
+            line["workload"] = "configs[1]: tree verify attention, 65 queries x 32 heads over 4096 + 65 keys (8 kv heads)"
+    elif config == 2:
+        import numpy as np
+        import torch.nn.functional as F
+
+        n, Hv, Hk = 64, 32, 16
+        g = torch.Generator(device=dev).manual_seed(2)
+        rng = np.random.default_rng(2)
+        parents = [-1] + [int(rng.integers(0, i)) for i in range(1, n)]
+        anc = torch.zeros(n, n, dtype=torch.int8)
+        for i in range(n):
+            if parents[i] >= 0:
+                anc[i] = anc[parents[i]]
+            anc[i, i] = 1
+        anc = anc.to(dev)
+        q = (F.normalize(torch.randn(n, Hk, D, generator=g, device=dev), dim=-1) * D ** -0.5).bfloat16()
+        k = F.normalize(torch.randn(n, Hk, D, generator=g, device=dev), dim=-1).bfloat16()
+        v = torch.randn(n, Hv, D, generator=g, device=dev).bfloat16()
+        beta = torch.sigmoid(torch.randn(n, Hv, generator=g, device=dev))
+        G = anc.float() @ (-F.softplus(torch.randn(n, Hv, generator=g, device=dev)))
+        s0 = torch.randn(Hv, D, D, generator=g, device=dev) * 0.02
+        u = torch.empty(n, Hv, D, device=dev)
+        o = torch.empty_like(u)
+        st = torch.empty(n, Hv, D, D, device=dev)
+        uo_us = timed_us(lambda: ops.tree_gdn(q, k, v, G, beta, s0, anc, out=(u, o, None)), steps, warmup, flush)
+        line["uo_us"] = round(uo_us, 2)
+        line["uo_roofline_us"] = round((2 * n * Hk * D * 2 + n * Hv * D * 2 + Hv * D * D * 4 + 2 * n * Hv * D * 4)
+                                       / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
+
+        def fn():
+            ops.tree_gdn(q, k, v, G, beta, s0, anc, emit_states=True, out=(u, o, st))
+        nbytes = 2 * n * Hk * D * 2 + n * Hv * D * 2 + Hv * D * D * 4 + 2 * n * Hv * D * 4 + st.numel() * 4
+        flops = 0
+        line["workload"] = "configs[2]: tree GDN layer, 64 nodes, 32/16 heads d128, with per-node states"
+    else:
+        raise SystemExit(f"--config {config}: not available")
+    us = timed_us(fn, steps, warmup, flush)
+    line["us"] = round(us, 2)
+    line["algorithmic_bytes"] = nbytes
+    line["hbm_roofline_us"] = round(nbytes / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
+    line["frac_of_hbm_roofline"] = round(line["hbm_roofline_us"] / us, 4)
+    if flops:
+        line["flops"] = flops
+        line["tensor_roofline_us"] = round(flops / (pk["bf16_tflops"] * 1e12) * 1e6, 2)
+        line["frac_of_tensor_roofline"] = round(line["tensor_roofline_us"] / us, 4)
+    line["l2"] = "flushed (256 MB write) before every timed call"
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mfd", choices=["mfd", "reference"])
-    ap.add_argument("--requests", type=int, default=TOTAL_REQUESTS)
+    ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
+    ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -400,20 +502,19 @@ def main():
             return
         torch.set_num_threads(os.cpu_count() or 1)
         ext, kind = reference_ext()
-        prefixes = prefix_lengths(TOTAL_REQUESTS)
-        per_step = 1
+        prefixes = prefix_lengths(REQUESTS_PER_GPU)
         for i in range(args.warmup):
             cpu_reference_request(i, prefixes[i], 1.0, ext)
         t0 = time.perf_counter()
         for i in range(args.steps):
-            cpu_reference_request(i % TOTAL_REQUESTS, prefixes[i % TOTAL_REQUESTS], 1.0, ext)
+            cpu_reference_request(i % REQUESTS_PER_GPU, prefixes[i % REQUESTS_PER_GPU], 1.0, ext)
         secs = (time.perf_counter() - t0) / args.steps
-        value = per_step / secs
+        value = 1.0 / secs
         line = {"impl": "reference", "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
                 "value": round(value, 4), "unit": "trees/s", "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "configs[4] batched verify step, one request per step (CPU)",
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "configs[4] batched verify step, one request per step on the host CPU",
                            "budget": BUDGET, "modes": K_MODES, "block": L_BLOCK, "vocab": VOCAB},
                 "cpu_baseline": {"value": round(value, 4), "unit": "trees/s", "cores": torch.get_num_threads(),
                                  "kind": kind, "sample": "one request of the workload per step"},
@@ -422,46 +523,57 @@ def main():
         print(json.dumps(line))
         return
 
+    if args.config is not None:
+        torch.cuda.set_device(0)
+        print(json.dumps(config_line(args.config, max(args.steps, 10), args.warmup)))
+        return
+
     ws, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local if ws > 1 else 0)
     from mfd_b200 import _lib
 
     _lib.load()
-    prefixes = prefix_lengths(args.requests)
-    reqs = partition(args.requests, ws, rank, prefixes)
+    total = args.requests_per_gpu * ws
+    prefixes = prefix_lengths(total)
+    reqs = partition(total, ws, rank, prefixes)
     batch = Batch(reqs, prefixes, dev)
     step = Step(batch)
     torch.cuda.synchronize()
     total_ms, per_kernel, clocks = time_steps(step, args.steps, args.warmup, ws, dev.index or 0)
     total_ms = max_over_ranks(ws, total_ms)
     ms_per_step = total_ms / args.steps
-    value = args.requests / (ms_per_step / 1e3)
+    value = total / (ms_per_step / 1e3)
 
     pk = peaks()
     # roofline of the dominant kernel: the logits step reads each request's float32 [8, 16, V] logits once
-    logits_bytes = len(reqs) * K_MODES * L_BLOCK * VOCAB * 4
+    rows = len(reqs) * K_MODES * L_BLOCK
+    logits_bytes = rows * VOCAB * 4
     achieved = logits_bytes / (per_kernel["logits_step"] * 1e-6) / 1e9
     line = {
         "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
         "value": round(value, 3), "unit": "trees/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32 logits / bf16 attention", "data": "synthetic",
-        "config": {"workload": "configs[4]: batched verify step, 256 requests split across GPUs, T=1",
-                   "requests": args.requests, "requests_per_gpu": len(reqs), "budget": BUDGET, "modes": K_MODES,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "configs[4]: batched verify step, 32 requests per GPU, T=1",
+                   "requests": total, "requests_per_gpu": len(reqs), "budget": BUDGET, "modes": K_MODES,
                    "block": L_BLOCK, "vocab": VOCAB, "heads": H, "kv_heads": HKV, "head_dim": D,
                    "prefix": "U(1024, 8192)", "l2": "inputs (~117 MB per request) far larger than L2",
+                   "dtypes": "fp32 drafter logits, bf16 q/k/v and target logits, fp32 accumulation",
                    "parallelism": f"requests partitioned over {ws} GPU(s), no collective"},
         "kernels_us_per_step": {k: round(v, 2) for k, v in per_kernel.items()},
         "roofline": {"kernel": "mfd_topk_logz (logits step)", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                     "peak_source": pk["source"], "traffic": None,
+                     "peak_source": pk["source"], "traffic": round(TOPK_TRAFFIC_PER_ROW * rows),
+                     "traffic_source": "ncu capture of 256 rows, scaled by rows",
                      "algorithmic_bytes_per_launch": logits_bytes},
         "clocks": clocks,
         "gpu_launches": Step.LAUNCHES * args.steps,
     }
-    if rank == 0 and not args.no_extras:
-        line["north_star"] = north_star(dev, steps=20, warmup=args.warmup)
-        line["e2e"] = e2e(dev, reqs, prefixes, steps=3)
+    if not args.no_extras:
+        if rank == 0:
+            line["north_star"] = north_star(dev, steps=20, warmup=args.warmup)
+        barrier(ws)
+        line["e2e"] = e2e(dev, reqs, prefixes, steps=3, ws=ws)
         if ws == 1:
             line["cpu_baseline"] = cpu_baseline()
     if ws > 1:
