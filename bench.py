@@ -469,6 +469,31 @@ def config_line(config: int, steps: int, warmup: int):
         nbytes = 2 * n * Hk * D * 2 + n * Hv * D * 2 + Hv * D * D * 4 + 2 * n * Hv * D * 4 + st.numel() * 4
         flops = 0
         line["workload"] = "configs[2]: tree GDN layer, 64 nodes, 32/16 heads d128, with per-node states"
+    elif config == 3:
+        from mfd_b200.mode_attention import mode_block_attention
+
+        Km, bsz, ctx = 8, 16, 4096
+        T = Km * bsz
+        g = torch.Generator(device=dev).manual_seed(3)
+        q = torch.randn(1, H, T, D, generator=g, device=dev).bfloat16()
+        k = (torch.randn(1, HKV, ctx + T, D, generator=g, device=dev) * 0.5).bfloat16()
+        v = (torch.randn(1, HKV, ctx + T, D, generator=g, device=dev) * 0.5).bfloat16()
+        batch = Batch([0], [4096], dev, temperature=0.0, target_std=1.0, uniform_prefix=64)
+        step = Step(batch)
+        step.run()
+        attn_us = timed_us(lambda: mode_block_attention(q, k, v, Km, bsz, D ** -0.5), steps, warmup, flush)
+        attn_flops = 4 * T * H * (ctx + bsz) * D
+        attn_bytes = 2 * (H * T * D * 2) + 2 * HKV * (ctx + T) * D * 2
+        line["mode_attention_us"] = round(attn_us, 2)
+        line["mode_attention_tensor_roofline_us"] = round(attn_flops / (pk["bf16_tflops"] * 1e12) * 1e6, 2)
+        line["mode_attention_hbm_roofline_us"] = round(attn_bytes / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
+
+        def fn():
+            ops.accept(batch.target, batch.tree[:, 0], batch.tree[:, 2], temperature=0.0, max_steps=L_BLOCK - 1,
+                       out_len=L_BLOCK)
+        nbytes, flops = W * VOCAB * 2, 0
+        line["workload"] = ("configs[3]: mode attention (128 queries x 32 heads over 4096 context + own 16-key block) "
+                            "then greedy acceptance over target logits bf16 [65, 151936]; 'us' is the acceptance")
     else:
         raise SystemExit(f"--config {config}: not available")
     us = timed_us(fn, steps, warmup, flush)
