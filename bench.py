@@ -148,9 +148,9 @@ class Batch:
 # ------------------------------------------------------------------------------------------------ the step
 
 class Step:
-    """One verify step over a Batch: 5 kernel launches (logits step, tree build, attention + merge, accept)."""
+    """One verify step over a Batch: 4 kernel launches (logits step, tree build, attention, accept)."""
 
-    LAUNCHES = 5
+    LAUNCHES = 4
 
     def __init__(self, batch: Batch, splits=None):
         from mfd_b200 import ops

@@ -136,22 +136,25 @@ int mfd_verify_inputs(const int64_t* root_tokens, const int64_t* prefix_lens, co
                       int8_t* mask_out, void* stream);
 
 /*
- * Tree-masked GQA verify attention.  q, out [bs, n, H, 128] bf16 (strides in elements, last dim
- * contiguous); k, v [bs, Hkv, S, 128] bf16 holding each request's prefix keys followed by its n tree keys;
- * prefix_lens [bs] int32 on the device (or null: every request uses prefix_len); anc_bits [bs, n, words]
- * ancestor-or-self bitsets (mfd_build_trees).  Row i sees all prefix keys and the tree keys of its
- * ancestors and itself.  Flash-decoding over `splits` key ranges, merged by log-sum-exp.
+ * Tree-masked GQA verify attention on the tcgen05 tensor cores.  q, out [bs, n, H, 128] bf16 (strides in elements,
+ * multiples of 8, last dim contiguous); k, v [bs, Hkv, max_keys, 128] bf16 holding each request's prefix keys
+ * followed by its n tree keys (keys at or past max_keys are never read); prefix_lens [bs] int32 on the device (or
+ * null: every request uses prefix_len); anc_bits [bs, n, words] ancestor-or-self bitsets (mfd_build_trees).  Row i
+ * sees all prefix keys and the tree keys of its ancestors and itself.  The keys are split into `splits` ranges;
+ * the last range to finish merges them by log-sum-exp.  H / Hkv must divide 128.
  * Replaces: the target's SDPA call with the compile_ddtree_tree mask (inference/hf/ddtree.py:352-356,
- *           598-605); SGLang's flashinfer custom-mask prefill (patch:86-142, 558-592).
- * Workspace: mfd_tree_attention_workspace(bs, n, H, splits) bytes.
+ *           598-605); SGLang's flashinfer custom-mask prefill (patch:86-142, 558-592); with a block-diagonal
+ *           visibility, the drafter's mode_block_attention (inference/hf/mode_attention.py:120-150).
+ * Workspace: mfd_tree_attention_workspace(bs, n, H, Hkv, splits) bytes, zeroed before its first use (its ticket
+ * words return to zero after every call).
  */
-size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t splits);
+size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads, int64_t splits);
 int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int64_t sq_h, const void* k, int64_t sk_b,
                        int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
-                       const int32_t* prefix_lens, int64_t prefix_len, const uint64_t* anc_bits, int64_t anc_words,
-                       int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim, float scale,
-                       int64_t splits, void* out, int64_t so_b, int64_t so_n, int64_t so_h, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       int64_t max_keys, const int32_t* prefix_lens, int64_t prefix_len, const uint64_t* anc_bits,
+                       int64_t anc_words, int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads,
+                       int64_t head_dim, float scale, int64_t splits, void* out, int64_t so_b, int64_t so_n,
+                       int64_t so_h, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Tree verification of one gated-delta-rule layer from the committed state S0 (fla layout, o = S^T q):

@@ -1,0 +1,567 @@
+// tree_attention_tc.cu -- tree-masked GQA verify attention on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// softmax(q k^T * scale + mask) v for the tree rows of every request: row i sees every prefix key and, among the
+// tree keys, exactly its ancestors and itself (the additive mask of inference/hf/ddtree.py:352-356, the flashinfer
+// custom mask of sglang-v0.5.22-mfd.patch:1625-1703).  The mask is read from the builder's ancestor bitsets.
+//
+// Rows: the G query heads sharing a KV head are packed as r = node * G + g (260 rows for 65 nodes x 4 heads), so
+// a key tile feeds G x n rows.  One CTA per (request, KV head, key split, 128-row M-tile); the M-tiles of one
+// split are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA producer: Q once, then 64-key K and V tiles into a 4-stage ring (128-byte swizzle, the
+//               canonical UMMA K-major / MN-major layouts; no multicast)
+//   warp 1      MMA issuer: S[i%2] = Q K_i^T (M=128, N=64, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
+//               (M=128, N=128, K=16 x 4, V MN-major), so the scores of tile i are computed while the softmax
+//               works on tile i-1's probabilities
+//   warps 2..9  softmax: the two warps of TMEM lane quarter q each take 32 of a row's 64 key columns (row max
+//               and sum exchanged through shared memory): tcgen05.ld of S, mask (only tiles reaching the tree keys
+//               or the split end), exp2 (half on the FMA pipe), bf16 P into shared memory; lazy O rescale in TMEM
+//               only when a row's running max grows by more than 2^8; epilogue through a shared-memory stage so
+//               every store is coalesced.
+// Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
+// merges all splits and writes bf16 out.  With one split the CTA writes out directly.
+//
+// TMEM: O at columns [0, 128), S[0] at [128, 192), S[1] at [192, 256).  Every mbarrier wait is bounded; when one
+// gives up the CTA records a nonzero status, finishes without waiting further, and still releases its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace mfd {
+namespace tca {
+
+constexpr int D = 128;
+constexpr int kM = 128;        // rows per CTA (one M-tile)
+constexpr int kKt = 64;        // keys per tile
+constexpr int kStages = 4;     // K/V ring depth
+constexpr int kThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2..9 softmax
+constexpr int kTmemCols = 256;
+constexpr int kSCol = 128;     // S[b] at column kSCol + 64 b
+
+constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
+constexpr int kKVBytes = kKt * D * 2;  // 16 KB: [2 d-halves][64 keys][128 B]
+constexpr int kPBytes = kM * kKt * 2;  // 16 KB: [128 rows][128 B]
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kQBytes;
+constexpr int kOffV = kOffK + kStages * kKVBytes;
+constexpr int kOffP = kOffV + kStages * kKVBytes;
+constexpr int kOffX = kOffP + 2 * kPBytes;  // row maxima / sums exchanged by the two halves of a row
+constexpr int kOffBar = kOffX + 2 * kM * 4;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers, TMEM address, flags, 1024-byte alignment slack
+constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
+
+struct Params {
+    __nv_bfloat16* out;  // [bs, n, H, D]
+    int64_t so_b, so_n, so_h;
+    const int32_t* prefix;  // [bs] prefix lengths (device) or null
+    int prefix_const;
+    const uint64_t* anc;  // [bs, n, words]
+    int words;
+    int n, H, Hkv, G;
+    int mtiles;        // M-tiles per (request, KV head) = ceil(n G / 128)
+    float scale_log2;  // scale * log2(e)
+    int splits;
+    float* o_part;          // [splits, bs, Hkv, mtiles * 128, D]
+    float* lse_part;        // [splits, bs, Hkv, mtiles * 128]
+    unsigned int* tickets;  // [bs, Hkv, mtiles], zero between launches
+    int* status;            // sticky: 1 once a bounded wait gave up
+    int bs;
+};
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+// UMMA shared-memory matrix descriptor: start address, leading / stride byte offsets (16-byte units), the sm100
+// version field (bits 46-47 = 1) and the swizzle mode (bits 61-63, 2 = 128-byte).
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, A K-major, B K- or MN-major, M and N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int b_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
+    uint32_t u[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]),
+          "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]),
+          "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(r[0])), "r"(__float_as_uint(r[1])), "r"(__float_as_uint(r[2])),
+        "r"(__float_as_uint(r[3])), "r"(__float_as_uint(r[4])), "r"(__float_as_uint(r[5])),
+        "r"(__float_as_uint(r[6])), "r"(__float_as_uint(r[7])), "r"(__float_as_uint(r[8])),
+        "r"(__float_as_uint(r[9])), "r"(__float_as_uint(r[10])), "r"(__float_as_uint(r[11])),
+        "r"(__float_as_uint(r[12])), "r"(__float_as_uint(r[13])), "r"(__float_as_uint(r[14])),
+        "r"(__float_as_uint(r[15])), "r"(__float_as_uint(r[16])), "r"(__float_as_uint(r[17])),
+        "r"(__float_as_uint(r[18])), "r"(__float_as_uint(r[19])), "r"(__float_as_uint(r[20])),
+        "r"(__float_as_uint(r[21])), "r"(__float_as_uint(r[22])), "r"(__float_as_uint(r[23])),
+        "r"(__float_as_uint(r[24])), "r"(__float_as_uint(r[25])), "r"(__float_as_uint(r[26])),
+        "r"(__float_as_uint(r[27])), "r"(__float_as_uint(r[28])), "r"(__float_as_uint(r[29])),
+        "r"(__float_as_uint(r[30])), "r"(__float_as_uint(r[31]))
+        : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+// named barriers: 1 = the 256 softmax threads, 2 + q = the two warps of TMEM lane quarter q
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void pair_sync(int quarter) { asm volatile("bar.sync %0, 64;" ::"r"(2 + quarter) : "memory"); }
+
+// 2^x on the FMA / integer pipes, for half of the probabilities so that the MUFU exp2 unit (16 results per clock
+// per SM) is not the softmax's only path: x = j + f with j = round(x) (1.5 * 2^23 rounding trick), f in [-0.5, 0.5],
+// 2^f by its Taylor series in f ln 2 to degree 4 (relative error below 5e-5, far under bf16's 2^-9), and j added
+// to the exponent field.  x is clamped to [-126, 126]; the callers' arguments are at most 8, and anything below
+// 2^-126 is a zero weight next to the row maximum's 1.
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fminf(fmaxf(x, -126.f), 126.f);
+    const float t = x + 12582912.f;
+    const float r = t - 12582912.f;
+    const float f = x - r;
+    const int j = __float_as_int(t) - 0x4B400000;
+    float q = 9.6181291076e-3f;        // ln2^4 / 24
+    q = fmaf(q, f, 5.5504108665e-2f);  // ln2^3 / 6
+    q = fmaf(q, f, 2.4022650696e-1f);  // ln2^2 / 2
+    q = fmaf(q, f, 6.9314718056e-1f);  // ln2
+    q = fmaf(q, f, 1.f);
+    return __int_as_float(__float_as_int(q) + (j << 23));
+}
+
+// barrier slots
+enum {
+    kBarQ = 0,
+    kBarKVFull = 1,                      // + stage
+    kBarKVEmpty = kBarKVFull + kStages,  // + stage
+    kBarSFull = kBarKVEmpty + kStages,   // + buffer
+    kBarSFree = kBarSFull + 2,           // + buffer
+    kBarPFull = kBarSFree + 2,           // + buffer
+    kBarPV = kBarPFull + 2,
+    kNumBars = kBarPV + 1
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const Params p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_addr(smem);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8 * kNumBars);
+    int* shared_flag = reinterpret_cast<int*>(smem + kOffBar + 8 * kNumBars + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int split = blockIdx.x / p.mtiles, mtile = blockIdx.x % p.mtiles;
+    const int hk = blockIdx.y, b = blockIdx.z;
+    const int nrows = p.n * p.G;
+    const int row0 = mtile * kM;
+    const int prefix = p.prefix ? p.prefix[b] : p.prefix_const;
+    const int total = prefix + p.n;
+    int chunk = (total + p.splits - 1) / p.splits;
+    chunk = (chunk + kKt - 1) / kKt * kKt;
+    const int k_lo = split * chunk;
+    const int k_hi = min(total, k_lo + chunk);
+    const int ntiles = k_hi > k_lo ? (k_hi - k_lo + kKt - 1) / kKt : 0;
+
+    // barriers and the first loads before anything else, so the TMA round trip overlaps the TMEM allocation
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarSFree && i < kBarPV) ? 8u : 1u);
+        *shared_flag = 0;
+        mbar_fence_init();
+    }
+    auto load_kv = [&](int i) {
+        const int st = i % kStages;
+        const int key0 = k_lo + i * kKt;
+        mbar_expect_tx(&bars[kBarKVFull + st], 2 * kKVBytes);
+        for (int h = 0; h < 2; ++h) {
+            tma_load_4d(sbase + kOffK + st * kKVBytes + h * (kKVBytes / 2), &tmk, &bars[kBarKVFull + st], h * 64,
+                        key0, hk, b);
+            tma_load_4d(sbase + kOffV + st * kKVBytes + h * (kKVBytes / 2), &tmv, &bars[kBarKVFull + st], h * 64,
+                        key0, hk, b);
+        }
+    };
+    if (threadIdx.x == 0 && ntiles > 0) {  // (a split past the keys loads nothing: every issued copy is waited for)
+        const int nodes_per_tile = kM / p.G;
+        mbar_expect_tx(&bars[kBarQ], kQBytes);
+        for (int h = 0; h < 2; ++h)
+            tma_load_4d(sbase + kOffQ + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G, mtile * nodes_per_tile,
+                        b);
+        for (int i = 0; i < min(kStages, ntiles); ++i) load_kv(i);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            for (int i = kStages; i < ntiles && ok; ++i) {
+                ok &= mbar_wait(&bars[kBarKVEmpty + i % kStages], ((i / kStages) - 1) & 1, kTries);
+                load_kv(i);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t kIdescS = idesc_bf16(kM, kKt, 0);
+            constexpr uint32_t kIdescO = idesc_bf16(kM, D, 1);
+            auto issue_pv = [&](int j) {
+                const int bj = j & 1, stj = j % kStages;
+                ok &= mbar_wait(&bars[kBarPFull + bj], (j >> 1) & 1, kTries);
+                tc_fence_after();
+                const uint32_t paddr = sbase + kOffP + bj * kPBytes;
+                const uint32_t vaddr = sbase + kOffV + stj * kKVBytes;
+#pragma unroll
+                for (int ks = 0; ks < kKt / 16; ++ks)
+                    umma(tmem, sdesc(paddr + ks * 32, 16, 1024), sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+                umma_commit(&bars[kBarPV]);
+                umma_commit(&bars[kBarKVEmpty + stj]);
+            };
+            if (ntiles > 0) ok &= mbar_wait(&bars[kBarQ], 0, kTries);
+            for (int i = 0; i < ntiles && ok; ++i) {
+                const int st = i % kStages, bi = i & 1;
+                ok &= mbar_wait(&bars[kBarKVFull + st], (i / kStages) & 1, kTries);
+                if (i >= 2) ok &= mbar_wait(&bars[kBarSFree + bi], ((i - 2) >> 1) & 1, kTries);
+                tc_fence_after();
+                const uint32_t kaddr = sbase + kOffK + st * kKVBytes;
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t qoff = (uint32_t)((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
+                    const uint32_t koff = (uint32_t)((ks >> 2) * (kKVBytes / 2) + (ks & 3) * 32);
+                    umma(tmem + kSCol + bi * kKt, sdesc(sbase + kOffQ + qoff, 16, 1024), sdesc(kaddr + koff, 16, 1024),
+                         kIdescS, ks > 0);
+                }
+                umma_commit(&bars[kBarSFull + bi]);
+                if (i >= 1) issue_pv(i - 1);
+            }
+            if (ntiles > 0 && ok) issue_pv(ntiles - 1);
+        }
+    } else {
+        // ---------------------------------------------------------------- softmax warps
+        // warp w (2..9): TMEM lane quarter w % 4, column half (w - 2) / 4; the two warps of a quarter exchange
+        // their row maxima (and at the end their row sums) through shared memory
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
+        const int r = row0 + rt;             // packed row
+        const bool live = r < nrows;
+        const int node = live ? r / p.G : 0;
+        const uint64_t* anc_row = p.anc + ((size_t)b * p.n + node) * p.words;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [2 halves][128 rows]
+        unsigned char* prow0 = smem + kOffP + (rt >> 3) * 1024 + (rt & 7) * 128;
+        const int pswz = rt & 7;
+        const int c_lo = half * 32;  // this warp's 32 of the tile's 64 key columns
+        const float sc = p.scale_log2;
+        float m_run = -INFINITY, l_run = 0.f;
+        for (int i = 0; i < ntiles; ++i) {
+            const int bi = i & 1;
+            const int key0 = k_lo + i * kKt;
+            ok &= mbar_wait(&bars[kBarSFull + bi], (i >> 1) & 1, kTries);
+            tc_fence_after();
+            float s[32];
+            tmem_ld32(tmem + lane_off + kSCol + bi * kKt + c_lo, s);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[kBarSFree + bi]);
+            float mx;
+            const bool fast = key0 + kKt <= prefix && key0 + kKt <= k_hi;
+            if (fast) {
+                // prefix keys only, all visible: no mask (padding rows compute finite values that are never stored)
+                mx = s[0];
+#pragma unroll
+                for (int j = 1; j < 32; ++j) mx = fmaxf(mx, s[j]);
+                mx *= sc;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s[j] *= sc;
+            } else {
+                mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int key = key0 + c_lo + j;
+                    bool vis;
+                    if (key < prefix) {
+                        vis = key < k_hi;
+                    } else if (key < k_hi) {
+                        const int tj = key - prefix;
+                        vis = (__ldg(anc_row + (tj >> 6)) >> (tj & 63)) & 1ull;
+                    } else {
+                        vis = false;
+                    }
+                    s[j] = vis ? s[j] * sc : -INFINITY;
+                    mx = fmaxf(mx, s[j]);
+                }
+            }
+            // the row's max over both halves
+            xmax[half * kM + rt] = mx;
+            pair_sync(quarter);
+            mx = fmaxf(mx, xmax[(half ^ 1) * kM + rt]);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (mx > m_run + 8.f) {  // lazy: keep the running max unless the tile's exceeds it by more than 2^8
+                if (m_run != -INFINITY) {
+                    alpha = fast_exp2(m_run - mx);
+                    rescale = true;
+                }
+                m_run = mx;
+            }
+            const float mref = m_run == -INFINITY ? 0.f : m_run;  // nothing visible yet: every p is 0
+            float rs = 0.f;
+            uint32_t pk[16];
+            if (fast) {  // no -inf scores: half of the exponentials on the FMA pipe
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float p0 = fast_exp2(s[j] - mref);
+                    const float p1 = exp2_fma(s[j + 1] - mref);
+                    rs += p0 + p1;
+                    pk[j >> 1] = pack_bf16(p0, p1);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float p0 = fast_exp2(s[j] - mref);
+                    const float p1 = fast_exp2(s[j + 1] - mref);
+                    rs += p0 + p1;
+                    pk[j >> 1] = pack_bf16(p0, p1);
+                }
+            }
+            l_run = l_run * alpha + rs;
+            // P V of tile i-1 complete: O is stable for a rescale and P[bi] (read by tile i-2) is free
+            if (i >= 1) {
+                ok &= mbar_wait(&bars[kBarPV], (i - 1) & 1, kTries);
+                tc_fence_after();
+            }
+            if (__any_sync(MFD_FULL_MASK, rescale)) {  // this half rescales O columns [64 half, 64 half + 64)
+                for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                    float o[32];
+                    tmem_ld32(tmem + lane_off + c0, o);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] *= alpha;
+                    tmem_st32(tmem + lane_off + c0, o);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            unsigned char* prow = prow0 + bi * kPBytes;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(prow + (((half * 4 + c) ^ pswz) << 4)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
+            if (!__all_sync(MFD_FULL_MASK, ok)) break;
+        }
+        if (ntiles > 0 && ok) {
+            ok &= mbar_wait(&bars[kBarPV], (ntiles - 1) & 1, kTries);
+            tc_fence_after();
+        }
+        // ---- epilogue: the row sum over both halves, then this half's 64 columns of O / l
+        pair_sync(quarter);  // both halves are past their last use of xmax
+        xmax[half * kM + rt] = l_run;
+        pair_sync(quarter);
+        const float l_row = l_run + xmax[(half ^ 1) * kM + rt];
+        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
+        const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
+        // staging of bf16 rows for coalesced stores: the P buffers are free once the last P V completed
+        unsigned char* stage = smem + kOffP;  // [128 rows][256 B]
+        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+            float o[32];
+            if (ntiles > 0) {
+                tmem_ld32(tmem + lane_off + c0, o);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = 0.f;
+            }
+            if (p.splits == 1) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8)
+                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c0 + j) * 2) =
+                        make_uint4(pack_bf16(o[j] * inv, o[j + 1] * inv), pack_bf16(o[j + 2] * inv, o[j + 3] * inv),
+                                   pack_bf16(o[j + 4] * inv, o[j + 5] * inv), pack_bf16(o[j + 6] * inv, o[j + 7] * inv));
+            } else {
+                // partials, chunk-major: float4 chunk c of row rt at [split][unit][c][rt] (a warp stores 512 B)
+                float4* dst = reinterpret_cast<float4*>(p.o_part) + ((size_t)split * units + unit) * (32 * kM);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    dst[((c0 + j) >> 2) * kM + rt] = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+            }
+        }
+        if (p.splits > 1) {
+            if (half == 0) p.lse_part[((size_t)split * units + unit) * kM + rt] =
+                               l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
+            // the last split of this (request, KV head, M-tile) merges all of them
+            __threadfence();
+            softmax_sync();
+            if (threadIdx.x == 64) {
+                unsigned int* tk = p.tickets + unit;
+                const unsigned int t = atomicAdd(tk, 1u);
+                const int last = t == (unsigned int)(p.splits - 1);
+                if (last) *tk = 0u;  // ready for the next launch
+                *shared_flag = last;
+            }
+            softmax_sync();
+            if (*shared_flag) {
+                __threadfence();
+                float m = -INFINITY;
+                for (int sp = 0; sp < p.splits; ++sp) m = fmaxf(m, __ldcg(p.lse_part + ((size_t)sp * units + unit) * kM + rt));
+                float acc[16][4];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+                float wsum = 0.f;
+                if (m != -INFINITY) {
+                    for (int sp = 0; sp < p.splits; ++sp) {
+                        const float l = __ldcg(p.lse_part + ((size_t)sp * units + unit) * kM + rt);
+                        if (l == -INFINITY) continue;
+                        const float w = fast_exp2(l - m);
+                        wsum += w;
+                        const float4* src = reinterpret_cast<const float4*>(p.o_part) + ((size_t)sp * units + unit) * (32 * kM);
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            const float4 v = __ldcg(src + (half * 16 + c) * kM + rt);
+                            acc[c][0] += w * v.x;
+                            acc[c][1] += w * v.y;
+                            acc[c][2] += w * v.z;
+                            acc[c][3] += w * v.w;
+                        }
+                    }
+                }
+                const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+                for (int c = 0; c < 16; c += 2)
+                    *reinterpret_cast<uint4*>(stage + rt * 256 + (half * 64 + c * 4) * 2) =
+                        make_uint4(pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
+                                   pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
+                                   pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+            }
+        }
+        // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
+        softmax_sync();
+        if (p.splits == 1 || *shared_flag) {
+            const int ts = threadIdx.x - 64;  // 0..255
+            for (int e = ts; e < kM * 16; e += 256) {
+                const int rr = e >> 4, c = e & 15;
+                const int pr = row0 + rr;
+                if (pr >= nrows) continue;
+                __nv_bfloat16* orow = p.out + (size_t)b * p.so_b + (size_t)(pr / p.G) * p.so_n +
+                                      (size_t)(hk * p.G + pr % p.G) * p.so_h;
+                *reinterpret_cast<uint4*>(orow + c * 8) = *reinterpret_cast<const uint4*>(stage + rr * 256 + c * 16);
+            }
+        }
+    }
+    if (!ok && p.status) atomicExch(p.status, 1);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// ------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+    }
+    return fn;
+}
+
+// 4-D bf16 map: dims (x = head dim, d1, d2, d3), element strides of d1..d3, box (64, b1, b2, 1), 128-byte
+// swizzle; boxes reaching past the dims read zeros
+static bool make_map(CUtensorMap* m, const void* base, uint64_t d1, uint64_t d2, uint64_t d3, int64_t s1, int64_t s2,
+                     int64_t s3, uint32_t b1, uint32_t b2) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)D, d1, d2, d3};
+    const cuuint64_t strides[3] = {(cuuint64_t)s1 * 2, (cuuint64_t)s2 * 2, (cuuint64_t)s3 * 2};
+    const cuuint32_t box[4] = {64, b1, b2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct Shape {
+    const void* q;
+    int64_t sq_b, sq_n, sq_h;
+    const void* k;
+    int64_t sk_b, sk_h, sk_s;
+    const void* v;
+    int64_t sv_b, sv_h, sv_s;
+    int64_t max_keys;
+};
+
+int launch(const Shape& sh, const Params& p, cudaStream_t stream) {
+    CUtensorMap tq, tk, tv;
+    const uint32_t nodes_per_tile = (uint32_t)(kM / p.G);
+    if (!make_map(&tq, sh.q, (uint64_t)p.H, (uint64_t)p.n, (uint64_t)p.bs, sh.sq_h, sh.sq_n, sh.sq_b, (uint32_t)p.G,
+                  nodes_per_tile) ||
+        !make_map(&tk, sh.k, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sk_s, sh.sk_h, sh.sk_b, kKt,
+                  1) ||
+        !make_map(&tv, sh.v, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sv_s, sh.sv_h, sh.sv_b, kKt,
+                  1)) {
+        set_error("mfd_tree_attention: could not encode the TMA tensor maps");
+        return MFD_ERR_CUDA;
+    }
+    cudaError_t e = cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) {
+        set_error("mfd_tree_attention: %s", cudaGetErrorString(e));
+        return MFD_ERR_CUDA;
+    }
+    dim3 grid((unsigned)(p.splits * p.mtiles), (unsigned)p.Hkv, (unsigned)p.bs);
+    tree_attn_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
+    MFD_CHECK_LAUNCH("mfd_tree_attention");
+    return MFD_OK;
+}
+
+}  // namespace tca
+}  // namespace mfd

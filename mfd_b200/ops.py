@@ -205,11 +205,14 @@ def verify_inputs(root_tokens, prefix_lens, tokens, depths, parents, mask_offset
 # ----------------------------------------------------------------------------------------------- attention
 
 def default_splits(bs: int, n: int, num_heads: int, num_kv_heads: int, keys: int) -> int:
+    """Key splits of the attention: at most one wave of CTAs (one CTA per SM), each split at least 4 tiles of 64
+    keys (shorter splits would spend more on their partial (o, lse) records than on keys)."""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    row_blocks = (n * (num_heads // num_kv_heads) + 63) // 64
-    base = bs * num_kv_heads * row_blocks
-    want = max(1, (2 * sms + base - 1) // base)
-    return int(max(1, min(want, (keys + 63) // 64)))
+    mtiles = (n * (num_heads // num_kv_heads) + 127) // 128
+    units = bs * num_kv_heads * mtiles
+    want = max(1, sms // units)
+    max_splits = max(1, (keys + 255) // 256)
+    return int(min(want, max_splits))
 
 
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch.Tensor, prefix_lens,
@@ -234,12 +237,12 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch
     if splits is None:
         splits = default_splits(bs, n, H, Hkv, max_keys)
     L = _lib.lib()
-    ws = Workspace.get(dev, "attn", L.mfd_tree_attention_workspace(bs, n, H, splits))
+    ws = Workspace.get(dev, "attn", L.mfd_tree_attention_workspace(bs, n, H, Hkv, splits))
     rc = L.mfd_tree_attention(q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(), k.stride(0),
                               k.stride(1), k.stride(2), v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
-                              ptr(pl_t), pl_c, anc.data_ptr(), anc.shape[-1], bs, n, H, Hkv, D, float(scale), splits,
-                              out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), ws.data_ptr(), ws.numel(),
-                              stream_ptr(dev))
+                              k.shape[2], ptr(pl_t), pl_c, anc.data_ptr(), anc.shape[-1], bs, n, H, Hkv, D,
+                              float(scale), splits, out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+                              ws.data_ptr(), ws.numel(), stream_ptr(dev))
     check(rc, "mfd_tree_attention")
     return out
 
