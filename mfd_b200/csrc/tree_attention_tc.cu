@@ -16,7 +16,7 @@
 //               works on tile i-1's probabilities
 //   warps 2..9  softmax: the two warps of TMEM lane quarter q each take 32 of a row's 64 key columns (row max
 //               and sum exchanged through shared memory): tcgen05.ld of S, mask (only tiles reaching the tree keys
-//               or the split end), exp2 (half on the FMA pipe), bf16 P into shared memory; lazy O rescale in TMEM
+//               or the split end), exp2, bf16 P written back over S in TMEM; lazy O rescale in TMEM
 //               only when a row's running max grows by more than 2^8; epilogue through a shared-memory stage so
 //               every store is coalesced.
 // Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
@@ -34,20 +34,18 @@ namespace tca {
 
 constexpr int D = 128;
 constexpr int kM = 128;        // rows per CTA (one M-tile)
-constexpr int kKt = 64;        // keys per tile
-constexpr int kStages = 4;     // K/V ring depth
+constexpr int kKt = 128;       // keys per tile
+constexpr int kStages = 3;     // K/V ring depth
 constexpr int kThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2..9 softmax
-constexpr int kTmemCols = 256;
-constexpr int kSCol = 128;     // S[b] at column kSCol + 64 b
+constexpr int kTmemCols = 512;
+constexpr int kSCol = 128;     // S[b] at column kSCol + 128 b; P[b] (bf16 pairs) over its first 64 columns
 
 constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
-constexpr int kKVBytes = kKt * D * 2;  // 16 KB: [2 d-halves][64 keys][128 B]
-constexpr int kPBytes = kM * kKt * 2;  // 16 KB: [128 rows][128 B]
+constexpr int kKVBytes = kKt * D * 2;  // 32 KB: [2 d-halves][128 keys][128 B]
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
-constexpr int kOffP = kOffV + kStages * kKVBytes;
-constexpr int kOffX = kOffP + 2 * kPBytes;  // row maxima / sums exchanged by the two halves of a row
+constexpr int kOffX = kOffV + kStages * kKVBytes;  // row maxima / sums exchanged by the two halves of a row
 constexpr int kOffBar = kOffX + 2 * kM * 4;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers, TMEM address, flags, 1024-byte alignment slack
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
@@ -99,6 +97,23 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+// A from tensor memory (M rows = lanes, K elements as bf16 pairs along the columns), B from shared memory
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                  : "memory");
@@ -144,24 +159,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void pair_sync(int quarter) { asm volatile("bar.sync %0, 64;" ::"r"(2 + quarter) : "memory"); }
 
-// 2^x on the FMA / integer pipes, for half of the probabilities so that the MUFU exp2 unit (16 results per clock
-// per SM) is not the softmax's only path: x = j + f with j = round(x) (1.5 * 2^23 rounding trick), f in [-0.5, 0.5],
-// 2^f by its Taylor series in f ln 2 to degree 4 (relative error below 5e-5, far under bf16's 2^-9), and j added
-// to the exponent field.  x is clamped to [-126, 126]; the callers' arguments are at most 8, and anything below
-// 2^-126 is a zero weight next to the row maximum's 1.
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fminf(fmaxf(x, -126.f), 126.f);
-    const float t = x + 12582912.f;
-    const float r = t - 12582912.f;
-    const float f = x - r;
-    const int j = __float_as_int(t) - 0x4B400000;
-    float q = 9.6181291076e-3f;        // ln2^4 / 24
-    q = fmaf(q, f, 5.5504108665e-2f);  // ln2^3 / 6
-    q = fmaf(q, f, 2.4022650696e-1f);  // ln2^2 / 2
-    q = fmaf(q, f, 6.9314718056e-1f);  // ln2
-    q = fmaf(q, f, 1.f);
-    return __int_as_float(__float_as_int(q) + (j << 23));
-}
 
 // barrier slots
 enum {
@@ -169,10 +166,9 @@ enum {
     kBarKVFull = 1,                      // + stage
     kBarKVEmpty = kBarKVFull + kStages,  // + stage
     kBarSFull = kBarKVEmpty + kStages,   // + buffer
-    kBarSFree = kBarSFull + 2,           // + buffer
-    kBarPFull = kBarSFree + 2,           // + buffer
-    kBarPV = kBarPFull + 2,
-    kNumBars = kBarPV + 1
+    kBarPFull = kBarSFull + 2,           // + buffer (P written into S[b]; also frees S[b] for tile + 2)
+    kBarPV = kBarPFull + 2,              // + buffer: P V of tile j completes kBarPV + j % 2
+    kNumBars = kBarPV + 2
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -200,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // barriers and the first loads before anything else, so the TMA round trip overlaps the TMEM allocation
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarSFree && i < kBarPV) ? 8u : 1u);
+        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarPFull && i < kBarPV) ? 8u : 1u);
         *shared_flag = 0;
         mbar_fence_init();
     }
@@ -251,20 +247,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int bj = j & 1, stj = j % kStages;
                 ok &= mbar_wait(&bars[kBarPFull + bj], (j >> 1) & 1, kTries);
                 tc_fence_after();
-                const uint32_t paddr = sbase + kOffP + bj * kPBytes;
                 const uint32_t vaddr = sbase + kOffV + stj * kKVBytes;
 #pragma unroll
-                for (int ks = 0; ks < kKt / 16; ++ks)
-                    umma(tmem, sdesc(paddr + ks * 32, 16, 1024), sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO,
-                         (j > 0 || ks > 0) ? 1u : 0u);
-                umma_commit(&bars[kBarPV]);
+                for (int ks = 0; ks < kKt / 16; ++ks)  // P: 16 keys = 8 columns of bf16 pairs per step
+                    umma_ts(tmem, tmem + kSCol + bj * kKt + ks * 8, sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024),
+                            kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                umma_commit(&bars[kBarPV + bj]);
                 umma_commit(&bars[kBarKVEmpty + stj]);
             };
             if (ntiles > 0) ok &= mbar_wait(&bars[kBarQ], 0, kTries);
             for (int i = 0; i < ntiles && ok; ++i) {
                 const int st = i % kStages, bi = i & 1;
+                // S[bi] last held P(i-2), which the P V issued in the previous iteration consumed (tensor-core
+                // operations of this thread execute in order)
                 ok &= mbar_wait(&bars[kBarKVFull + st], (i / kStages) & 1, kTries);
-                if (i >= 2) ok &= mbar_wait(&bars[kBarSFree + bi], ((i - 2) >> 1) & 1, kTries);
                 tc_fence_after();
                 const uint32_t kaddr = sbase + kOffK + st * kKVBytes;
 #pragma unroll
@@ -281,8 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------------- softmax warps
-        // warp w (2..9): TMEM lane quarter w % 4, column half (w - 2) / 4; the two warps of a quarter exchange
-        // their row maxima (and at the end their row sums) through shared memory
+        // warp w (2..9): TMEM lane quarter w % 4, key half (w - 2) / 4 of each 128-key tile; the two warps of a
+        // quarter exchange their row maxima (and at the end their row sums) through shared memory
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
@@ -292,50 +288,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t* anc_row = p.anc + ((size_t)b * p.n + node) * p.words;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [2 halves][128 rows]
-        unsigned char* prow0 = smem + kOffP + (rt >> 3) * 1024 + (rt & 7) * 128;
-        const int pswz = rt & 7;
-        const int c_lo = half * 32;  // this warp's 32 of the tile's 64 key columns
+        const int c_lo = half * 64;  // this warp's 64 of the tile's 128 key columns
         const float sc = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
         for (int i = 0; i < ntiles; ++i) {
             const int bi = i & 1;
             const int key0 = k_lo + i * kKt;
+            const uint32_t s_tm = tmem + lane_off + kSCol + bi * kKt;
             ok &= mbar_wait(&bars[kBarSFull + bi], (i >> 1) & 1, kTries);
             tc_fence_after();
-            float s[32];
-            tmem_ld32(tmem + lane_off + kSCol + bi * kKt + c_lo, s);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[kBarSFree + bi]);
+            float s[64];
+            {
+                float t0[32], t1[32];
+                tmem_ld32(s_tm + c_lo, t0);
+                tmem_ld32(s_tm + c_lo + 32, t1);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    s[j] = t0[j];
+                    s[32 + j] = t1[j];
+                }
+            }
             float mx;
             const bool fast = key0 + kKt <= prefix && key0 + kKt <= k_hi;
             if (fast) {
                 // prefix keys only, all visible: no mask (padding rows compute finite values that are never stored)
                 mx = s[0];
 #pragma unroll
-                for (int j = 1; j < 32; ++j) mx = fmaxf(mx, s[j]);
+                for (int j = 1; j < 64; ++j) mx = fmaxf(mx, s[j]);
                 mx *= sc;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) s[j] *= sc;
+                for (int j = 0; j < 64; ++j) s[j] *= sc;
             } else {
+                // visibility of this thread's 64 keys as one bitmask: prefix keys, then the row's ancestor bits
+                // for the tree keys (two bitset words funnel-shifted into place), all cut at the split end
+                const int kb = key0 + c_lo;           // first key of this half
+                const int t0 = kb - prefix;           // its tree index (negative: prefix keys come first)
+                uint64_t vis;
+                if (t0 <= -64) {
+                    vis = ~0ull;
+                } else {
+                    const int w = t0 >> 6;            // floor division: word holding tree index t0 (t0 >= -63)
+                    const int sh = t0 & 63;
+                    const uint64_t lo = (w >= 0 && w < p.words) ? __ldg(anc_row + w) : 0ull;
+                    const uint64_t hi = (w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull;
+                    uint64_t tree = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;  // bit j: tree index t0 + j
+                    if (t0 < 0) {  // the first -t0 keys are prefix keys
+                        const int np = -t0;
+                        tree = ((w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull) << np;
+                        vis = tree | ((1ull << np) - 1ull);
+                    } else {
+                        vis = tree;
+                    }
+                }
+                const int live_keys = k_hi - kb;      // keys of this half before the split end
+                if (live_keys < 64) vis &= live_keys <= 0 ? 0ull : ((1ull << live_keys) - 1ull);
                 mx = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int key = key0 + c_lo + j;
-                    bool vis;
-                    if (key < prefix) {
-                        vis = key < k_hi;
-                    } else if (key < k_hi) {
-                        const int tj = key - prefix;
-                        vis = (__ldg(anc_row + (tj >> 6)) >> (tj & 63)) & 1ull;
-                    } else {
-                        vis = false;
-                    }
-                    s[j] = vis ? s[j] * sc : -INFINITY;
+                for (int j = 0; j < 64; ++j) {
+                    s[j] = ((vis >> j) & 1ull) ? s[j] * sc : -INFINITY;
                     mx = fmaxf(mx, s[j]);
                 }
             }
-            // the row's max over both halves
+            // the row's max over both halves (both halves have finished reading S[bi] after this barrier, so P
+            // may overwrite it)
             xmax[half * kM + rt] = mx;
             pair_sync(quarter);
             mx = fmaxf(mx, xmax[(half ^ 1) * kM + rt]);
@@ -350,31 +365,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float mref = m_run == -INFINITY ? 0.f : m_run;  // nothing visible yet: every p is 0
             float rs = 0.f;
-            uint32_t pk[16];
-            if (fast) {  // no -inf scores: half of the exponentials on the FMA pipe
+            uint32_t pk[32];
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const float p0 = fast_exp2(s[j] - mref);
-                    const float p1 = exp2_fma(s[j + 1] - mref);
-                    rs += p0 + p1;
-                    pk[j >> 1] = pack_bf16(p0, p1);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const float p0 = fast_exp2(s[j] - mref);
-                    const float p1 = fast_exp2(s[j + 1] - mref);
-                    rs += p0 + p1;
-                    pk[j >> 1] = pack_bf16(p0, p1);
-                }
+            for (int j = 0; j < 64; j += 2) {
+                const float p0 = fast_exp2(s[j] - mref);
+                const float p1 = fast_exp2(s[j + 1] - mref);
+                rs += p0 + p1;
+                pk[j >> 1] = pack_bf16(p0, p1);
             }
             l_run = l_run * alpha + rs;
-            // P V of tile i-1 complete: O is stable for a rescale and P[bi] (read by tile i-2) is free
-            if (i >= 1) {
-                ok &= mbar_wait(&bars[kBarPV], (i - 1) & 1, kTries);
-                tc_fence_after();
-            }
-            if (__any_sync(MFD_FULL_MASK, rescale)) {  // this half rescales O columns [64 half, 64 half + 64)
+            const bool any_rescale = __any_sync(MFD_FULL_MASK, rescale);
+            if (any_rescale) {  // O must hold the P V of tile i-1; this half rescales O columns [64 half, +64)
+                if (i >= 1) {
+                    ok &= mbar_wait(&bars[kBarPV + (bi ^ 1)], ((i - 1) >> 1) & 1, kTries);
+                    tc_fence_after();
+                }
                 for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
                     float o[32];
                     tmem_ld32(tmem + lane_off + c0, o);
@@ -382,21 +387,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j) o[j] *= alpha;
                     tmem_st32(tmem + lane_off + c0, o);
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
-            unsigned char* prow = prow0 + bi * kPBytes;
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                *reinterpret_cast<uint4*>(prow + (((half * 4 + c) ^ pswz) << 4)) =
-                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            // P(i) as bf16 pairs over the first 64 columns of S[bi]: this half's 64 keys = 32 columns
+            tmem_st32u(s_tm + half * 32, pk);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
             if (!__all_sync(MFD_FULL_MASK, ok)) break;
         }
-        if (ntiles > 0 && ok) {
-            ok &= mbar_wait(&bars[kBarPV], (ntiles - 1) & 1, kTries);
+        if (ntiles > 0 && ok) {  // the last P V (every earlier one completed before it)
+            ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
             tc_fence_after();
         }
         // ---- epilogue: the row sum over both halves, then this half's 64 columns of O / l
@@ -407,8 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
         const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
-        // staging of bf16 rows for coalesced stores: the P buffers are free once the last P V completed
-        unsigned char* stage = smem + kOffP;  // [128 rows][256 B]
+        // staging of bf16 rows for coalesced stores: K stage 0 is free once the last P V completed
+        unsigned char* stage = smem + kOffK;  // [128 rows][256 B]
         for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
             float o[32];
             if (ntiles > 0) {
