@@ -66,7 +66,8 @@ def dist_setup(n_gpus: int):
         import datetime
 
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        # a short timeout: a rank that fails ends the others' next collective with an error instead of a hang
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
@@ -82,7 +83,8 @@ def barrier(ws):
 def max_over_ranks(ws, value: float) -> float:
     if ws == 1:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dev = "cuda" if torch.distributed.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
 
@@ -94,6 +96,8 @@ def prefix_lengths(total: int, seed: int = 4321):
 
 
 def partition(total: int, ws: int, rank: int, prefixes):
+    """This rank's request ids: sorted by prefix length and dealt round-robin, so every rank gets the same count
+    and nearly the same attention work."""
     order = sorted(range(total), key=lambda r: prefixes[r])
     return order[rank::ws]
 

@@ -23,10 +23,14 @@ namespace accept {
 
 // exp(y), y <= 0, float32: Cody & Waite range reduction (ln 2 = 0.693359375 - 2.12194440e-4) and the
 // degree-7 Taylor polynomial of exp evaluated by Horner's rule; every operation individually rounded.
+// n = rint(y log2 e) is formed by adding 1.5 * 2^23 (the sum rounds to the nearest integer, ties to even, exactly
+// as rintf) so that neither the rounding nor the float -> int conversion uses the slow conversion pipe.
 __device__ __forceinline__ float exp32_rule(float y) {
     const bool ok = y > -87.0f;  // also false for NaN
     y = ok ? y : 0.0f;
-    const float n = rintf(__fmul_rn(y, 1.44269504088896341f));
+    const float t = __fadd_rn(__fmul_rn(y, 1.44269504088896341f), 12582912.0f);
+    const float n = __fsub_rn(t, 12582912.0f);
+    const int ni = __float_as_int(t) - 0x4B400000;
     float r = __fmaf_rn(n, -0.693359375f, y);
     r = __fmaf_rn(n, 2.12194440e-4f, r);
     float q = 1.0f / 5040.0f;
@@ -37,12 +41,16 @@ __device__ __forceinline__ float exp32_rule(float y) {
     q = __fmaf_rn(q, r, 0.5f);
     q = __fmaf_rn(q, r, 1.0f);
     q = __fmaf_rn(q, r, 1.0f);
-    const int ni = (int)n;
     return ok ? __uint_as_float(__float_as_uint(q) + ((uint32_t)ni << 23)) : 0.0f;
 }
+// trunc(e * 2^40) for 0 <= e < 2 from e's fields: e = M * 2^(k - 23) with M the 24-bit significand, so
+// e * 2^40 = M * 2^(k + 17) (exact: the conversion truncates only the fraction); tiny e gives 0.
 __device__ __forceinline__ uint64_t fixed40(float x, float m, float inv_t) {
-    const float e = exp32_rule(__fmul_rn(__fsub_rn(x, m), inv_t));
-    return (uint64_t)__fmul_rn(e, 1099511627776.0f);  // 2^40; float -> uint64 truncates toward zero
+    const uint32_t u = __float_as_uint(exp32_rule(__fmul_rn(__fsub_rn(x, m), inv_t)));
+    const int s = (int)(u >> 23) - 127 + 17;
+    const uint32_t M = (u & 0x7FFFFFu) | 0x800000u;
+    if (u == 0u) return 0ull;
+    return s >= 0 ? ((uint64_t)M << s) : (uint64_t)(M >> min(-s, 31));
 }
 
 struct Params {
@@ -251,39 +259,87 @@ __device__ __forceinline__ uint64_t weight_sum(const uint16_t* x, int64_t c0, in
     return z;
 }
 
-constexpr int kSampleThreads = 512;
+constexpr int kSampleThreads = 768;
+constexpr int kSampleWarps = kSampleThreads / 32;
+constexpr int kMaxRounds = 64;  // rows up to 64 rounds x 768 threads x 8 elements = 393216 logits
 
-// stochastic: one CTA per row.  Pass 1: the row max (coalesced).  Pass 2: thread t sums the weights of its
-// contiguous segment; a block scan turns the sums into prefix offsets and Z.  Pass 3: warp 0 finds the crossing
-// inside the one segment that holds floor(u * Z).  All sums are integers, so no order changes the result.
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(Params p) {
-    __shared__ uint64_t red[kSampleThreads / 32];
-    __shared__ uint64_t seg_sum[kSampleThreads];
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += shfl_xor_u64(v, o);
+    return v;
+}
+// the weights of vector v (elements 8v .. 8v+7 of the row) and its float maximum; absent elements weigh 0
+__device__ __forceinline__ uint4 load_vec8(const uint16_t* x, int64_t v, int64_t V, bool aligned) {
+    const int64_t e0 = v * 8;
+    if (aligned && e0 + 8 <= V) return ldg_stream_u4(x + e0);
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t lo = e0 + 2 * q < V ? x[e0 + 2 * q] : 0xFF80u;      // bf16 -inf
+        const uint32_t hi = e0 + 2 * q + 1 < V ? x[e0 + 2 * q + 1] : 0xFF80u;
+        w[q] = lo | (hi << 16);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ uint64_t vec8_weight(uint4 w, float m, float inv_t) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint64_t z = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) z += fixed40(bf16lo(ws[q]), m, inv_t) + fixed40(bf16hi(ws[q]), m, inv_t);
+    return z;
+}
+
+// stochastic: one 768-thread CTA per row (two resident per SM, so about 300 rows are in flight and the second
+// pass over a row hits L2).  Vector v = r * 768 + t (8 logits) belongs to thread t in round r, so every load is coalesced and the rounds
+// are in row order.  Pass 1: the row max.  Pass 2: per round, each warp's 256-logit weight sum.  Warp 0 scans
+// the (round, warp) sums in row order to find the one holding floor(u * Z) and searches its 256 logits.  All
+// sums are integers, so no order changes the result.
+__global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
+    __shared__ uint64_t wsum[kMaxRounds * kSampleWarps];
+    __shared__ float wmax[kSampleWarps];
     __shared__ int flag;
     __shared__ int64_t s_token;
     const int64_t row = blockIdx.x;
     const int64_t b = row / p.width;
     const uint16_t* x = p.logits + row * p.row_stride;
     const int64_t V = p.vocab;
-    const uint64_t best = block_reduce_max_u64<kSampleThreads>(argmax_share<kSampleThreads>(x, 0, V), red);
-    const float m = key_value(best);
-    const float inv_t = __frcp_rn(p.temperature);
-    int64_t seg = (V + kSampleThreads - 1) / kSampleThreads;
-    seg = (seg + 7) / 8 * 8;
-    const int64_t a0 = min(V, (int64_t)threadIdx.x * seg), a1 = min(V, a0 + seg);
-    const uint64_t mine = weight_sum(x, a0, a1, m, inv_t);
-    seg_sum[threadIdx.x] = mine;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        // warp 0: exclusive prefix over the 512 segment sums (16 per lane, in order)
-        const int lane = threadIdx.x;
-        uint64_t loc[16];
-        uint64_t tot = 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool aligned = (((uintptr_t)x) & 15u) == 0;
+    const int64_t nv = (V + 7) / 8;
+    const int rounds = (int)((nv + kSampleThreads - 1) / kSampleThreads);
+    // ---- pass 1: max
+    float mx = -INFINITY;
+    for (int r = 0; r < rounds; ++r) {
+        const int64_t v = (int64_t)r * kSampleThreads + threadIdx.x;
+        if (v >= nv) break;
+        const uint4 w = load_vec8(x, v, V, aligned);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            loc[i] = seg_sum[lane * 16 + i];
-            tot += loc[i];
-        }
+        for (int q = 0; q < 4; ++q) mx = fmaxf(mx, fmaxf(bf16lo(ws[q]), bf16hi(ws[q])));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MFD_FULL_MASK, mx, o));
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();
+    float m = wmax[0];
+#pragma unroll 8
+    for (int w = 1; w < kSampleWarps; ++w) m = fmaxf(m, wmax[w]);
+    const float inv_t = __frcp_rn(p.temperature);
+    // ---- pass 2: the weight of each (round, warp) block of 256 logits
+    for (int r = 0; r < rounds; ++r) {
+        const int64_t v = (int64_t)r * kSampleThreads + threadIdx.x;
+        const uint64_t z = v < nv ? vec8_weight(load_vec8(x, v, V, aligned), m, inv_t) : 0ull;
+        const uint64_t ws = warp_sum_u64(z);
+        if (lane == 0) wsum[r * kSampleWarps + warp] = ws;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scan over the rounds x warps block sums in row order, a contiguous run of entries per lane
+        const int ne = rounds * kSampleWarps;
+        const int per = (ne + 31) / 32;  // entries per lane, in row order
+        const int e0 = min(lane * per, ne), e1 = min(e0 + per, ne);
+        uint64_t tot = 0;
+        for (int e = e0; e < e1; ++e) tot += wsum[e];
         uint64_t incl = tot;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -292,42 +348,55 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(Params p) {
         }
         const uint64_t Z = shfl_u64(incl, 31);
         const uint64_t target = (uint64_t)floor(p.uniforms[row] * (double)Z);
-        uint64_t run = incl - tot;  // exclusive prefix of this lane's first segment
+        uint64_t run = incl - tot;
         int hit = -1;
         uint64_t before = 0;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            if (hit < 0 && run + loc[i] > target) { hit = lane * 16 + i; before = run; }
-            run += loc[i];
+        for (int e = e0; e < e1; ++e) {
+            const uint64_t w = wsum[e];
+            if (hit < 0 && run + w > target) {
+                hit = e;
+                before = run;
+            }
+            run += w;
         }
         const uint32_t bal = __ballot_sync(MFD_FULL_MASK, hit >= 0);
-        const int src = __ffs(bal) - 1;  // segments are in lane order: the first lane with a hit holds the crossing
-        const int segi = __shfl_sync(MFD_FULL_MASK, hit, src);
-        const uint64_t base = shfl_u64(before, src);
-        // pass 3 over segment segi: lane l takes elements [s0 + l*sub, ...)
-        const int64_t s0 = min(V, (int64_t)segi * seg), s1 = min(V, s0 + seg);
-        const int64_t sub = (s1 - s0 + 31) / 32;
-        const int64_t l0 = min(s1, s0 + lane * sub), l1 = min(s1, l0 + sub);
-        const uint64_t ls = weight_sum(x, l0, l1, m, inv_t);
-        uint64_t li = ls;
+        int64_t tok = V - 1;  // Z == 0 (every logit -inf): no crossing
+        if (bal) {
+            const int src = __ffs(bal) - 1;  // blocks are in lane order: the first lane with a hit holds it
+            const int eh = __shfl_sync(MFD_FULL_MASK, hit, src);
+            const uint64_t base = shfl_u64(before, src);
+            // block eh = (round eh / warps, warp eh % warps): 32 consecutive vectors, one per lane
+            const int64_t v = (int64_t)(eh / kSampleWarps) * kSampleThreads + (eh % kSampleWarps) * 32 + lane;
+            const uint4 w = v < nv ? load_vec8(x, v, V, aligned) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u,
+                                                                                0xFF80FF80u);
+            const uint64_t ls = v < nv ? vec8_weight(w, m, inv_t) : 0ull;
+            uint64_t li = ls;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t y = shfl_u64(li, lane >= o ? lane - o : lane);
-            if (lane >= o) li += y;
-        }
-        const uint64_t lex = base + li - ls;
-        const bool in_me = (lex <= target) && (target < lex + ls);
-        const uint32_t b2 = __ballot_sync(MFD_FULL_MASK, in_me && ls > 0);
-        if (b2 && lane == __ffs(b2) - 1) {
-            uint64_t c = lex;
-            int64_t tok = l1 - 1;
-            for (int64_t j = l0; j < l1; ++j) {
-                c += fixed40(bf16_at(x + j), m, inv_t);
-                if (c > target) { tok = j; break; }
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t y = shfl_u64(li, lane >= o ? lane - o : lane);
+                if (lane >= o) li += y;
             }
-            s_token = tok;
+            const uint64_t lex = base + li - ls;
+            const bool in_me = ls > 0 && lex <= target && target < lex + ls;
+            const uint32_t b2 = __ballot_sync(MFD_FULL_MASK, in_me);
+            const int owner = b2 ? __ffs(b2) - 1 : 0;
+            if (b2 && lane == owner) {
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                uint64_t c = lex;
+                tok = v * 8 + 7;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float xv = (q & 1) ? bf16hi(ws[q >> 1]) : bf16lo(ws[q >> 1]);
+                    c += fixed40(xv, m, inv_t);
+                    if (c > target) {
+                        tok = v * 8 + q;
+                        break;
+                    }
+                }
+            }
+            tok = __shfl_sync(MFD_FULL_MASK, (long long)tok, owner);
         }
-        if (!b2 && lane == 0) s_token = V - 1;  // unreachable when Z > 0
+        if (lane == 0) s_token = tok;
     }
     __syncthreads();
     if (threadIdx.x == 0) p.posterior[row] = s_token;
@@ -425,6 +494,10 @@ extern "C" int mfd_accept(const void* logits, int64_t row_stride, int64_t vocab,
         set_error("mfd_accept: temperature > 0 needs uniforms");
         return MFD_ERR_INVALID;
     }
+    if (temperature >= 1e-5f && vocab > (int64_t)accept::kMaxRounds * accept::kSampleThreads * 8) {
+        set_error("mfd_accept: sampling supports vocab <= %d", accept::kMaxRounds * accept::kSampleThreads * 8);
+        return MFD_ERR_UNSUPPORTED;
+    }
     if (!workspace || workspace_bytes < mfd_accept_workspace(bs, width) || !tickets ||
         tickets_len < mfd_accept_tickets(bs, width)) {
         set_error("mfd_accept: workspace of %zu bytes and %lld zeroed tickets needed", mfd_accept_workspace(bs, width),
@@ -474,6 +547,10 @@ extern "C" int mfd_sample_tokens(const void* logits, int64_t row_stride, int64_t
     if (!logits || !posterior || (temperature >= 1e-5f && !uniforms)) {
         set_error("mfd_sample_tokens: null pointer");
         return MFD_ERR_INVALID;
+    }
+    if (temperature >= 1e-5f && vocab > (int64_t)accept::kMaxRounds * accept::kSampleThreads * 8) {
+        set_error("mfd_sample_tokens: sampling supports vocab <= %d", accept::kMaxRounds * accept::kSampleThreads * 8);
+        return MFD_ERR_UNSUPPORTED;
     }
     accept::Params p = {};
     p.logits = (const uint16_t*)logits;

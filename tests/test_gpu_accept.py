@@ -84,6 +84,27 @@ def test_stochastic_accept_bit_exact_vs_oracle(V, T):
         assert int(o["accept_len"][b]) == len(acc) - 1 and int(o["bonus"][b]) == bonus
 
 
+def test_sample_tokens_edge_rows_bit_exact():
+    """-inf entries, a single finite logit, a peaked row, u at the ends of [0, 1), vocab not a multiple of 8 (rows
+    start at unaligned addresses), and a row of all -inf (sampled token V - 1, as the oracle defines it)."""
+    from mfd_b200 import ops
+    V = 5003
+    g = torch.Generator().manual_seed(5)
+    x = (torch.randn(8, V, generator=g) * 2).to(torch.bfloat16)
+    x[0, ::2] = float("-inf")
+    x[1, :] = float("-inf")
+    x[1, 4321] = 3.0
+    x[2, 17] = 40.0
+    x[3, :] = float("-inf")
+    u = torch.tensor([0.0, 0.5, 0.999999, 0.3, 0.0, 0.9999999999, 0.25, 0.75], dtype=torch.float64)
+    post = ops.sample_tokens(x.to(DEV), temperature=0.8, uniforms=u.to(DEV))
+    bits = x.view(torch.int16).numpy().astype(np.uint16)
+    inv_t = float(np.float32(1.0) / np.float32(0.8))
+    ref = oracle.sample_rows(bits, inv_t, u.numpy())
+    assert np.array_equal(post.cpu().numpy(), ref)
+    assert int(post[1]) == 4321 and int(post[3]) == V - 1
+
+
 def test_sglang_follow_outputs():
     from mfd_b200 import ddtree_utils
     g = torch.Generator().manual_seed(11)
