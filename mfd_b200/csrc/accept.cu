@@ -289,12 +289,59 @@ __device__ __forceinline__ uint64_t vec8_weight(uint4 w, float m, float inv_t) {
     return z;
 }
 
+// The weight of a logit depends only on its bf16 bit pattern (m and T are fixed per row), so each row first
+// tabulates fixed40 over the patterns it can contain and pass 2 looks weights up instead of evaluating the
+// exponential 150k times.  Table: magnitudes [lo, hi_p] of positive patterns, then [lo, hi_n] of negative ones.
+//   * below lo (|x| < tau) every pattern has the weight of x = 0: with m != 0, tau = 2^(e_m - 26) is under a
+//     quarter ulp of m, so fsub(x, m) == -m exactly; with m == 0, tau = 2^(e_T - 28) keeps |x / T| < 2^-26, where
+//     the polynomial rounds to exactly 1.0, as it does for x = 0;
+//   * positive patterns above m cannot occur (m is the row max);
+//   * negative magnitudes at or beyond 90 T + |m| have (x - m) / T < -88 after rounding: weight 0.
+// Every table entry is fixed40 itself, so pass 2 sums exactly the values the direct evaluation would.
+constexpr int kTableCap = 12 * 1024;  // entries; rows needing more are evaluated directly
+
+struct RowTable {
+    int lo, hi_p, hi_n, npos;  // magnitude range limits and the positive-part size; npos < 0: no table
+};
+
+__device__ __forceinline__ int bf16_mag_ceil(float v) {  // smallest bf16 magnitude pattern >= v (v >= 0, finite)
+    uint32_t u = __float_as_uint(v);
+    uint32_t hi = u >> 16;
+    if (u & 0xFFFFu) ++hi;
+    return (int)min(hi, 0x7F80u);
+}
+
+__device__ RowTable plan_table(float m, float inv_t) {
+    RowTable t;
+    t.npos = -1;
+    if (!isfinite(m) || !(inv_t > 0.f) || !isfinite(inv_t)) return t;
+    const float T = 1.0f / inv_t;
+    float tau;
+    if (m != 0.0f && fabsf(m) >= 1e-30f) {
+        const int e_m = ((__float_as_uint(m) >> 23) & 0xFF) - 127;
+        tau = ldexpf(1.0f, e_m - 26);
+    } else if (m == 0.0f) {
+        const int e_t = ((__float_as_uint(T) >> 23) & 0xFF) - 127;
+        tau = ldexpf(1.0f, max(e_t - 28, -126));
+    } else {
+        return t;  // a tiny nonzero max: evaluate directly
+    }
+    t.lo = (int)(__float_as_uint(tau) >> 16);  // tau is a power of two: exact as bf16
+    t.hi_p = m > 0.f ? (int)(__float_as_uint(m) >> 16) : t.lo - 1;
+    t.hi_n = bf16_mag_ceil(90.0f * T + fabsf(m));
+    const int np = max(t.hi_p - t.lo + 1, 0), nn = max(t.hi_n - t.lo + 1, 0);
+    if (np + nn + 2 > kTableCap) return t;
+    t.npos = np;
+    return t;
+}
+
 // stochastic: one 768-thread CTA per row (two resident per SM, so about 300 rows are in flight and the second
-// pass over a row hits L2).  Vector v = r * 768 + t (8 logits) belongs to thread t in round r, so every load is coalesced and the rounds
-// are in row order.  Pass 1: the row max.  Pass 2: per round, each warp's 256-logit weight sum.  Warp 0 scans
-// the (round, warp) sums in row order to find the one holding floor(u * Z) and searches its 256 logits.  All
-// sums are integers, so no order changes the result.
+// pass over a row hits L2).  Vector v = r * 768 + t (8 logits) belongs to thread t in round r, so every load is
+// coalesced and the rounds are in row order.  Pass 1: the row max.  Table of weights.  Pass 2: per round, each
+// warp's 256-logit weight sum.  Warp 0 scans the (round, warp) sums in row order to find the one holding
+// floor(u * Z) and searches its 256 logits.  All sums are integers, so no order changes the result.
 __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
+    extern __shared__ __align__(16) uint64_t table[];  // [kTableCap]
     __shared__ uint64_t wsum[kMaxRounds * kSampleWarps];
     __shared__ float wmax[kSampleWarps];
     __shared__ int flag;
@@ -325,10 +372,46 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
 #pragma unroll 8
     for (int w = 1; w < kSampleWarps; ++w) m = fmaxf(m, wmax[w]);
     const float inv_t = __frcp_rn(p.temperature);
+    // ---- the row's weight table
+    const RowTable tb = plan_table(m, inv_t);
+    const int n_tab = tb.npos >= 0 ? tb.npos + max(tb.hi_n - tb.lo + 1, 0) : 0;
+    if (tb.npos >= 0) {
+        for (int i = threadIdx.x; i < n_tab + 2; i += kSampleThreads) {
+            uint64_t e;
+            if (i < tb.npos) {
+                e = fixed40(__uint_as_float((uint32_t)(tb.lo + i) << 16), m, inv_t);
+            } else if (i < n_tab) {
+                e = fixed40(__uint_as_float((uint32_t)(0x8000 | (tb.lo + i - tb.npos)) << 16), m, inv_t);
+            } else if (i == n_tab) {
+                e = fixed40(0.0f, m, inv_t);  // every magnitude below tau
+            } else {
+                e = 0ull;  // beyond the cut (and impossible patterns)
+            }
+            table[i] = e;
+        }
+        __syncthreads();
+    }
+    auto weight = [&](uint32_t bits) -> uint64_t {  // bits: one bf16 pattern; selects only, no branches
+        const int mag = (int)(bits & 0x7FFFu);
+        const bool neg = (bits & 0x8000u) != 0u;
+        const int i = mag - tb.lo;
+        const int hi = neg ? tb.hi_n : tb.hi_p;
+        const int base = neg ? tb.npos : 0;
+        const int idx = i < 0 ? n_tab : (mag <= hi ? base + i : n_tab + 1);
+        return table[idx];
+    };
+    auto vec_weight = [&](uint4 w) -> uint64_t {
+        if (tb.npos < 0) return vec8_weight(w, m, inv_t);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        uint64_t z = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) z += weight(ws[q] & 0xFFFFu) + weight(ws[q] >> 16);
+        return z;
+    };
     // ---- pass 2: the weight of each (round, warp) block of 256 logits
     for (int r = 0; r < rounds; ++r) {
         const int64_t v = (int64_t)r * kSampleThreads + threadIdx.x;
-        const uint64_t z = v < nv ? vec8_weight(load_vec8(x, v, V, aligned), m, inv_t) : 0ull;
+        const uint64_t z = v < nv ? vec_weight(load_vec8(x, v, V, aligned)) : 0ull;
         const uint64_t ws = warp_sum_u64(z);
         if (lane == 0) wsum[r * kSampleWarps + warp] = ws;
     }
@@ -336,7 +419,7 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     if (warp == 0) {
         // exclusive scan over the rounds x warps block sums in row order, a contiguous run of entries per lane
         const int ne = rounds * kSampleWarps;
-        const int per = (ne + 31) / 32;  // entries per lane, in row order
+        const int per = (ne + 31) / 32;
         const int e0 = min(lane * per, ne), e1 = min(e0 + per, ne);
         uint64_t tot = 0;
         for (int e = e0; e < e1; ++e) tot += wsum[e];
@@ -367,8 +450,8 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
             const uint64_t base = shfl_u64(before, src);
             // block eh = (round eh / warps, warp eh % warps): 32 consecutive vectors, one per lane
             const int64_t v = (int64_t)(eh / kSampleWarps) * kSampleThreads + (eh % kSampleWarps) * 32 + lane;
-            const uint4 w = v < nv ? load_vec8(x, v, V, aligned) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u,
-                                                                                0xFF80FF80u);
+            const uint4 w = v < nv ? load_vec8(x, v, V, aligned)
+                                   : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
             const uint64_t ls = v < nv ? vec8_weight(w, m, inv_t) : 0ull;
             uint64_t li = ls;
 #pragma unroll
@@ -461,7 +544,13 @@ static int launch_accept(accept::Params& p, int64_t rows, void* scratch, unsigne
         accept::greedy_kernel<<<(unsigned)(rows * p.parts), accept::kGreedyThreads, 0, stream>>>(p);
     } else {
         p.parts = 1;
-        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
+        const int smem = accept::kTableCap * (int)sizeof(uint64_t);
+        cudaError_t e = cudaFuncSetAttribute(accept::sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) {
+            set_error("%s: %s", fn, cudaGetErrorString(e));
+            return MFD_ERR_CUDA;
+        }
+        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, smem, stream>>>(p);
     }
     MFD_CHECK_LAUNCH(fn);
     return MFD_OK;

@@ -92,6 +92,47 @@ __device__ __forceinline__ int tuple_cmp(const int16_t* a, int na, const int16_t
     return na == nb ? 0 : (na < nb ? -1 : 1);
 }
 
+// Tree outputs of request b from its node arrays: the SGLang layout, the count, ancestor bitsets, dense mask.
+__device__ void write_tree_outputs(const Params& p, int b, int n, const int32_t* ntok, const int16_t* npar,
+                                   const uint8_t* ndep) {
+    const int W = p.B + 1;
+    int64_t* t = p.tree + (size_t)b * 3 * W;
+    int64_t* d = t + W;
+    int64_t* pa = d + W;
+    for (int i = threadIdx.x; i < W; i += kThreads) {
+        const bool live_node = i <= n;
+        t[i] = (live_node && i > 0) ? (int64_t)ntok[i] : 0;
+        d[i] = live_node ? (int64_t)ndep[i] : 0;
+        pa[i] = live_node ? (int64_t)npar[i] : -1;
+    }
+    if (threadIdx.x == 0) p.counts[b] = n;
+    if (p.anc || p.vis) {
+        const int words = p.words;
+        for (int i = threadIdx.x; i < W; i += kThreads) {
+            uint64_t bits[8];  // words <= 8 (B < 512)
+#pragma unroll
+            for (int w = 0; w < 8; ++w) bits[w] = 0;
+            if (i <= n) {
+                int node = i;
+                while (node >= 0) {
+                    bits[node >> 6] |= 1ull << (node & 63);
+                    node = node == 0 ? -1 : npar[node];
+                }
+            }
+            if (p.anc) {
+                uint64_t* row = p.anc + ((size_t)b * W + i) * words;
+#pragma unroll
+                for (int w = 0; w < 8; ++w)
+                    if (w < words) row[w] = bits[w];
+            }
+            if (p.vis) {
+                uint8_t* row = p.vis + ((size_t)b * W + i) * W;
+                for (int j = 0; j < W; ++j) row[j] = (uint8_t)((bits[j >> 6] >> (j & 63)) & 1ull);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int b = blockIdx.x;
@@ -353,42 +394,196 @@ __global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
     const int n = sh_count;
     if (sh_fail && threadIdx.x == 0 && p.status) atomicExch(p.status, (int)MFD_ERR_CAPACITY);
 
-    // ---- outputs
-    int64_t* t = p.tree + (size_t)b * 3 * W;
-    int64_t* d = t + W;
-    int64_t* pa = d + W;
-    for (int i = threadIdx.x; i < W; i += kThreads) {
-        const bool live_node = i <= n;
-        t[i] = (live_node && i > 0) ? (int64_t)s.ntok[i] : 0;
-        d[i] = live_node ? (int64_t)s.ndep[i] : 0;
-        pa[i] = live_node ? (int64_t)s.npar[i] : -1;
-    }
-    if (threadIdx.x == 0) p.counts[b] = n;
-    if (p.anc || p.vis) {
-        const int words = p.words;
-        for (int i = threadIdx.x; i < W; i += kThreads) {
-            uint64_t bits[8];  // words <= 8 (B < 512)
-#pragma unroll
-            for (int w = 0; w < 8; ++w) bits[w] = 0;
-            if (i <= n) {
-                int node = i;
-                while (node >= 0) {
-                    bits[node >> 6] |= 1ull << (node & 63);
-                    node = node == 0 ? -1 : s.npar[node];
-                }
-            }
-            if (p.anc) {
-                uint64_t* row = p.anc + ((size_t)b * W + i) * words;
-#pragma unroll
-                for (int w = 0; w < 8; ++w)
-                    if (w < words) row[w] = bits[w];
-            }
-            if (p.vis) {
-                uint8_t* row = p.vis + ((size_t)b * W + i) * W;
-                for (int j = 0; j < W; ++j) row[j] = (uint8_t)((bits[j >> 6] >> (j & 63)) & 1ull);
+    write_tree_outputs(p, b, n, s.ntok, s.npar, s.ndep);
+}
+
+// ------------------------------------------------------------------ mixture heap with register-resident entries
+// The same mixture pop order as build_trees_kernel, for trees of at most 127 nodes whose live entries fit
+// 32 x E registers (K (B+1) <= 32 E, the worst case: every pop adds at most one entry).  Lane l keeps entries in
+// registers (comp: the packed 64-bit comparator, unique per entry, whose low word is the entry's mode, parent,
+// depth and rank; lw: its float64 logw) and the (token, parent) keys of nodes l, l + 32, ... for the dedup, so a
+// pop touches shared memory only for the candidate tables: a warp min over the lanes' cached minima, a broadcast
+// of the popped logw, one ballot for the dedup, and the successors written back into registers.
+constexpr int kRegNodesPerLane = 4;  // nodes <= 128
+
+template <int E>
+__global__ void __launch_bounds__(kThreads) mixture_reg_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int b = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int K = p.K, L = p.L, k = p.k, B = p.B, W = B + 1;
+    float* s_lp = (float*)smem_raw;                 // [K][L][k]
+    int32_t* s_ids = (int32_t*)(s_lp + K * L * k);  // [K][L][k]
+    int32_t* ntok = s_ids + K * L * k;               // [W]
+    int16_t* npar = (int16_t*)(ntok + W);           // [W]
+    uint8_t* ndep = (uint8_t*)(npar + W);           // [W]
+    float* prior = (float*)(((uintptr_t)(ndep + W) + 15) & ~(uintptr_t)15);  // [K]
+    const float* glp = p.lp + (size_t)b * K * L * k;
+    const void* gids = p.ids_i64 ? (const void*)((const int64_t*)p.ids + (size_t)b * K * L * k)
+                                 : (const void*)((const int32_t*)p.ids + (size_t)b * K * L * k);
+    const int n_el = K * L * k;
+    if ((n_el % 4) == 0 && (((uintptr_t)glp) & 15u) == 0 && (((uintptr_t)gids) & 15u) == 0) {
+        for (int c = threadIdx.x; c < n_el / 4; c += kThreads) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_lp + 4 * c)), "l"(glp + 4 * c));
+            if (!p.ids_i64)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_ids + 4 * c)),
+                             "l"((const int32_t*)gids + 4 * c));
+        }
+        asm volatile("cp.async.commit_group;");
+        if (p.ids_i64) {
+            const longlong2* g2 = (const longlong2*)gids;
+#pragma unroll 4
+            for (int c = threadIdx.x; c < n_el / 2; c += kThreads) {
+                const longlong2 v = __ldg(g2 + c);
+                s_ids[2 * c] = (int32_t)v.x;
+                s_ids[2 * c + 1] = (int32_t)v.y;
             }
         }
+        asm volatile("cp.async.wait_all;");
+    } else {
+        for (int i = threadIdx.x; i < n_el; i += kThreads) {
+            s_lp[i] = glp[i];
+            s_ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[i] : ((const int32_t*)gids)[i];
+        }
     }
+    for (int i = threadIdx.x; i < K; i += kThreads) prior[i] = p.prior ? p.prior[(size_t)b * K + i] : 0.f;
+    if (threadIdx.x == 0) {
+        ntok[0] = 0;
+        npar[0] = -1;
+        ndep[0] = 0;
+    }
+    __syncthreads();
+
+    __shared__ int sh_count;
+    if (warp == 0) {
+        uint64_t comp[E];
+        double lw[E];
+#pragma unroll
+        for (int q = 0; q < E; ++q) {
+            comp[q] = ~0ull;
+            lw[q] = 0.0;
+        }
+        uint64_t tp[kRegNodesPerLane];  // (token << 32 | parent << 16) of nodes lane + 32 q
+#pragma unroll
+        for (int q = 0; q < kRegNodesPerLane; ++q) tp[q] = ~0ull;
+        constexpr uint32_t kFull = E >= 32 ? 0xffffffffu : ((1u << E) - 1u);
+        uint32_t occ = 0;
+        uint64_t lmin = ~0ull;
+        int lq = 0;
+        int count = 0, live = 0, rr = 0;
+        auto lane_min = [&]() {
+            lmin = ~0ull;
+            lq = 0;
+#pragma unroll
+            for (int q = 0; q < E; ++q)
+                if (comp[q] < lmin) {
+                    lmin = comp[q];
+                    lq = q;
+                }
+        };
+        auto insert = [&](int dst, uint64_t c, double w) {  // warp-uniform; capacity suffices by construction
+            const uint32_t room = __ballot_sync(MFD_FULL_MASK, occ != kFull);
+            if (!((room >> dst) & 1u)) dst = __ffs(room) - 1;
+            if (lane == dst) {
+                const int q = __ffs(~occ) - 1;
+                occ |= 1u << q;
+#pragma unroll
+                for (int qq = 0; qq < E; ++qq)
+                    if (qq == q) {
+                        comp[qq] = c;
+                        lw[qq] = w;
+                    }
+                if (c < lmin) {
+                    lmin = c;
+                    lq = q;
+                }
+            }
+            ++live;
+        };
+        auto mix_comp = [&](double w, int m, uint32_t ax) -> uint64_t {
+            float key = -(__double2float_rn(w) + prior[m]);
+            key = key + 0.0f;  // -0.0 and +0.0 compare equal in the reference: fold them
+            return ((uint64_t)ord_f32(key) << 32) | ax;
+        };
+        if (B > 0 && L > 0)
+            for (int m = 0; m < K; ++m) {
+                const double w = (double)s_lp[(m * L) * k];
+                const uint32_t ax = pack_aux(m, 0, 1, 0);
+                insert(m & 31, mix_comp(w, m, ax), w);
+            }
+        while (live > 0 && count < B) {
+            const uint64_t M = warp_min_u64(lmin);
+            const int owner = __ffs(__ballot_sync(MFD_FULL_MASK, lmin == M)) - 1;
+            double wo = 0.0;
+            if (lane == owner) {
+#pragma unroll
+                for (int q = 0; q < E; ++q)
+                    if (q == lq) wo = lw[q];
+            }
+            const double lwp = shfl_f64(wo, owner);
+            const uint32_t ax = (uint32_t)M;
+            const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
+            const int row = (m * L + dep - 1) * k;
+            const int32_t token = s_ids[row + rk];
+            const float lp_r = s_lp[row + rk];
+            const bool has_sib = rk + 1 < k, has_child = dep < L;
+            const float lp_r1 = has_sib ? s_lp[row + rk + 1] : 0.f;
+            const float lp_c = has_child ? s_lp[row + k] : 0.f;  // (m, dep, 0)
+            // node: an existing prefix reached by another mode, or a new one
+            const uint64_t want = ((uint64_t)(uint32_t)token << 32) | ((uint64_t)(uint32_t)par << 16);
+            int hq = -1;
+#pragma unroll
+            for (int q = 0; q < kRegNodesPerLane; ++q)
+                if (tp[q] == want) hq = q;
+            const uint32_t hit = __ballot_sync(MFD_FULL_MASK, hq >= 0);
+            int current;
+            if (hit) {
+                const int hl = __ffs(hit) - 1;
+                current = hl + 32 * __shfl_sync(MFD_FULL_MASK, hq, hl);
+            } else {
+                current = count + 1;
+                if (lane == (current & 31)) {
+#pragma unroll
+                    for (int q = 0; q < kRegNodesPerLane; ++q)
+                        if (q == (current >> 5)) tp[q] = want;
+                }
+                if (lane == 0) {
+                    ntok[current] = token;
+                    npar[current] = (int16_t)par;
+                    ndep[current] = (uint8_t)dep;
+                }
+                ++count;
+            }
+            // successors: the sibling replaces the popped entry, the child takes a free slot
+            if (lane == owner) {
+                if (has_sib) {
+                    const double slw = (lwp - (double)lp_r) + (double)lp_r1;
+                    const uint64_t sc = mix_comp(slw, m, pack_aux(m, par, dep, rk + 1));
+#pragma unroll
+                    for (int q = 0; q < E; ++q)
+                        if (q == lq) {
+                            comp[q] = sc;
+                            lw[q] = slw;
+                        }
+                } else {
+                    occ &= ~(1u << lq);
+#pragma unroll
+                    for (int q = 0; q < E; ++q)
+                        if (q == lq) comp[q] = ~0ull;
+                }
+                lane_min();
+            }
+            if (!has_sib) --live;
+            if (has_child) {
+                const double clw = lwp + (double)lp_c;
+                insert(rr, mix_comp(clw, m, pack_aux(m, current, dep + 1, 0)), clw);
+                rr = (rr + 1) & 31;
+            }
+        }
+        if (lane == 0) sh_count = count;
+    }
+    __syncthreads();
+    write_tree_outputs(p, b, sh_count, ntok, npar, ndep);
 }
 
 struct Plan {
@@ -455,6 +650,12 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
                   (long long)budget);
         return MFD_ERR_UNSUPPORTED;
     }
+    // the register-resident mixture heap when the tree and its worst-case entry count fit
+    const int64_t W = budget + 1;
+    const int64_t need = (num_modes * W + 31) / 32;
+    const size_t reg_smem = (size_t)8 * num_modes * depth_limit * topk + (size_t)W * 7 + 16 + (size_t)num_modes * 4 + 64;
+    const bool reg_path = !single && depth_limit > 0 && budget > 0 && W <= 32 * tree::kRegNodesPerLane &&
+                          need <= 17 && reg_smem <= 220 * 1024;
     tree::Params p;
     p.lp = top_logp;
     p.ids = top_ids;
@@ -475,6 +676,22 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
     p.anc = anc_bits;
     p.vis = visibility;
     p.status = status;
+    if (reg_path) {
+        auto launch_reg = [&](auto kern) -> int {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)reg_smem);
+            if (e != cudaSuccess) {
+                set_error("mfd_build_trees: %s", cudaGetErrorString(e));
+                return MFD_ERR_CUDA;
+            }
+            kern<<<(unsigned)bs, tree::kThreads, reg_smem, (cudaStream_t)stream>>>(p);
+            MFD_CHECK_LAUNCH("mfd_build_trees");
+            return MFD_OK;
+        };
+        if (need <= 4) return launch_reg(tree::mixture_reg_kernel<4>);
+        if (need <= 8) return launch_reg(tree::mixture_reg_kernel<8>);
+        if (need <= 12) return launch_reg(tree::mixture_reg_kernel<12>);
+        return launch_reg(tree::mixture_reg_kernel<17>);
+    }
     cudaError_t e = cudaFuncSetAttribute(tree::build_trees_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)pl.smem);
     if (e != cudaSuccess) {

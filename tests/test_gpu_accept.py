@@ -105,6 +105,26 @@ def test_sample_tokens_edge_rows_bit_exact():
     assert int(post[1]) == 4321 and int(post[3]) == V - 1
 
 
+@pytest.mark.parametrize("scale,shift,T", [(1.5, 0.0, 1.0), (0.5, -3.0, 0.1), (3.0, 0.0, 10.0), (0.001, 0.0, 1.0),
+                                           (300.0, 20.0, 2.0), (1.0, -50.0, 0.7)])
+def test_sample_tokens_weight_table_regimes(scale, shift, T):
+    """Rows whose max is positive, negative, zero (all logits <= 0), tiny or large, at small and large
+    temperatures: the per-row weight table (or the direct evaluation it falls back to) reproduces the oracle's
+    integer weights bit for bit."""
+    from mfd_b200 import ops
+    V = 151936
+    g = torch.Generator().manual_seed(int(scale * 7 + T * 13))
+    x = (torch.randn(6, V, generator=g) * scale + shift).to(torch.bfloat16)
+    if shift == 0.0 and scale == 0.001:
+        x = -x.abs()
+        x[:, 7] = 0.0  # max exactly 0
+    u = torch.rand(6, generator=g, dtype=torch.float64)
+    post = ops.sample_tokens(x.to(DEV), temperature=T, uniforms=u.to(DEV))
+    bits = x.view(torch.int16).numpy().astype(np.uint16)
+    inv_t = float(np.float32(1.0) / np.float32(T))
+    assert np.array_equal(post.cpu().numpy(), oracle.sample_rows(bits, inv_t, u.numpy()))
+
+
 def test_sglang_follow_outputs():
     from mfd_b200 import ddtree_utils
     g = torch.Generator().manual_seed(11)
