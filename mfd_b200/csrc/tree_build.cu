@@ -1,4 +1,4 @@
-// tree_build.cu -- exact best-first tree builders on the GPU, one warp per request.
+// tree_build.cu -- exact best-first tree builders on the GPU, one CTA per request.
 //
 // Reproduces the pop order of the reference heaps bit for bit:
 //   mixture (K modes): key = -(float(logw) + prior[mode]) in float32, ties by mode, parent, depth, rank
@@ -9,12 +9,13 @@
 // (logw - lp[rank]) + lp[rank+1], a child logw + lp[depth][0].  A prefix popped again by another mode
 // reuses its node (dedup by (parent, token) in a shared-memory hash table).
 //
-// Heap representation: the live entries sit in shared memory, each lane of the warp owning the slots
-// lane + 32*j.  The comparator is packed into one 64-bit key (mixture: orderable float32 key in the high
-// word, mode|parent|depth|rank in the low word -- unique per entry, so no further tie-break is ever reached;
-// single mode: the orderable float64 key), each lane caches the minimum of its slots, and a pop is a
-// warp-wide min (two redux.sync) over the cached minima.  Single-mode entries whose float64 keys tie exactly
-// are ordered by rank tuple on a slow path that walks parent pointers.
+// Heaps: the mixture heap (mixture_heap1_kernel) is a binary min-heap kept by one thread in shared memory; its
+// comparator is one 64-bit key (orderable float32 key in the high word, mode|parent|depth|rank in the low word)
+// that is unique per entry, so no further tie-break is ever reached and a pop is a sift-down, a push a sift-up.
+// The single-mode heap (build_trees_kernel, also the fallback when the mixture tables do not fit shared memory)
+// spreads the live entries over the lanes of a warp, each lane caching the minimum of its slots, and pops by a
+// warp-wide min (two redux.sync); single-mode entries whose float64 keys tie exactly are ordered by rank tuple on
+// a slow path that walks parent pointers.
 //
 // Outputs: the SGLang layout tree[bs, 3, B+1] (tokens, depths, parents; index 0 = root; tail entries
 // tokens 0 / depths 0 / parents -1), counts[bs], and optionally each node's ancestor-or-self set as a
@@ -397,27 +398,30 @@ __global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
     write_tree_outputs(p, b, n, s.ntok, s.npar, s.ndep);
 }
 
-// ------------------------------------------------------------------ mixture heap with register-resident entries
-// The same mixture pop order as build_trees_kernel, for trees of at most 127 nodes whose live entries fit
-// 32 x E registers (K (B+1) <= 32 E, the worst case: every pop adds at most one entry).  Lane l keeps entries in
-// registers (comp: the packed 64-bit comparator, unique per entry, whose low word is the entry's mode, parent,
-// depth and rank; lw: its float64 logw) and the (token, parent) keys of nodes l, l + 32, ... for the dedup, so a
-// pop touches shared memory only for the candidate tables: a warp min over the lanes' cached minima, a broadcast
-// of the popped logw, one ballot for the dedup, and the successors written back into registers.
-constexpr int kRegNodesPerLane = 4;  // nodes <= 128
-
-template <int E>
-__global__ void __launch_bounds__(kThreads) mixture_reg_kernel(Params p) {
+// ------------------------------------------------------------------ mixture heap in one thread
+// The same pop order from a binary min-heap kept by one thread in shared memory (keys are unique, so any exact
+// priority queue pops the same sequence): a pop is a sift-down of about log2(live) levels and a push a sift-up,
+// with the (parent, token) dedup in a shared-memory hash -- no warp-wide collective on the critical path.
+__global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int b = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int K = p.K, L = p.L, k = p.k, B = p.B, W = B + 1;
-    float* s_lp = (float*)smem_raw;                 // [K][L][k]
-    int32_t* s_ids = (int32_t*)(s_lp + K * L * k);  // [K][L][k]
-    int32_t* ntok = s_ids + K * L * k;               // [W]
-    int16_t* npar = (int16_t*)(ntok + W);           // [W]
-    uint8_t* ndep = (uint8_t*)(npar + W);           // [W]
-    float* prior = (float*)(((uintptr_t)(ndep + W) + 15) & ~(uintptr_t)15);  // [K]
+    const int cap = K * W;  // live entries never exceed K (B + 1)
+    unsigned char* q = smem_raw;
+    auto take = [&](size_t bytes) {
+        unsigned char* r = q;
+        q += (bytes + 15) & ~(size_t)15;
+        return r;
+    };
+    uint64_t* hc = (uint64_t*)take(8 * (size_t)cap);  // heap: comparator keys
+    double* hw = (double*)take(8 * (size_t)cap);      // heap: logw
+    uint64_t* hash = (uint64_t*)take(8 * (size_t)p.hcap);
+    float* s_lp = (float*)take(4 * (size_t)K * L * k);
+    int32_t* s_ids = (int32_t*)take(4 * (size_t)K * L * k);
+    int32_t* ntok = (int32_t*)take(4 * (size_t)W);
+    int16_t* npar = (int16_t*)take(2 * (size_t)W);
+    uint8_t* ndep = (uint8_t*)take((size_t)W);
+    float* prior = (float*)take(4 * (size_t)K);
     const float* glp = p.lp + (size_t)b * K * L * k;
     const void* gids = p.ids_i64 ? (const void*)((const int64_t*)p.ids + (size_t)b * K * L * k)
                                  : (const void*)((const int32_t*)p.ids + (size_t)b * K * L * k);
@@ -446,6 +450,7 @@ __global__ void __launch_bounds__(kThreads) mixture_reg_kernel(Params p) {
             s_ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[i] : ((const int32_t*)gids)[i];
         }
     }
+    for (int i = threadIdx.x; i < p.hcap; i += kThreads) hash[i] = kEmptyHash;
     for (int i = threadIdx.x; i < K; i += kThreads) prior[i] = p.prior ? p.prior[(size_t)b * K + i] : 0.f;
     if (threadIdx.x == 0) {
         ntok[0] = 0;
@@ -453,136 +458,106 @@ __global__ void __launch_bounds__(kThreads) mixture_reg_kernel(Params p) {
         ndep[0] = 0;
     }
     __syncthreads();
-
-    __shared__ int sh_count;
-    if (warp == 0) {
-        uint64_t comp[E];
-        double lw[E];
-#pragma unroll
-        for (int q = 0; q < E; ++q) {
-            comp[q] = ~0ull;
-            lw[q] = 0.0;
-        }
-        uint64_t tp[kRegNodesPerLane];  // (token << 32 | parent << 16) of nodes lane + 32 q
-#pragma unroll
-        for (int q = 0; q < kRegNodesPerLane; ++q) tp[q] = ~0ull;
-        constexpr uint32_t kFull = E >= 32 ? 0xffffffffu : ((1u << E) - 1u);
-        uint32_t occ = 0;
-        uint64_t lmin = ~0ull;
-        int lq = 0;
-        int count = 0, live = 0, rr = 0;
-        auto lane_min = [&]() {
-            lmin = ~0ull;
-            lq = 0;
-#pragma unroll
-            for (int q = 0; q < E; ++q)
-                if (comp[q] < lmin) {
-                    lmin = comp[q];
-                    lq = q;
-                }
-        };
-        auto insert = [&](int dst, uint64_t c, double w) {  // warp-uniform; capacity suffices by construction
-            const uint32_t room = __ballot_sync(MFD_FULL_MASK, occ != kFull);
-            if (!((room >> dst) & 1u)) dst = __ffs(room) - 1;
-            if (lane == dst) {
-                const int q = __ffs(~occ) - 1;
-                occ |= 1u << q;
-#pragma unroll
-                for (int qq = 0; qq < E; ++qq)
-                    if (qq == q) {
-                        comp[qq] = c;
-                        lw[qq] = w;
-                    }
-                if (c < lmin) {
-                    lmin = c;
-                    lq = q;
-                }
-            }
-            ++live;
-        };
+    __shared__ int sh_count, sh_fail;
+    if (threadIdx.x == 0) {
+        int n = 0;  // live entries
         auto mix_comp = [&](double w, int m, uint32_t ax) -> uint64_t {
             float key = -(__double2float_rn(w) + prior[m]);
             key = key + 0.0f;  // -0.0 and +0.0 compare equal in the reference: fold them
             return ((uint64_t)ord_f32(key) << 32) | ax;
         };
+        auto push = [&](uint64_t c, double w) {
+            int i = n++;
+            while (i > 0) {
+                const int par = (i - 1) >> 1;
+                const uint64_t pc = hc[par];
+                if (pc <= c) break;
+                hc[i] = pc;
+                hw[i] = hw[par];
+                i = par;
+            }
+            hc[i] = c;
+            hw[i] = w;
+        };
+        // replace the root by (c, w) and sift it down
+        auto replace_top = [&](uint64_t c, double w) {
+            int i = 0;
+            for (;;) {
+                const int l = 2 * i + 1;
+                if (l >= n) break;
+                const int r = l + 1;
+                const uint64_t lc = hc[l];
+                const uint64_t rc = r < n ? hc[r] : ~0ull;
+                const int j = rc < lc ? r : l;
+                const uint64_t jc = rc < lc ? rc : lc;
+                if (c <= jc) break;
+                hc[i] = jc;
+                hw[i] = hw[j];
+                i = j;
+            }
+            hc[i] = c;
+            hw[i] = w;
+        };
+        int count = 0, fail = 0;
         if (B > 0 && L > 0)
             for (int m = 0; m < K; ++m) {
                 const double w = (double)s_lp[(m * L) * k];
-                const uint32_t ax = pack_aux(m, 0, 1, 0);
-                insert(m & 31, mix_comp(w, m, ax), w);
+                push(mix_comp(w, m, pack_aux(m, 0, 1, 0)), w);
             }
-        while (live > 0 && count < B) {
-            const uint64_t M = warp_min_u64(lmin);
-            const int owner = __ffs(__ballot_sync(MFD_FULL_MASK, lmin == M)) - 1;
-            double wo = 0.0;
-            if (lane == owner) {
-#pragma unroll
-                for (int q = 0; q < E; ++q)
-                    if (q == lq) wo = lw[q];
-            }
-            const double lwp = shfl_f64(wo, owner);
+        while (n > 0 && count < B) {
+            const uint64_t M = hc[0];
+            const double lwp = hw[0];
             const uint32_t ax = (uint32_t)M;
             const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
             const int row = (m * L + dep - 1) * k;
             const int32_t token = s_ids[row + rk];
-            const float lp_r = s_lp[row + rk];
             const bool has_sib = rk + 1 < k, has_child = dep < L;
+            const float lp_r = s_lp[row + rk];
             const float lp_r1 = has_sib ? s_lp[row + rk + 1] : 0.f;
-            const float lp_c = has_child ? s_lp[row + k] : 0.f;  // (m, dep, 0)
-            // node: an existing prefix reached by another mode, or a new one
+            const float lp_c = has_child ? s_lp[row + k] : 0.f;
+            // node: dedup by (parent, token)
             const uint64_t want = ((uint64_t)(uint32_t)token << 32) | ((uint64_t)(uint32_t)par << 16);
-            int hq = -1;
-#pragma unroll
-            for (int q = 0; q < kRegNodesPerLane; ++q)
-                if (tp[q] == want) hq = q;
-            const uint32_t hit = __ballot_sync(MFD_FULL_MASK, hq >= 0);
-            int current;
-            if (hit) {
-                const int hl = __ffs(hit) - 1;
-                current = hl + 32 * __shfl_sync(MFD_FULL_MASK, hq, hl);
-            } else {
-                current = count + 1;
-                if (lane == (current & 31)) {
-#pragma unroll
-                    for (int q = 0; q < kRegNodesPerLane; ++q)
-                        if (q == (current >> 5)) tp[q] = want;
-                }
-                if (lane == 0) {
+            uint32_t h = (uint32_t)(((uint64_t)(uint32_t)token * 0x9E3779B1u) ^ ((uint32_t)par * 0x85EBCA77u));
+            int current = -1;
+            for (int t = 0; t < p.hcap; ++t) {
+                const uint32_t hs = (h + (uint32_t)t) & (uint32_t)(p.hcap - 1);
+                const uint64_t v = hash[hs];
+                if (v == kEmptyHash) {
+                    current = count + 1;
+                    hash[hs] = want | (uint64_t)(uint32_t)current;
                     ntok[current] = token;
                     npar[current] = (int16_t)par;
                     ndep[current] = (uint8_t)dep;
+                    ++count;
+                    break;
                 }
-                ++count;
-            }
-            // successors: the sibling replaces the popped entry, the child takes a free slot
-            if (lane == owner) {
-                if (has_sib) {
-                    const double slw = (lwp - (double)lp_r) + (double)lp_r1;
-                    const uint64_t sc = mix_comp(slw, m, pack_aux(m, par, dep, rk + 1));
-#pragma unroll
-                    for (int q = 0; q < E; ++q)
-                        if (q == lq) {
-                            comp[q] = sc;
-                            lw[q] = slw;
-                        }
-                } else {
-                    occ &= ~(1u << lq);
-#pragma unroll
-                    for (int q = 0; q < E; ++q)
-                        if (q == lq) comp[q] = ~0ull;
+                if ((v & ~0xffffull) == want) {
+                    current = (int)(v & 0xffffu);
+                    break;
                 }
-                lane_min();
             }
-            if (!has_sib) --live;
+            if (current < 0) {
+                fail = 1;
+                break;
+            }
+            // successors: the sibling replaces the popped root, the child is pushed
+            if (has_sib) {
+                const double slw = (lwp - (double)lp_r) + (double)lp_r1;
+                replace_top(mix_comp(slw, m, pack_aux(m, par, dep, rk + 1)), slw);
+            } else {
+                --n;
+                if (n > 0) replace_top(hc[n], hw[n]);
+            }
             if (has_child) {
                 const double clw = lwp + (double)lp_c;
-                insert(rr, mix_comp(clw, m, pack_aux(m, current, dep + 1, 0)), clw);
-                rr = (rr + 1) & 31;
+                push(mix_comp(clw, m, pack_aux(m, current, dep + 1, 0)), clw);
             }
         }
-        if (lane == 0) sh_count = count;
+        sh_count = count;
+        sh_fail = fail;
     }
     __syncthreads();
+    if (sh_fail && threadIdx.x == 0 && p.status) atomicExch(p.status, (int)MFD_ERR_CAPACITY);
     write_tree_outputs(p, b, sh_count, ntok, npar, ndep);
 }
 
@@ -650,12 +625,7 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
                   (long long)budget);
         return MFD_ERR_UNSUPPORTED;
     }
-    // the register-resident mixture heap when the tree and its worst-case entry count fit
     const int64_t W = budget + 1;
-    const int64_t need = (num_modes * W + 31) / 32;
-    const size_t reg_smem = (size_t)8 * num_modes * depth_limit * topk + (size_t)W * 7 + 16 + (size_t)num_modes * 4 + 64;
-    const bool reg_path = !single && depth_limit > 0 && budget > 0 && W <= 32 * tree::kRegNodesPerLane &&
-                          need <= 17 && reg_smem <= 220 * 1024;
     tree::Params p;
     p.lp = top_logp;
     p.ids = top_ids;
@@ -676,21 +646,18 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
     p.anc = anc_bits;
     p.vis = visibility;
     p.status = status;
-    if (reg_path) {
-        auto launch_reg = [&](auto kern) -> int {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)reg_smem);
-            if (e != cudaSuccess) {
-                set_error("mfd_build_trees: %s", cudaGetErrorString(e));
-                return MFD_ERR_CUDA;
-            }
-            kern<<<(unsigned)bs, tree::kThreads, reg_smem, (cudaStream_t)stream>>>(p);
-            MFD_CHECK_LAUNCH("mfd_build_trees");
-            return MFD_OK;
-        };
-        if (need <= 4) return launch_reg(tree::mixture_reg_kernel<4>);
-        if (need <= 8) return launch_reg(tree::mixture_reg_kernel<8>);
-        if (need <= 12) return launch_reg(tree::mixture_reg_kernel<12>);
-        return launch_reg(tree::mixture_reg_kernel<17>);
+    const size_t h1_smem = (size_t)16 * num_modes * W + (size_t)pl.hcap * 8 + (size_t)8 * num_modes * depth_limit * topk +
+                           (size_t)W * 7 + (size_t)num_modes * 4 + 160;
+    if (!single && depth_limit > 0 && budget > 0 && h1_smem <= 220 * 1024) {  // the mixture heap in one thread
+        cudaError_t e = cudaFuncSetAttribute(tree::mixture_heap1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)h1_smem);
+        if (e != cudaSuccess) {
+            set_error("mfd_build_trees: %s", cudaGetErrorString(e));
+            return MFD_ERR_CUDA;
+        }
+        tree::mixture_heap1_kernel<<<(unsigned)bs, tree::kThreads, h1_smem, (cudaStream_t)stream>>>(p);
+        MFD_CHECK_LAUNCH("mfd_build_trees");
+        return MFD_OK;
     }
     cudaError_t e = cudaFuncSetAttribute(tree::build_trees_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)pl.smem);
