@@ -10,17 +10,19 @@
 // the piece's sorted top-k keys (64-bit: orderable value, then the complement of the index).
 //
 // Streaming (the hot loop) is register-only and software pipelined: every thread keeps eight 16-byte
-// non-allocating loads in flight (each register slot is refilled from the next batch as soon as it is consumed), maintains an online (max, sum exp)
-// with a lazy rescale, and tests each vector's maximum against ONE floor per piece (a compare and a warp vote);
-// elements at or above the floor are appended, warp-aggregated, to a small per-warp buffer.  The floor comes
-// from the piece's first batch: each warp sorts its 32 lane maxima, the CTA merges them, and the floor is the
-// r-th largest lane maximum with r chosen so that about 2.5 k elements of the whole piece are expected to pass.
+// non-allocating loads in flight (the slots of a group are refilled from the next batch as soon as the group is
+// unpacked).  Per group of 32 elements a thread takes ONE maximum, tests it against ONE floor per piece, makes ONE
+// lazy-rescale check of its online (max, sum exp) and adds the 32 exponentials as a tree.  A thread whose group
+// reaches the floor (rare) appends those elements with shared atomics to the CTA's candidate buffer.  The floor
+// comes from the piece's first batch: each warp sorts its 32 lane maxima and the floor is the r-th largest over
+// the CTA, found by rank, with r chosen so that about 2.5 k elements of the whole piece are expected to pass.
 // That floor is speculative and is verified at the end of the piece: if at least k candidates were collected
-// (and no buffer overflowed), every element of the piece's top k is among them -- an element below the floor has
-// at least k collected elements above it.  Otherwise the piece is scanned again (an L2 hit) against a valid lower
-// bound, the minimum over warps of each warp's ceil(k/8)-th largest lane maximum (the minimum of >= k distinct
-// elements cannot exceed the k-th largest), so the result is exact either way.
-// At the end of a piece the candidates are sorted by 8 warps in parallel and combined by bitonic merges.
+// (and the buffer did not overflow), every element of the piece's top k is among them -- an element below the
+// floor has at least k collected elements above it.  Otherwise the piece is scanned again (an L2 hit) against a
+// valid lower bound, the minimum over warps of each warp's ceil(k/8)-th largest lane maximum (the minimum of >= k
+// distinct elements cannot exceed the k-th largest), so the result is exact either way.
+// At the end of a piece each warp sorts a chunk of the candidates and every key finds its rank by binary searches
+// in the other chunks; the keys ranked below k are the piece's sorted top k.
 #include "common.cuh"
 
 namespace mfd {
@@ -134,22 +136,18 @@ struct Params {
     unsigned int* tickets;  // [rows], zero between launches
 };
 
-constexpr int kWarpCap = 128;  // per-warp candidate buffer
 
 template <int KP>
 struct Smem {
     uint64_t cand[kCap];
-    uint64_t wbuf[kWarps][kWarpCap];
     uint64_t lists[kWarps][KP];
     uint64_t res[KP];
     float2 ms[kWarps];
     float wthr[kWarps];
-    int wcnt[kWarps];
     int count;
     int flag;
-    int overflow;
+    int spec;        // a speculative floor was found
     float floor_v;   // speculative floor (value)
-    float bound_v;   // valid lower bound (value)
     float logz;
 };
 
@@ -233,10 +231,22 @@ __device__ __forceinline__ void scan_piece(const char* base, int64_t c0, int64_t
     }
 }
 
-// CTA: the descending top KP (zero-padded) of the n keys in sm.cand into sm.res.  Each warp sorts a chunk of
-// 32*PER keys; the chunk lists combine by a tree of warp merges.
+// Number of keys greater than `key` in the descending list c[0..CH) (binary search; CH a power of two).
+template <int CH>
+__device__ __forceinline__ int count_greater(const uint64_t* c, uint64_t key) {
+    int pos = 0;
+#pragma unroll
+    for (int step = CH / 2; step > 0; step >>= 1)
+        if (c[pos + step - 1] > key) pos += step;
+    return pos + (c[pos] > key ? 1 : 0);
+}
+
+// CTA: the descending top KP (zero-padded) of the n distinct keys in sm.cand into sm.res.  Each warp sorts a
+// chunk of 32*PER keys in registers and writes it back sorted; a key's rank is its position in its own chunk
+// plus, for every other chunk, the number of keys there above it (a binary search).  Keys ranked below KP are
+// stored at their rank.
 template <int KP, int PER>
-__device__ __forceinline__ void select_chunks(Smem<KP>& sm, int n) {
+__device__ __forceinline__ void select_rank(Smem<KP>& sm, int n) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int CH = 32 * PER;
     uint64_t r[PER];
@@ -246,41 +256,37 @@ __device__ __forceinline__ void select_chunks(Smem<KP>& sm, int n) {
         r[j] = e < n ? sm.cand[e] : 0ull;
     }
     warp_sort_desc<PER>(r);
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < KP / 32; ++j) sm.lists[warp][j * 32 + lane] = j < PER ? r[j < PER ? j : 0] : 0ull;
+    for (int j = 0; j < PER; ++j) sm.cand[warp * CH + j * 32 + lane] = r[j];
+    for (int e = threadIdx.x; e < KP; e += kThreads)
+        if (e >= n) sm.res[e] = 0ull;
     __syncthreads();
 #pragma unroll
-    for (int span = 1; span < kWarps; span <<= 1) {
-        if ((warp % (2 * span)) == 0) warp_merge_lists<KP>(sm.lists[warp], sm.lists[warp + span], sm.lists[warp]);
-        __syncthreads();
+    for (int j = 0; j < PER; ++j) {
+        if (j * 32 >= KP) break;  // own position alone already >= KP
+        const uint64_t key = r[j];
+        if (key == 0ull) continue;
+        int rank = j * 32 + lane;
+#pragma unroll
+        for (int w2 = 0; w2 < kWarps; ++w2)
+            if (w2 != warp) rank += count_greater<CH>(sm.cand + w2 * CH, key);
+        if (rank < KP) sm.res[rank] = key;
     }
-    for (int e = threadIdx.x; e < KP; e += kThreads) sm.res[e] = sm.lists[0][e];
     __syncthreads();
 }
 
 template <int KP>
 __device__ __noinline__ void select_topk(Smem<KP>& sm, int n) {
     if (n <= kWarps * 32) {
-        select_chunks<KP, 1>(sm, n);
+        select_rank<KP, 1>(sm, n);
     } else if (n <= kWarps * 64) {
-        select_chunks<KP, 2>(sm, n);
+        select_rank<KP, 2>(sm, n);
     } else if (n <= kWarps * 128) {
-        select_chunks<KP, 4>(sm, n);
+        select_rank<KP, 4>(sm, n);
     } else {
-        select_chunks<KP, 8>(sm, n);  // n <= kCap = 2048
+        select_rank<KP, 8>(sm, n);  // n <= kCap = 2048
     }
-}
-
-// Append key if `take`; warp-aggregated slot, the caller guarantees room.
-__device__ __forceinline__ void cta_append(int* count, uint64_t* cand, bool take, uint64_t key) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t bal = __ballot_sync(MFD_FULL_MASK, take);
-    if (!bal) return;
-    const int leader = __ffs(bal) - 1;
-    int base = 0;
-    if (lane == leader) base = atomicAdd(count, __popc(bal));
-    base = __shfl_sync(MFD_FULL_MASK, base, leader);
-    if (take) cand[base + __popc(bal & ((1u << lane) - 1u))] = key;
 }
 
 template <int KP>
@@ -298,8 +304,10 @@ __device__ __forceinline__ void write_outputs(const Params& p, int64_t row, cons
     if (threadIdx.x == 0 && p.logz) p.logz[row] = logz;
 }
 
-// Rare: scan the piece for every element at or above the value floor `vf` (then every key above the running
-// k-th best) into sm.cand and select; repeated with the improved k-th best while more than kCap keys qualify.
+// Rare: scan the piece for every element at or above the value floor `vf` (then every key at or above the
+// running k-th best) into sm.cand and select; repeated with the improved k-th best while more than kCap keys
+// qualify.  The k-th best of kCap qualifying keys is itself a key of the piece, so at least k keys are at or above
+// it; when every one of a full buffer's keys qualifies again, its k-th best is strictly higher, so the loop ends.
 template <int KP, bool BF16>
 __device__ __noinline__ void rescan_select(Smem<KP>& sm, const char* base, int64_t c0, int64_t c1, float vf,
                                            int k) {
@@ -314,7 +322,7 @@ __device__ __noinline__ void rescan_select(Smem<KP>& sm, const char* base, int64
             for (int e = 0; e < VE; ++e) {
                 if (e < live && x[e] >= vf) {
                     const uint64_t key = topk_key(x[e], col0 + e);
-                    if (key > thr) {
+                    if (key >= thr) {
                         const int slot = atomicAdd(&sm.count, 1);
                         if (slot < kCap) sm.cand[slot] = key;
                         else overflow = 1;
@@ -353,9 +361,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         constexpr int kBatch = kThreads * kLoads;  // vectors per batch
         float m = -INFINITY, mL = -INFINITY, s = 0.f;
         float lmax = -INFINITY;  // lane maximum over the head/tail scalar and the first batch
-        int wcnt = 0;            // this warp's buffered candidates (warp-uniform)
-        bool wover = false;      // this warp's buffer overflowed
-        uint64_t* wb = sm.wbuf[warp];
         int64_t hb = c0;
         {
             const uintptr_t ad = (uintptr_t)(base + c0 * ES);
@@ -368,18 +373,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         const uint4* vb = (const uint4*)(base + hb * ES);
         const int64_t nbatch = (nvec + kBatch - 1) / kBatch;
         // warp-aggregated append of the elements of x[0..live) at or above fl
+        // append the elements of x[0..live) at or above fl to the CTA's candidates (a lane that has some works
+        // alone: shared atomics, no warp collective; a count past kCap marks the overflow)
         auto offer = [&](const float (&x)[VE], uint32_t col0, int live, float fl) {
 #pragma unroll
             for (int e = 0; e < VE; ++e) {
-                const bool take = e < live && x[e] >= fl;
-                const uint32_t bal = __ballot_sync(MFD_FULL_MASK, take);
-                if (bal) {
-                    const int slot = wcnt + __popc(bal & ((1u << lane) - 1u));
-                    if (take && slot < kWarpCap) wb[slot] = topk_key(x[e], col0 + e);
-                    wcnt += __popc(bal);
+                if (e < live && x[e] >= fl) {
+                    const int slot = atomicAdd(&sm.count, 1);
+                    if (slot < kCap) sm.cand[slot] = topk_key(x[e], col0 + e);
                 }
             }
-            if (wcnt > kWarpCap) wover = true;
         };
         // head/tail scalar of this thread
         float xs[VE];
@@ -418,42 +421,45 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
                 }
             }
         }
-        // floors: each warp sorts its lane maxima; the speculative floor is the r-th largest over the CTA and the
-        // valid bound the minimum over warps of each warp's ceil(k/8)-th largest
+        float bv = -INFINITY, fl = -INFINITY;
+        // floors: each warp sorts its lane maxima (made distinct by the thread index); the speculative floor is the
+        // r-th largest over the CTA (found by rank, as in select_rank) and the valid bound the minimum over warps of
+        // each warp's ceil(k/8)-th largest
         {
             const int64_t sample = min(nvec, (int64_t)kBatch) * VE + (hb - c0) + (c1 - tb);
             const int64_t np = c1 - c0;
             int r = (int)((5LL * k * sample + 2 * np - 1) / (2 * np));
             r = max(r, 1);
-            uint64_t r1[1] = {(uint64_t)ord_f32(lmax) << 32};
+            uint64_t r1[1] = {((uint64_t)ord_f32(lmax) << 32) | (uint64_t)(~(uint32_t)threadIdx.x)};
             warp_sort_desc<1>(r1);
             const int q = (k + kWarps - 1) / kWarps;
             const uint64_t qth = shfl_u64(r1[0], q - 1);
             if (lane == 0) sm.wthr[warp] = unord_f32((uint32_t)(qth >> 32));
-            // the warp's sorted lane maxima as a list of KP (zero padded) for the CTA merge
-#pragma unroll
-            for (int j = 0; j < KP / 32; ++j) sm.lists[warp][j * 32 + lane] = j == 0 ? r1[0] : 0ull;
-            __syncthreads();
-#pragma unroll
-            for (int span = 1; span < kWarps; span <<= 1) {
-                if ((warp % (2 * span)) == 0) warp_merge_lists<KP>(sm.lists[warp], sm.lists[warp + span], sm.lists[warp]);
-                __syncthreads();
-            }
+            sm.cand[threadIdx.x] = r1[0];  // (the candidate buffer is free until the floors are known)
             if (threadIdx.x == 0) {
-                float bv = INFINITY;
-                for (int w = 0; w < kWarps; ++w) bv = fminf(bv, sm.wthr[w]);
-                sm.bound_v = bv;
-                // r-th largest lane maximum; r beyond the list (or beyond the lanes) -> no speculation
-                sm.floor_v = (r <= KP && r <= kThreads && sm.lists[0][r - 1] != 0ull)
-                                 ? fmaxf(bv, unord_f32((uint32_t)(sm.lists[0][r - 1] >> 32)))
-                                 : bv;
-                sm.overflow = 0;
+                sm.spec = 0;
+                sm.count = 0;
             }
             __syncthreads();
+            if (r <= kThreads) {
+                int rank = lane;
+#pragma unroll
+                for (int w2 = 0; w2 < kWarps; ++w2)
+                    if (w2 != warp) rank += count_greater<32>(sm.cand + w2 * 32, r1[0]);
+                if (rank == r - 1) {
+                    sm.floor_v = unord_f32((uint32_t)(r1[0] >> 32));
+                    sm.spec = 1;
+                }
+            }
+            __syncthreads();
+            bv = sm.wthr[0];
+#pragma unroll
+            for (int w2 = 1; w2 < kWarps; ++w2) bv = fminf(bv, sm.wthr[w2]);
+            fl = sm.spec ? fmaxf(bv, sm.floor_v) : bv;
+            __syncthreads();  // every thread has read the floors (and the buffer is free for candidates)
         }
-        const float fl = sm.floor_v;
         // the head/tail scalar and the first batch against the floor
-        offer(xs, (uint32_t)(cs >= 0 ? cs : 0), cs >= 0 ? 1 : 0, fl);
+        if (cs >= 0 && xs[0] >= fl) offer(xs, (uint32_t)cs, 1, fl);
         if (nbatch > 0) {
 #pragma unroll
             for (int u = 0; u < kLoads; ++u) {
@@ -463,26 +469,86 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
                 float mx = x[0];
 #pragma unroll
                 for (int e = 1; e < VE; ++e) mx = fmaxf(mx, x[e]);
-                if (__any_sync(MFD_FULL_MASK, vi < nvec && mx >= fl)) offer(x, (uint32_t)(hb + vi * VE), vi < nvec ? VE : 0, fl);
+                if (vi < nvec && mx >= fl) offer(x, (uint32_t)(hb + vi * VE), VE, fl);
                 const int64_t vn = vi + kBatch;  // the next batch's vector into the freed slot
                 if (vn < nvec) w[u] = ldg_stream_u4(vb + vn);
             }
         }
-        // the remaining batches, each slot refilled from two batches ahead as it is consumed
+        // the remaining batches, in groups of 32 elements per thread (the whole batch in float32, half of it in
+        // bf16): a group's vectors are unpacked and their slots refilled with the next batch at once, then ONE
+        // maximum, ONE floor test, ONE lazy-rescale check and a tree sum of the exponentials per group
+        constexpr int kGroup = 32 / VE;  // vectors per group
+        static_assert(kLoads % kGroup == 0, "whole groups per batch");
+        const int64_t nfull = nvec / kBatch;
+        const uint4* pb = vb + threadIdx.x;
         for (int64_t bt = 1; bt < nbatch; ++bt) {
+            pb += kBatch;
+            const bool full = bt < nfull, next_full = bt + 1 < nfull;
 #pragma unroll
-            for (int u = 0; u < kLoads; ++u) {
-                const int64_t vi = bt * kBatch + (int64_t)u * kThreads + threadIdx.x;
-                const bool ok = vi < nvec;
-                float x[VE];
-                unpack<BF16>(w[u], x);
-                const int64_t vn = vi + kBatch;
-                if (vn < nvec) w[u] = ldg_stream_u4(vb + vn);
-                float mx = x[0];
+            for (int g0 = 0; g0 < kLoads; g0 += kGroup) {
+                float x[kGroup][VE];
 #pragma unroll
-                for (int e = 1; e < VE; ++e) mx = fmaxf(mx, x[e]);
-                if (ok) lse_vec<VE>(m, mL, s, x, mx);
-                if (__any_sync(MFD_FULL_MASK, ok && mx >= fl)) offer(x, (uint32_t)(hb + vi * VE), ok ? VE : 0, fl);
+                for (int u = 0; u < kGroup; ++u) unpack<BF16>(w[g0 + u], x[u]);
+#pragma unroll
+                for (int u = 0; u < kGroup; ++u) {
+                    const int uu = g0 + u;
+                    if (next_full || (bt + 1) * kBatch + uu * kThreads + threadIdx.x < nvec)
+                        w[uu] = ldg_stream_u4(pb + kBatch + uu * kThreads);
+                }
+                if (!full) {  // vectors past the piece read as -inf
+#pragma unroll
+                    for (int u = 0; u < kGroup; ++u)
+                        if (bt * kBatch + (g0 + u) * kThreads + threadIdx.x >= nvec) {
+#pragma unroll
+                            for (int e = 0; e < VE; ++e) x[u][e] = -INFINITY;
+                        }
+                }
+                float vm[kGroup];
+#pragma unroll
+                for (int u = 0; u < kGroup; ++u) {
+                    float t[VE];
+#pragma unroll
+                    for (int e = 0; e < VE; ++e) t[e] = x[u][e];
+#pragma unroll
+                    for (int h = VE / 2; h > 0; h >>= 1)
+#pragma unroll
+                        for (int e = 0; e < h; ++e) t[e] = fmaxf(t[e], t[e + h]);
+                    vm[u] = t[0];
+                }
+                float bmx = vm[0];
+#pragma unroll
+                for (int u = 1; u < kGroup; ++u) bmx = fmaxf(bmx, vm[u]);
+                if (bmx >= fl) {  // rare; vectors past the piece are excluded explicitly (fl may be -inf)
+#pragma unroll
+                    for (int u = 0; u < kGroup; ++u) {
+                        const int64_t vi = bt * kBatch + (int64_t)(g0 + u) * kThreads + threadIdx.x;
+                        if (vi < nvec && vm[u] >= fl) offer(x[u], (uint32_t)(hb + vi * VE), VE, fl);
+                    }
+                }
+                if (bmx > m) {
+                    s = (m == -INFINITY) ? 0.f : s * fast_exp2((m - bmx) * kLog2e);
+                    m = bmx;
+                    mL = bmx * kLog2e;
+                }
+                if (m != -INFINITY) {
+                    float acc[kGroup];
+#pragma unroll
+                    for (int u = 0; u < kGroup; ++u) {
+                        float t[VE];
+#pragma unroll
+                        for (int e = 0; e < VE; ++e) t[e] = fast_exp2(__fmaf_rn(x[u][e], kLog2e, -mL));
+#pragma unroll
+                        for (int h = VE / 2; h > 0; h >>= 1)
+#pragma unroll
+                            for (int e = 0; e < h; ++e) t[e] += t[e + h];
+                        acc[u] = t[0];
+                    }
+#pragma unroll
+                    for (int h = kGroup / 2; h > 0; h >>= 1)
+#pragma unroll
+                        for (int u = 0; u < h; ++u) acc[u] += acc[u + h];
+                    s += acc[0];
+                }
             }
         }
 
@@ -495,25 +561,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
                 const float s2 = __shfl_xor_sync(MFD_FULL_MASK, ss, o);
                 lse_merge(mm, ss, m2, s2);
             }
-            if (lane == 0) {
-                sm.ms[warp] = make_float2(mm, ss);
-                sm.wcnt[warp] = wcnt < kWarpCap ? wcnt : kWarpCap;
-                if (wover) sm.overflow = 1;
-            }
+            if (lane == 0) sm.ms[warp] = make_float2(mm, ss);
         }
         __syncthreads();
 
-        // ---- gather the warp buffers; verify the speculative floor; select the top KP
-        int n = 0, off = 0;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            if (w < warp) off += sm.wcnt[w];
-            n += sm.wcnt[w];
-        }
-        for (int i = lane; i < sm.wcnt[warp]; i += 32) sm.cand[off + i] = wb[i];
-        __syncthreads();
-        if (sm.overflow || n < k) {
-            rescan_select<KP, BF16>(sm, base, c0, c1, sm.bound_v, k);
+        // ---- verify the speculative floor; select the top KP
+        const int cnt = sm.count;
+        const int n = cnt < kCap ? cnt : kCap;
+        __syncthreads();  // every thread has read the count before the selection may reset it
+        if (cnt > kCap || n < k) {
+            rescan_select<KP, BF16>(sm, base, c0, c1, bv, k);
         } else {
             select_topk<KP>(sm, n);
         }

@@ -41,6 +41,46 @@ def test_topk_logz_vs_oracle(dtype, R, V, k):
     np.testing.assert_allclose(top.cpu().numpy(), ref_lp, rtol=0, atol=8e-6)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("pattern", ["constant", "two_levels", "first_batch_high", "ascending", "few_values"])
+def test_topk_adversarial_rows(dtype, pattern):
+    """Rows that defeat the speculative floor: every element passes it (constant and tie-heavy rows overflow the
+    candidate buffer, so the piece is rescanned with a raised key threshold, twice when ties fill it again), or the
+    first batch overstates the row (too few candidates, rescan against the valid bound).  Ties order by index."""
+    from mfd_b200 import ops
+    R, V, k = 24, 151936, 64
+    g = torch.Generator().manual_seed(11)
+    if pattern == "constant":
+        x = torch.full((R, V), 0.5)
+    elif pattern == "two_levels":
+        x = (torch.rand(R, V, generator=g) < 0.3).float()
+    elif pattern == "first_batch_high":
+        x = torch.randn(R, V, generator=g)
+        x[:, :9000] += 8.0
+    elif pattern == "ascending":
+        x = torch.linspace(-4, 4, V).repeat(R, 1)
+    else:
+        x = torch.randint(0, 6, (R, V), generator=g).float() * 0.25
+    x = x.to(dtype)
+    top, ids, lz = ops.topk_logz(x.to(DEV), k)
+    ref_lp, ref_ids, ref_lz = oracle.topk_logz(x.float().numpy(), k)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    np.testing.assert_allclose(lz.cpu().numpy(), ref_lz, rtol=0, atol=4e-6 * max(1.0, float(np.abs(ref_lz).max()) / 8))
+    np.testing.assert_allclose(top.cpu().numpy(), ref_lp, rtol=0, atol=8e-6)
+
+
+def test_topk_repeatable_at_batch_size():
+    """The bench's logits-step size (4096 rows): two calls give identical ids and log Z."""
+    from mfd_b200 import ops
+    x = torch.randn(4096, V0, generator=torch.Generator(device=DEV).manual_seed(5), device=DEV)
+    a = [t.clone() for t in ops.topk_logz(x, 64, ids_dtype=torch.int32)]
+    b = ops.topk_logz(x, 64, ids_dtype=torch.int32)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2]) and torch.equal(a[0], b[0])
+    rows = torch.arange(0, 4096, 97)
+    ref_lp, ref_ids, _ = oracle.topk_logz(x[rows].cpu().numpy(), 64)
+    assert np.array_equal(a[1][rows].cpu().numpy(), ref_ids)
+
+
 def test_topk_strided_rows_and_int32_ids():
     from mfd_b200 import ops
     g = torch.Generator().manual_seed(3)
