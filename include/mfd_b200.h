@@ -146,7 +146,9 @@ int mfd_verify_inputs(const int64_t* root_tokens, const int64_t* prefix_lens, co
  *           598-605); SGLang's flashinfer custom-mask prefill (patch:86-142, 558-592); with a block-diagonal
  *           visibility, the drafter's mode_block_attention (inference/hf/mode_attention.py:120-150).
  * Workspace: mfd_tree_attention_workspace(bs, n, H, Hkv, splits) bytes, zeroed before its first use (its ticket
- * words return to zero after every call).
+ * words return to zero after every call).  Its first int32 (at the 256-byte aligned base) is a sticky device status:
+ * 1 once a bounded wait in the kernel gave up, 2 if a CTA's shared-memory base was misaligned beyond the slack it
+ * reserves (that CTA did no work); the caller reads and clears it.
  */
 size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads, int64_t splits);
 int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int64_t sq_h, const void* k, int64_t sk_b,

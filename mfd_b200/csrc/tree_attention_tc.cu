@@ -6,23 +6,25 @@
 //
 // Rows: the G query heads sharing a KV head are packed as r = node * G + g (260 rows for 65 nodes x 4 heads), so
 // a key tile feeds G x n rows.  One CTA per (request, KV head, key split, 128-row M-tile); the M-tiles of one
-// split are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.
+// split are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.  With per-request prefix
+// lengths (up to 64 requests) the CTAs of the longest requests are launched first, so the short ones fill the tail.
 //
-// Warp roles (192 threads):
-//   warp 0      TMA producer: Q once, then 64-key K and V tiles into a 4-stage ring (128-byte swizzle, the
-//               canonical UMMA K-major / MN-major layouts; no multicast)
-//   warp 1      MMA issuer: S[i%2] = Q K_i^T (M=128, N=64, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
-//               (M=128, N=128, K=16 x 4, V MN-major), so the scores of tile i are computed while the softmax
-//               works on tile i-1's probabilities
-//   warps 2..9  softmax: the two warps of TMEM lane quarter q each take 32 of a row's 64 key columns (row max
-//               and sum exchanged through shared memory): tcgen05.ld of S, mask (only tiles reaching the tree keys
-//               or the split end), exp2, bf16 P written back over S in TMEM; lazy O rescale in TMEM
-//               only when a row's running max grows by more than 2^8; epilogue through a shared-memory stage so
-//               every store is coalesced.
+// Warp roles (576 threads):
+//   warp 0       TMA producer: Q once, then 128-key K and V tiles into a 3-stage ring (128-byte swizzle, the
+//                canonical UMMA K-major / MN-major layouts; no multicast)
+//   warp 1       MMA issuer: S[i%2] = Q K_i^T (M=128, N=128, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
+//                (M=128, N=128, K=16 x 8, A = P read from TMEM, V MN-major), so the scores of tile i are computed
+//                while the softmax works on tile i-1
+//   warps 2..17  softmax: the four warps of TMEM lane quarter q each take 32 of a tile's 128 key columns (row max
+//                and, at the end, row sum exchanged through shared memory): tcgen05.ld of S, mask (only tiles
+//                reaching the tree keys or the split end), exp2, bf16 P written back over S in TMEM; lazy O rescale
+//                in TMEM only when a row's running max grows by more than 2^8.  A quarter whose 32 rows are all
+//                padding (the last M-tile holds 4 of 128 rows for 65 x 4) keeps only the barrier protocol.
+//                Epilogue through a shared-memory stage so every store is coalesced.
 // Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
 // merges all splits and writes bf16 out.  With one split the CTA writes out directly.
 //
-// TMEM: O at columns [0, 128), S[0] at [128, 192), S[1] at [192, 256).  Every mbarrier wait is bounded; when one
+// TMEM: O at columns [0, 128), S[0] at [128, 256), S[1] at [256, 384).  Every mbarrier wait is bounded; when one
 // gives up the CTA records a nonzero status, finishes without waiting further, and still releases its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -36,7 +38,9 @@ constexpr int D = 128;
 constexpr int kM = 128;        // rows per CTA (one M-tile)
 constexpr int kKt = 128;       // keys per tile
 constexpr int kStages = 3;     // K/V ring depth
-constexpr int kThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2..9 softmax
+constexpr int kParts = 4;      // softmax warps per TMEM lane quarter, each taking 32 of a tile's 128 key columns
+constexpr int kSoftmaxThreads = 128 * kParts;
+constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, warps 2..17 softmax
 constexpr int kTmemCols = 512;
 constexpr int kSCol = 128;     // S[b] at column kSCol + 128 b; P[b] (bf16 pairs) over its first 64 columns
 
@@ -45,9 +49,15 @@ constexpr int kKVBytes = kKt * D * 2;  // 32 KB: [2 d-halves][128 keys][128 B]
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kQBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
-constexpr int kOffX = kOffV + kStages * kKVBytes;  // row maxima / sums exchanged by the two halves of a row
-constexpr int kOffBar = kOffX + 2 * kM * 4;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers, TMEM address, flags, 1024-byte alignment slack
+constexpr int kOffX = kOffV + kStages * kKVBytes;  // row maxima / sums exchanged by the column parts of a row
+constexpr int kOffBar = kOffX + kParts * kM * 4;
+constexpr int kSmemUsed = kOffBar + 128;            // + barriers, TMEM address, flags
+constexpr int kSmemMax = 227 * 1024;                // the per-block opt-in maximum
+// the 128-byte-swizzled TMA destinations need a 1024-byte aligned base: the slack that fits is reserved and the
+// kernel checks at entry that the base's misalignment is within it
+constexpr int kSmemSlack = kSmemMax - kSmemUsed < 1024 ? kSmemMax - kSmemUsed : 1024;
+constexpr int kSmemBytes = kSmemUsed + kSmemSlack;
+static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemMax, "shared memory");
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
 
 struct Params {
@@ -104,6 +114,14 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
@@ -155,9 +173,22 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
 }
-// named barriers: 1 = the 256 softmax threads, 2 + q = the two warps of TMEM lane quarter q
-__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-__device__ __forceinline__ void pair_sync(int quarter) { asm volatile("bar.sync %0, 64;" ::"r"(2 + quarter) : "memory"); }
+// named barriers: 1 = the softmax threads, 2 + q = the kParts warps of TMEM lane quarter q
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory"); }
+__device__ __forceinline__ void quarter_sync(int quarter) {
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + quarter), "n"(32 * kParts) : "memory");
+}
+// the same barrier, returning the AND of v over the quarter's threads (so its warps leave a loop together)
+__device__ __forceinline__ bool quarter_sync_and(int quarter, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.b32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(2 + quarter), "n"(32 * kParts)
+        : "memory");
+    return r != 0u;
+}
 
 
 // barrier slots
@@ -171,11 +202,40 @@ enum {
     kNumBars = kBarPV + 2
 };
 
+// The request whose prefix is the z-th longest (ties by request index), so that the longest requests' CTAs are
+// launched first and the shortest fill the tail.  Every warp computes it (lane j ranks requests j, j + 32, ...);
+// used for up to kMaxOrdered requests with per-request prefix lengths, otherwise request z.
+constexpr int kMaxOrdered = 64;
+__device__ __forceinline__ int request_by_length_rank(const int32_t* prefix, int bs, int z) {
+    const int lane = threadIdx.x & 31;
+    int found = z;
+    for (int c0 = 0; c0 < bs; c0 += 32) {
+        const int me = c0 + lane;
+        int rank = -1;
+        if (me < bs) {
+            const int lm = __ldg(prefix + me);
+            rank = 0;
+            for (int o = 0; o < bs; ++o) {
+                const int lo = __ldg(prefix + o);
+                rank += (lo > lm || (lo == lm && o < me)) ? 1 : 0;
+            }
+        }
+        const uint32_t hit = __ballot_sync(MFD_FULL_MASK, rank == z);
+        if (hit) found = c0 + __ffs(hit) - 1;
+    }
+    return found;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const Params p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
+    if (pad > (uint32_t)kSmemSlack) {  // (uniform: before any barrier, copy or TMEM use)
+        if (threadIdx.x == 0 && p.status) atomicExch(p.status, 2);
+        return;
+    }
+    unsigned char* smem = smem_raw + pad;
     const uint32_t sbase = smem_addr(smem);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8 * kNumBars);
@@ -183,7 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int split = blockIdx.x / p.mtiles, mtile = blockIdx.x % p.mtiles;
-    const int hk = blockIdx.y, b = blockIdx.z;
+    const int hk = blockIdx.y;
+    const int b = (p.prefix && p.bs > 1 && p.bs <= kMaxOrdered)
+                      ? request_by_length_rank(p.prefix, p.bs, (int)blockIdx.z)
+                      : (int)blockIdx.z;
     const int nrows = p.n * p.G;
     const int row0 = mtile * kM;
     const int prefix = p.prefix ? p.prefix[b] : p.prefix_const;
@@ -196,7 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // barriers and the first loads before anything else, so the TMA round trip overlaps the TMEM allocation
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kNumBars; ++i) mbar_init(&bars[i], (i >= kBarPFull && i < kBarPV) ? 8u : 1u);
+        for (int i = 0; i < kNumBars; ++i)
+            mbar_init(&bars[i], (i >= kBarPFull && i < kBarPV) ? (uint32_t)(4 * kParts) : 1u);
         *shared_flag = 0;
         mbar_fence_init();
     }
@@ -277,83 +341,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------------------------------------------------------- softmax warps
-        // warp w (2..9): TMEM lane quarter w % 4, key half (w - 2) / 4 of each 128-key tile; the two warps of a
-        // quarter exchange their row maxima (and at the end their row sums) through shared memory
+        // warp w (2..17): TMEM lane quarter w % 4, key columns [32 part, 32 part + 32) of each 128-key tile with
+        // part = (w - 2) / 4; the kParts warps of a quarter exchange their row maxima (and at the end their row
+        // sums) through shared memory
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int part = (warp - 2) >> 2;
         const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
         const int r = row0 + rt;             // packed row
         const bool live = r < nrows;
         const int node = live ? r / p.G : 0;
         const uint64_t* anc_row = p.anc + ((size_t)b * p.n + node) * p.words;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-        float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [2 halves][128 rows]
-        const int c_lo = half * 64;  // this warp's 64 of the tile's 128 key columns
+        float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [kParts][128 rows]
+        const int c_lo = part * 32;  // this warp's 32 of the tile's 128 key columns
         const float sc = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
+        // a quarter whose 32 rows are all padding keeps only the barrier protocol: it leaves its TMEM rows as they
+        // are, and the P V rows they feed (rows are independent in the MMA) are never stored
+        const bool quarter_live = row0 + quarter * 32 < nrows;
         for (int i = 0; i < ntiles; ++i) {
             const int bi = i & 1;
             const int key0 = k_lo + i * kKt;
             const uint32_t s_tm = tmem + lane_off + kSCol + bi * kKt;
             ok &= mbar_wait(&bars[kBarSFull + bi], (i >> 1) & 1, kTries);
             tc_fence_after();
-            float s[64];
-            {
-                float t0[32], t1[32];
-                tmem_ld32(s_tm + c_lo, t0);
-                tmem_ld32(s_tm + c_lo + 32, t1);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    s[j] = t0[j];
-                    s[32 + j] = t1[j];
-                }
+            if (!quarter_live) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
+                if (!__all_sync(MFD_FULL_MASK, ok)) break;
+                continue;
             }
-            float mx;
+            float s[32];
+            tmem_ld32(s_tm + c_lo, s);
             const bool fast = key0 + kKt <= prefix && key0 + kKt <= k_hi;
-            if (fast) {
-                // prefix keys only, all visible: no mask (padding rows compute finite values that are never stored)
-                mx = s[0];
-#pragma unroll
-                for (int j = 1; j < 64; ++j) mx = fmaxf(mx, s[j]);
-                mx *= sc;
-#pragma unroll
-                for (int j = 0; j < 64; ++j) s[j] *= sc;
-            } else {
-                // visibility of this thread's 64 keys as one bitmask: prefix keys, then the row's ancestor bits
-                // for the tree keys (two bitset words funnel-shifted into place), all cut at the split end
-                const int kb = key0 + c_lo;           // first key of this half
-                const int t0 = kb - prefix;           // its tree index (negative: prefix keys come first)
+            if (!fast) {
+                // visibility of this thread's 32 keys as a bitmask: prefix keys, then the row's ancestor bits for
+                // the tree keys (two bitset words funnel-shifted into place), all cut at the split end
+                const int kb = key0 + c_lo;  // first key of this part
+                const int t0 = kb - prefix;  // its tree index (negative: prefix keys come first)
                 uint64_t vis;
                 if (t0 <= -64) {
                     vis = ~0ull;
                 } else {
-                    const int w = t0 >> 6;            // floor division: word holding tree index t0 (t0 >= -63)
+                    const int w = t0 >> 6;  // floor division: word holding tree index t0 (t0 >= -63)
                     const int sh = t0 & 63;
                     const uint64_t lo = (w >= 0 && w < p.words) ? __ldg(anc_row + w) : 0ull;
                     const uint64_t hi = (w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull;
                     uint64_t tree = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;  // bit j: tree index t0 + j
                     if (t0 < 0) {  // the first -t0 keys are prefix keys
                         const int np = -t0;
-                        tree = ((w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull) << np;
+                        tree = hi << np;
                         vis = tree | ((1ull << np) - 1ull);
                     } else {
                         vis = tree;
                     }
                 }
-                const int live_keys = k_hi - kb;      // keys of this half before the split end
-                if (live_keys < 64) vis &= live_keys <= 0 ? 0ull : ((1ull << live_keys) - 1ull);
-                mx = -INFINITY;
+                const int live_keys = k_hi - kb;  // keys of this part before the split end
+                if (live_keys < 32) vis &= live_keys <= 0 ? 0ull : ((1ull << live_keys) - 1ull);
 #pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    s[j] = ((vis >> j) & 1ull) ? s[j] * sc : -INFINITY;
-                    mx = fmaxf(mx, s[j]);
-                }
+                for (int j = 0; j < 32; ++j) s[j] = ((vis >> j) & 1ull) ? s[j] : -INFINITY;
             }
-            // the row's max over both halves (both halves have finished reading S[bi] after this barrier, so P
-            // may overwrite it)
-            xmax[half * kM + rt] = mx;
-            pair_sync(quarter);
-            mx = fmaxf(mx, xmax[(half ^ 1) * kM + rt]);
+            float mx;
+            {  // the raw scores' maximum as a tree (scaling by sc > 0 keeps the order: max(s) * sc = max(s * sc))
+                float t[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) t[j] = fmaxf(s[j], s[j + 16]);
+#pragma unroll
+                for (int h = 8; h > 0; h >>= 1)
+#pragma unroll
+                    for (int j = 0; j < h; ++j) t[j] = fmaxf(t[j], t[j + h]);
+                mx = t[0] * sc;
+            }
+            // the row's max over the parts (every part has finished reading S[bi] after this barrier, so P may
+            // overwrite it)
+            xmax[part * kM + rt] = mx;
+            quarter_sync(quarter);
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[q * kM + rt]);
             float alpha = 1.f;
             bool rescale = false;
             if (mx > m_run + 8.f) {  // lazy: keep the running max unless the tile's exceeds it by more than 2^8
@@ -364,56 +429,61 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m_run = mx;
             }
             const float mref = m_run == -INFINITY ? 0.f : m_run;  // nothing visible yet: every p is 0
-            float rs = 0.f;
-            uint32_t pk[32];
+            uint32_t pk[16];
+            float ps[4];  // independent partial row sums
 #pragma unroll
-            for (int j = 0; j < 64; j += 2) {
-                const float p0 = fast_exp2(s[j] - mref);
-                const float p1 = fast_exp2(s[j + 1] - mref);
-                rs += p0 + p1;
+            for (int j = 0; j < 4; ++j) ps[j] = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float p0 = fast_exp2(__fmaf_rn(s[j], sc, -mref));
+                const float p1 = fast_exp2(__fmaf_rn(s[j + 1], sc, -mref));
+                ps[(j >> 1) & 3] += p0 + p1;
                 pk[j >> 1] = pack_bf16(p0, p1);
             }
-            l_run = l_run * alpha + rs;
-            const bool any_rescale = __any_sync(MFD_FULL_MASK, rescale);
-            if (any_rescale) {  // O must hold the P V of tile i-1; this half rescales O columns [64 half, +64)
+            l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+            if (__any_sync(MFD_FULL_MASK, rescale)) {  // O must hold the P V of tile i-1; this part rescales O
+                                                       // columns [32 part, +32)
                 if (i >= 1) {
                     ok &= mbar_wait(&bars[kBarPV + (bi ^ 1)], ((i - 1) >> 1) & 1, kTries);
                     tc_fence_after();
                 }
-                for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-                    float o[32];
-                    tmem_ld32(tmem + lane_off + c0, o);
+                float o[32];
+                tmem_ld32(tmem + lane_off + c_lo, o);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) o[j] *= alpha;
-                    tmem_st32(tmem + lane_off + c0, o);
-                }
+                for (int j = 0; j < 32; ++j) o[j] *= alpha;
+                tmem_st32(tmem + lane_off + c_lo, o);
             }
-            // P(i) as bf16 pairs over the first 64 columns of S[bi]: this half's 64 keys = 32 columns
-            tmem_st32u(s_tm + half * 32, pk);
+            // P(i) as bf16 pairs over the first 64 columns of S[bi]: this part's 32 keys = 16 columns
+            tmem_st16u(s_tm + part * 16, pk);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
-            if (!__all_sync(MFD_FULL_MASK, ok)) break;
+            // the next tile's maxima may be written only after every part has read these; a failed wait anywhere
+            // in the quarter ends the loop for all its warps
+            ok = quarter_sync_and(quarter, ok);
+            if (!ok) break;
         }
         if (ntiles > 0 && ok) {  // the last P V (every earlier one completed before it)
             ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
             tc_fence_after();
         }
-        // ---- epilogue: the row sum over both halves, then this half's 64 columns of O / l
-        pair_sync(quarter);  // both halves are past their last use of xmax
-        xmax[half * kM + rt] = l_run;
-        pair_sync(quarter);
-        const float l_row = l_run + xmax[(half ^ 1) * kM + rt];
+        // ---- epilogue: the row sum over the parts, then this part's 32 columns of O / l
+        quarter_sync(quarter);  // every part is past its last use of xmax
+        xmax[part * kM + rt] = l_run;
+        quarter_sync(quarter);
+        float l_row = 0.f;
+#pragma unroll
+        for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
         const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
         const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
         // staging of bf16 rows for coalesced stores: K stage 0 is free once the last P V completed
         unsigned char* stage = smem + kOffK;  // [128 rows][256 B]
-        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+        {
             float o[32];
-            if (ntiles > 0) {
-                tmem_ld32(tmem + lane_off + c0, o);
+            if (ntiles > 0 && quarter_live) {
+                tmem_ld32(tmem + lane_off + c_lo, o);
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) o[j] = 0.f;
@@ -421,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.splits == 1) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 8)
-                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c0 + j) * 2) =
+                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c_lo + j) * 2) =
                         make_uint4(pack_bf16(o[j] * inv, o[j + 1] * inv), pack_bf16(o[j + 2] * inv, o[j + 3] * inv),
                                    pack_bf16(o[j + 4] * inv, o[j + 5] * inv), pack_bf16(o[j + 6] * inv, o[j + 7] * inv));
             } else {
@@ -429,12 +499,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4* dst = reinterpret_cast<float4*>(p.o_part) + ((size_t)split * units + unit) * (32 * kM);
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
-                    dst[((c0 + j) >> 2) * kM + rt] = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+                    dst[((c_lo + j) >> 2) * kM + rt] =
+                        make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
             }
         }
         if (p.splits > 1) {
-            if (half == 0) p.lse_part[((size_t)split * units + unit) * kM + rt] =
-                               l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
+            if (part == 0)
+                p.lse_part[((size_t)split * units + unit) * kM + rt] = l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
             // the last split of this (request, KV head, M-tile) merges all of them
             __threadfence();
             softmax_sync();
@@ -448,33 +519,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             softmax_sync();
             if (*shared_flag) {
                 __threadfence();
+                const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
                 float m = -INFINITY;
-                for (int sp = 0; sp < p.splits; ++sp) m = fmaxf(m, __ldcg(p.lse_part + ((size_t)sp * units + unit) * kM + rt));
-                float acc[16][4];
+                for (int sp = 0; sp < p.splits; ++sp) m = fmaxf(m, __ldcg(lse + (size_t)sp * units * kM));
+                float acc[8][4];
 #pragma unroll
-                for (int c = 0; c < 16; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+                for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
                 float wsum = 0.f;
                 if (m != -INFINITY) {
-                    for (int sp = 0; sp < p.splits; ++sp) {
-                        const float l = __ldcg(p.lse_part + ((size_t)sp * units + unit) * kM + rt);
-                        if (l == -INFINITY) continue;
-                        const float w = fast_exp2(l - m);
-                        wsum += w;
-                        const float4* src = reinterpret_cast<const float4*>(p.o_part) + ((size_t)sp * units + unit) * (32 * kM);
+                    // two splits' loads in flight at a time
+                    for (int sp = 0; sp < p.splits; sp += 2) {
+                        float4 v[2][8];
+                        float w[2];
 #pragma unroll
-                        for (int c = 0; c < 16; ++c) {
-                            const float4 v = __ldcg(src + (half * 16 + c) * kM + rt);
-                            acc[c][0] += w * v.x;
-                            acc[c][1] += w * v.y;
-                            acc[c][2] += w * v.z;
-                            acc[c][3] += w * v.w;
+                        for (int t = 0; t < 2; ++t) {
+                            const int sq = sp + t < p.splits ? sp + t : sp;
+                            const float l = __ldcg(lse + (size_t)sq * units * kM);
+                            w[t] = (sp + t < p.splits && l != -INFINITY) ? fast_exp2(l - m) : 0.f;
+                            const float4* src =
+                                reinterpret_cast<const float4*>(p.o_part) + ((size_t)sq * units + unit) * (32 * kM);
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) v[t][c] = __ldcg(src + (part * 8 + c) * kM + rt);
+                        }
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            if (w[t] == 0.f) continue;  // (a split without visible keys holds zeros)
+                            wsum += w[t];
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) {
+                                acc[c][0] += w[t] * v[t][c].x;
+                                acc[c][1] += w[t] * v[t][c].y;
+                                acc[c][2] += w[t] * v[t][c].z;
+                                acc[c][3] += w[t] * v[t][c].w;
+                            }
                         }
                     }
                 }
                 const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-                for (int c = 0; c < 16; c += 2)
-                    *reinterpret_cast<uint4*>(stage + rt * 256 + (half * 64 + c * 4) * 2) =
+                for (int c = 0; c < 8; c += 2)
+                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c_lo + c * 4) * 2) =
                         make_uint4(pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
                                    pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
                                    pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
@@ -483,8 +567,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
         softmax_sync();
         if (p.splits == 1 || *shared_flag) {
-            const int ts = threadIdx.x - 64;  // 0..255
-            for (int e = ts; e < kM * 16; e += 256) {
+            const int ts = threadIdx.x - 64;
+            for (int e = ts; e < kM * 16; e += kSoftmaxThreads) {
                 const int rr = e >> 4, c = e & 15;
                 const int pr = row0 + rr;
                 if (pr >= nrows) continue;

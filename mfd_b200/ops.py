@@ -247,6 +247,18 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch
     return out
 
 
+def tree_attention_status(device=None) -> int:
+    """The sticky status word at the head of the verify-attention workspace (the first int32 at its 256-byte aligned
+    base): 0; 1 once a bounded wait in the kernel gave up; 2 when a CTA found its shared-memory base misaligned
+    beyond the reserved slack and did no work.  0 when no attention call has run on the device."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    ws = Workspace._cache.get((dev.index if dev.index is not None else torch.cuda.current_device(), "attn"))
+    if ws is None:
+        return 0
+    off = (-ws.data_ptr()) % 256
+    return int(ws[off:off + 4].view(torch.int32).item())
+
+
 # ----------------------------------------------------------------------------------------------- tree GDN
 
 def tree_gdn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_cum: torch.Tensor, beta: torch.Tensor,

@@ -58,6 +58,7 @@ def test_tree_attention_vs_oracle(P, n, H, Hkv, splits):
     ref = oracle.tree_attention(q[0].float().numpy(), kk[:P], vv[:P], kk[P:], vv[P:], parents, D ** -0.5)
     err = np.abs(out[0].float().cpu().numpy() - ref).max()
     assert err <= TOL, err
+    assert ops.tree_attention_status() == 0  # no wait gave up, no CTA skipped
 
 
 def test_tree_attention_batched_variable_prefix():
@@ -80,3 +81,29 @@ def test_tree_attention_batched_variable_prefix():
                                     D ** -0.5)
         err = np.abs(out[b].float().cpu().numpy() - ref).max()
         assert err <= TOL, (b, err)
+
+
+@pytest.mark.parametrize("bs", [40, 70])
+def test_tree_attention_many_requests_tied_prefixes(bs):
+    """Launch order by prefix length (longest first, ties by request index) for up to 64 requests, natural order
+    above that: every request's rows match the oracle either way."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(bs)
+    n, H, Hkv, D = 9, 8, 2, 128
+    prefixes = [int(x) for x in torch.randint(0, 4, (bs,), generator=g) * 60 + 1]  # 1, 61, 121, 181: many ties
+    S = max(prefixes) + n
+    q = torch.randn(bs, n, H, D, generator=g).to(torch.bfloat16)
+    k = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    trees = [[-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)] for _ in range(bs)]
+    anc = torch.stack([anc_bits(t, 1) for t in trees]).to(DEV)
+    pl = torch.tensor(prefixes, dtype=torch.int32, device=DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, pl, D ** -0.5).float().cpu().numpy()
+    for b in range(bs):
+        P = prefixes[b]
+        kk = k[b].transpose(0, 1).float().numpy()
+        vv = v[b].transpose(0, 1).float().numpy()
+        ref = oracle.tree_attention(q[b].float().numpy(), kk[:P], vv[:P], kk[P:P + n], vv[P:P + n], trees[b],
+                                    D ** -0.5)
+        assert np.abs(out[b] - ref).max() <= TOL, b
+    assert ops.tree_attention_status() == 0
