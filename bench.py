@@ -3,6 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests-per-gpu R]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
     python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
+    python bench.py --kernel K                             (one kernel of the batch step alone, L2 flushed between
+                                                            launches: logits_step, tree_build, attention, accept)
 
 Workload (synthetic, seeded per global request id so any partition computes the same
 requests): 32 requests per GPU per step (32/64/128/256 requests at 1/2/4/8 GPUs), each with drafter logits
@@ -40,9 +42,10 @@ K_MODES, L_BLOCK, VOCAB, BUDGET = 8, 16, 151936, 64
 W = BUDGET + 1
 H, HKV, D = 32, 8, 128
 REQUESTS_PER_GPU = 32
-# Logits-step DRAM traffic per row (read + write) from an ncu capture of 256 rows x 151936 fp32, k = 64:
-# 155.75 MB read + 5.15 MB written.  Traffic grows with the rows, so a launch of R rows moves R times this.
-TOPK_TRAFFIC_PER_ROW = (155.754496e6 + 5.148672e6) / 256
+# Logits-step DRAM traffic per row (read + write) from an ncu capture of 1024 rows x 151936 fp32, k = 64
+# (bench.py --kernel logits_step --requests-per-gpu 8): 626.81 MB read + 10.39 MB written.  Traffic grows with the
+# rows, so a launch of R rows moves R times this.
+TOPK_TRAFFIC_PER_ROW = (626.812672e6 + 10.390272e6) / 1024
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -322,6 +325,40 @@ def e2e(dev, reqs, prefixes, steps: int, ws: int, chunk: int = 8):
             "d2h_bytes_per_step": out_bytes * ws, "requests_per_step": len(sample) * ws, "ms_per_step": round(ms, 3)}
 
 
+def kernel_line(name: str, steps: int, warmup: int, requests: int):
+    """One kernel of the batch step alone, on the batch workload of one GPU (the profiling case of its ncu
+    summaries): device time per launch with the L2 flushed (256 MB write) before each."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prefixes = prefix_lengths(requests)
+    batch = Batch(list(range(requests)), prefixes, dev)
+    step = Step(batch)
+    step.run()  # the trees and ancestor bitsets the later kernels read
+    ops, b = step.ops, batch
+    _, _, anc, _ = ops.build_trees(b.top.view(b.bs, K_MODES, L_BLOCK, BUDGET), b.ids.view(b.bs, K_MODES, L_BLOCK, BUDGET),
+                                   None, BUDGET, tree=b.tree, counts=b.counts)
+    fns = {
+        "logits_step": lambda: ops.topk_logz(b.draft.view(-1, VOCAB), BUDGET, ids_dtype=torch.int32,
+                                             out=(b.top, b.ids, b.logz)),
+        "tree_build": lambda: ops.build_trees(b.top.view(b.bs, K_MODES, L_BLOCK, BUDGET),
+                                              b.ids.view(b.bs, K_MODES, L_BLOCK, BUDGET), None, BUDGET, tree=b.tree,
+                                              counts=b.counts),
+        "attention": lambda: ops.tree_attention(b.q, b.k, b.v, anc, b.prefix_t, D ** -0.5, splits=step.splits,
+                                                out=b.attn_out),
+        "accept": lambda: ops.accept(b.target, b.tree[:, 0], b.tree[:, 2], temperature=b.temperature, uniforms=b.u,
+                                     max_steps=L_BLOCK - 1, out_len=L_BLOCK),
+    }
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    us = timed_us(fns[name], steps, warmup, flush)
+    rows = requests * K_MODES * L_BLOCK
+    alg = {"logits_step": rows * VOCAB * 4, "tree_build": rows * BUDGET * 8,
+           "attention": sum(2 * HKV * (p + W) * D * 2 for p in batch.prefix) + b.q.numel() * 2 * 2,
+           "accept": b.target.numel() * 2}[name]
+    return {"kernel": name, "requests": requests, "us_per_launch": round(us, 2), "algorithmic_bytes": alg,
+            "achieved_gbs": round(alg / us / 1e3, 1), "peak_hbm_gbs": peaks()["hbm_gbs"],
+            "frac_of_hbm": round(alg / us / 1e3 / peaks()["hbm_gbs"], 4), "l2": "flushed (256 MB write) per launch"}
+
+
 # ------------------------------------------------------------------------------------------------ CPU reference
 
 def cpu_reference_request(req: int, prefix: int, temperature: float, ext):
@@ -522,6 +559,8 @@ def main():
     ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
+    ap.add_argument("--kernel", default=None, choices=["logits_step", "tree_build", "attention", "accept"],
+                    help="time one kernel of the batch step alone (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -550,6 +589,10 @@ def main():
                 "e2e": {"value": round(value, 4), "unit": "trees/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
+        return
+
+    if args.kernel is not None:
+        print(json.dumps(kernel_line(args.kernel, args.steps, args.warmup, args.requests_per_gpu)))
         return
 
     if args.config is not None:
@@ -593,7 +636,7 @@ def main():
         "roofline": {"kernel": "mfd_topk_logz (logits step)", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "peak_source": pk["source"], "traffic": round(TOPK_TRAFFIC_PER_ROW * rows),
-                     "traffic_source": "ncu capture of 256 rows, scaled by rows",
+                     "traffic_source": "ncu capture of 1024 rows, scaled by rows",
                      "algorithmic_bytes_per_launch": logits_bytes},
         "clocks": clocks,
         "gpu_launches": Step.LAUNCHES * args.steps,
