@@ -413,8 +413,7 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
         q += (bytes + 15) & ~(size_t)15;
         return r;
     };
-    uint64_t* hc = (uint64_t*)take(8 * (size_t)cap);  // heap: comparator keys
-    double* hw = (double*)take(8 * (size_t)cap);      // heap: logw
+    ulonglong2* he = (ulonglong2*)take(16 * (size_t)cap);  // 4-ary heap: (comparator key, logw bits)
     uint64_t* hash = (uint64_t*)take(8 * (size_t)p.hcap);
     float* s_lp = (float*)take(4 * (size_t)K * L * k);
     int32_t* s_ids = (int32_t*)take(4 * (size_t)K * L * k);
@@ -466,37 +465,41 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
             key = key + 0.0f;  // -0.0 and +0.0 compare equal in the reference: fold them
             return ((uint64_t)ord_f32(key) << 32) | ax;
         };
+        // a 4-ary min-heap of 16-byte entries: children of i are 4i+1 .. 4i+4, so about 3 levels for the at most
+        // K (B + 1) live entries, and the four children of a level are loaded together
         auto push = [&](uint64_t c, double w) {
             int i = n++;
             while (i > 0) {
-                const int par = (i - 1) >> 1;
-                const uint64_t pc = hc[par];
-                if (pc <= c) break;
-                hc[i] = pc;
-                hw[i] = hw[par];
+                const int par = (i - 1) >> 2;
+                const ulonglong2 pe = he[par];
+                if (pe.x <= c) break;
+                he[i] = pe;
                 i = par;
             }
-            hc[i] = c;
-            hw[i] = w;
+            he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
         };
         // replace the root by (c, w) and sift it down
         auto replace_top = [&](uint64_t c, double w) {
             int i = 0;
             for (;;) {
-                const int l = 2 * i + 1;
+                const int l = 4 * i + 1;
                 if (l >= n) break;
-                const int r = l + 1;
-                const uint64_t lc = hc[l];
-                const uint64_t rc = r < n ? hc[r] : ~0ull;
-                const int j = rc < lc ? r : l;
-                const uint64_t jc = rc < lc ? rc : lc;
-                if (c <= jc) break;
-                hc[i] = jc;
-                hw[i] = hw[j];
+                ulonglong2 e[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) e[t] = l + t < n ? he[l + t] : make_ulonglong2(~0ull, 0ull);
+                int j = l;
+                ulonglong2 best = e[0];
+#pragma unroll
+                for (int t = 1; t < 4; ++t)
+                    if (e[t].x < best.x) {
+                        best = e[t];
+                        j = l + t;
+                    }
+                if (c <= best.x) break;
+                he[i] = best;
                 i = j;
             }
-            hc[i] = c;
-            hw[i] = w;
+            he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
         };
         int count = 0, fail = 0;
         if (B > 0 && L > 0)
@@ -505,8 +508,9 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
                 push(mix_comp(w, m, pack_aux(m, 0, 1, 0)), w);
             }
         while (n > 0 && count < B) {
-            const uint64_t M = hc[0];
-            const double lwp = hw[0];
+            const ulonglong2 top = he[0];
+            const uint64_t M = top.x;
+            const double lwp = __longlong_as_double((long long)top.y);
             const uint32_t ax = (uint32_t)M;
             const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
             const int row = (m * L + dep - 1) * k;
@@ -546,7 +550,7 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
                 replace_top(mix_comp(slw, m, pack_aux(m, par, dep, rk + 1)), slw);
             } else {
                 --n;
-                if (n > 0) replace_top(hc[n], hw[n]);
+                if (n > 0) replace_top(he[n].x, __longlong_as_double((long long)he[n].y));
             }
             if (has_child) {
                 const double clw = lwp + (double)lp_c;
