@@ -5,9 +5,10 @@
 // inference/hf/tree_logits.py:16-46 (bf16 top-k + one-pass online logsumexp), SGLang
 // DDTreeDraftTopK / _row_logsumexp_kernel (sglang-v0.5.22-mfd.patch:1451-1550).
 //
-// Work split: the R x V element space is cut into equal contiguous ranges, 2 CTAs of 256 threads per SM (one
-// wave).  A range may span a row boundary, so a CTA emits one partial record per row piece: (max, sum exp) and
-// the piece's sorted top-k keys (64-bit: orderable value, then the complement of the index).
+// Work split: 2 CTAs of 256 threads per SM (one wave), and no CTA's range crosses a row.  With at least as many
+// rows as CTAs each CTA takes a balanced run of whole rows; with fewer, each row is cut into equal pieces, one per
+// CTA, which emit partial records -- (max, sum exp) and the piece's sorted top-k keys (64-bit: orderable value,
+// then the complement of the index) -- merged by the row's last CTA.
 //
 // Streaming (the hot loop) is register-only and software pipelined: every thread keeps eight 16-byte
 // non-allocating loads in flight (the slots of a group are refilled from the next batch as soon as the group is
@@ -129,8 +130,9 @@ struct Params {
     void* top_ids;          // [rows, k] int32 or int64
     int ids_i64;
     float* logz;            // [rows] or null
-    int64_t per_cta;        // elements per CTA (multiple of 8)
-    int max_pieces;         // partial-record slots per row
+    int pieces_per_row;     // P > 1: CTA c takes piece c % P of row c / P; P = 1: CTA c takes whole rows
+    int64_t piece_len;      // elements per piece when P > 1 (a multiple of 8)
+    int max_pieces;         // partial-record slots per row (= P)
     float2* part_ms;        // [rows, max_pieces]
     uint64_t* part_keys;    // [rows, max_pieces, KP]
     unsigned int* tickets;  // [rows], zero between launches
@@ -347,14 +349,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
     constexpr int ES = BF16 ? 2 : 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int k = p.k;
-    const int64_t total = p.rows * p.vocab;
-    const int64_t a = (int64_t)blockIdx.x * p.per_cta;
-    const int64_t b = a + p.per_cta < total ? a + p.per_cta : total;
-    if (a >= b) return;
-    for (int64_t row = a / p.vocab; row * p.vocab < b; ++row) {
-        const int64_t r0 = row * p.vocab;
-        const int64_t c0 = a > r0 ? a - r0 : 0;
-        const int64_t c1 = (b < r0 + p.vocab ? b : r0 + p.vocab) - r0;
+    // the CTA's pieces never cross a row: one piece of one row (P > 1), or a balanced run of whole rows
+    const int P = p.pieces_per_row;
+    int64_t row_begin, row_end, cc0 = 0, cc1 = p.vocab;
+    int piece = 0;
+    if (P > 1) {
+        row_begin = blockIdx.x / P;
+        row_end = row_begin + 1;
+        piece = (int)(blockIdx.x % P);
+        cc0 = (int64_t)piece * p.piece_len;
+        cc1 = cc0 + p.piece_len < p.vocab ? cc0 + p.piece_len : p.vocab;
+    } else {
+        row_begin = (int64_t)blockIdx.x * p.rows / gridDim.x;
+        row_end = (int64_t)(blockIdx.x + 1) * p.rows / gridDim.x;
+    }
+    if (row_begin >= p.rows || cc0 >= cc1) return;
+    for (int64_t row = row_begin; row < row_end; ++row) {
+        const int64_t c0 = cc0, c1 = cc1;
         const char* base = (const char*)p.x + (size_t)row * p.row_stride * ES;
 
         // ---- the streaming pass
@@ -576,10 +587,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         }
 
         // ---- publish this piece
-        const int64_t first_cta = r0 / p.per_cta;
-        const int64_t last_cta = (r0 + p.vocab - 1) / p.per_cta;
-        const int pieces = (int)(last_cta - first_cta + 1);
-        const int slot = (int)(blockIdx.x - first_cta);
+        const int pieces = P, slot = piece;
         if (pieces == 1) {
             if (threadIdx.x == 0) {
                 float mm = -INFINITY, ss = 0.f;
@@ -682,24 +690,37 @@ static int kp_for(int64_t k) {
 
 struct Plan {
     int grid;
-    int64_t per_cta;
+    int pieces_per_row;
+    int64_t piece_len;
     int max_pieces;
     int kp;
 };
 
+// One wave of kCtasPerSm CTAs per SM.  With at least as many rows as CTA slots every CTA takes a balanced run of
+// whole rows (no partial records); with fewer, each row is cut into P = slots / rows equal pieces of at least
+// 8192 elements, one per CTA, so no CTA ever pays a piece's fixed costs (first-batch latency, floors, select)
+// twice in a row.
 static Plan plan(int64_t rows, int64_t vocab, int64_t k) {
     Plan pl;
-    const int64_t total = rows * vocab;
-    int64_t grid = (int64_t)sm_count() * kCtasPerSm;
-    const int64_t min_per = 8192;
-    if (grid * min_per > total) grid = (total + min_per - 1) / min_per;
-    if (grid < 1) grid = 1;
-    int64_t per = (total + grid - 1) / grid;
-    per = (per + 7) / 8 * 8;
-    grid = (total + per - 1) / per;
-    pl.grid = (int)grid;
-    pl.per_cta = per;
-    pl.max_pieces = (int)((vocab + per - 1) / per + 1);
+    const int64_t slots = (int64_t)sm_count() * kCtasPerSm;
+    const int64_t min_piece = 8192;
+    if (rows >= slots) {
+        pl.grid = (int)slots;
+        pl.pieces_per_row = 1;
+        pl.piece_len = vocab;
+    } else {
+        int64_t P = slots / rows;
+        const int64_t cap = vocab / min_piece;
+        if (P > cap) P = cap;
+        if (P < 1) P = 1;
+        int64_t len = (vocab + P - 1) / P;
+        len = (len + 7) / 8 * 8;
+        P = (vocab + len - 1) / len;
+        pl.pieces_per_row = (int)P;
+        pl.piece_len = len;
+        pl.grid = (int)(rows * P);
+    }
+    pl.max_pieces = pl.pieces_per_row;
     pl.kp = kp_for(k);
     return pl;
 }
@@ -763,7 +784,8 @@ extern "C" int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t v
     p.top_ids = top_ids;
     p.ids_i64 = ids_dtype == MFD_I64;
     p.logz = logz;
-    p.per_cta = pl.per_cta;
+    p.pieces_per_row = pl.pieces_per_row;
+    p.piece_len = pl.piece_len;
     p.max_pieces = pl.max_pieces;
     const size_t ms = (size_t)rows * pl.max_pieces * sizeof(float2);
     p.part_ms = (float2*)ws;
