@@ -16,7 +16,8 @@
 // lazy-rescale check of its online (max, sum exp) and adds the 32 exponentials as a tree.  A thread whose group
 // reaches the floor (rare) appends those elements with shared atomics to the CTA's candidate buffer.  The floor
 // comes from the piece's first batch: each warp sorts its 32 lane maxima and the floor is the r-th largest over
-// the CTA, found by rank, with r chosen so that about 2.5 k elements of the whole piece are expected to pass.
+// the CTA, found by rank, with r chosen so that about 3.5 k elements of the whole piece are expected to pass (a
+// lower target sorts fewer candidates but fails the verification below more often, and a rescan costs more).
 // That floor is speculative and is verified at the end of the piece: if at least k candidates were collected
 // (and the buffer did not overflow), every element of the piece's top k is among them -- an element below the
 // floor has at least k collected elements above it.  Otherwise the piece is scanned again (an L2 hit) against a
@@ -278,8 +279,9 @@ __device__ __forceinline__ void select_rank(Smem<KP>& sm, int n) {
     __syncthreads();
 }
 
+// inlined: the next row's first loads are in flight across it, and a call would have to save their registers
 template <int KP>
-__device__ __noinline__ void select_topk(Smem<KP>& sm, int n) {
+__device__ __forceinline__ void select_topk(Smem<KP>& sm, int n) {
     if (n <= kWarps * 32) {
         select_rank<KP, 1>(sm, n);
     } else if (n <= kWarps * 64) {
@@ -364,26 +366,51 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         row_end = (int64_t)(blockIdx.x + 1) * p.rows / gridDim.x;
     }
     if (row_begin >= p.rows || cc0 >= cc1) return;
+    constexpr int kBatch = kThreads * kLoads;  // vectors per batch
+    // the geometry of a row's piece: aligned body [hb, tb) as nvec 16-byte vectors, head / tail scalars outside it
+    auto geometry = [&](int64_t row, const char*& base, int64_t& hb, int64_t& nvec, int64_t& tb) {
+        base = (const char*)p.x + (size_t)row * p.row_stride * ES;
+        hb = cc0;
+        const uintptr_t ad = (uintptr_t)(base + cc0 * ES);
+        const int64_t mis = (int64_t)((ad & 15u) / ES);
+        if (mis) hb = cc0 + (VE - mis);
+        if (hb > cc1) hb = cc1;
+        nvec = (cc1 - hb) / VE;
+        tb = hb + nvec * VE;
+    };
+    // the first batch and the head/tail scalar of a row, issued before the previous row's select when possible
+    uint4 w[kLoads];
+    float xs0 = -INFINITY;
+    int64_t cs = -1;
+    auto first_loads = [&](int64_t row) {
+        const char* bse;
+        int64_t hb_, nv_, tb_;
+        geometry(row, bse, hb_, nv_, tb_);
+        const uint4* vb_ = (const uint4*)(bse + hb_ * ES);
+#pragma unroll
+        for (int u = 0; u < kLoads; ++u) {
+            const int64_t vi = (int64_t)u * kThreads + threadIdx.x;
+            if (vi < nv_) w[u] = ldg_stream_u4(vb_ + vi);
+        }
+        const int64_t nh = hb_ - cc0, nt = cc1 - tb_, t = threadIdx.x;
+        cs = -1;
+        if (t < nh) cs = cc0 + t;
+        else if (t - nh < nt) cs = tb_ + (t - nh);
+        xs0 = -INFINITY;
+        if (cs >= 0) xs0 = BF16 ? bf16_at((const uint16_t*)bse + cs) : ((const float*)bse)[cs];
+    };
+    first_loads(row_begin);
     for (int64_t row = row_begin; row < row_end; ++row) {
         const int64_t c0 = cc0, c1 = cc1;
-        const char* base = (const char*)p.x + (size_t)row * p.row_stride * ES;
+        const char* base;
 
         // ---- the streaming pass
-        constexpr int kBatch = kThreads * kLoads;  // vectors per batch
         float m = -INFINITY, mL = -INFINITY, s = 0.f;
         float lmax = -INFINITY;  // lane maximum over the head/tail scalar and the first batch
-        int64_t hb = c0;
-        {
-            const uintptr_t ad = (uintptr_t)(base + c0 * ES);
-            const int64_t mis = (int64_t)((ad & 15u) / ES);
-            if (mis) hb = c0 + (VE - mis);
-            if (hb > c1) hb = c1;
-        }
-        const int64_t nvec = (c1 - hb) / VE;
-        const int64_t tb = hb + nvec * VE;
+        int64_t hb, nvec, tb;
+        geometry(row, base, hb, nvec, tb);
         const uint4* vb = (const uint4*)(base + hb * ES);
         const int64_t nbatch = (nvec + kBatch - 1) / kBatch;
-        // warp-aggregated append of the elements of x[0..live) at or above fl
         // append the elements of x[0..live) at or above fl to the CTA's candidates (a lane that has some works
         // alone: shared atomics, no warp collective; a count past kCap marks the overflow)
         auto offer = [&](const float (&x)[VE], uint32_t col0, int live, float fl) {
@@ -395,27 +422,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
                 }
             }
         };
-        // head/tail scalar of this thread
+        // head/tail scalar of this thread (loaded with the first batch)
         float xs[VE];
-        int64_t cs = -1;
         {
-            const int64_t nh = hb - c0, nt = c1 - tb, t = threadIdx.x;
-            if (t < nh) cs = c0 + t;
-            else if (t - nh < nt) cs = tb + (t - nh);
 #pragma unroll
             for (int e = 0; e < VE; ++e) xs[e] = -INFINITY;
-            if (cs >= 0) xs[0] = BF16 ? bf16_at((const uint16_t*)base + cs) : ((const float*)base)[cs];
+            xs[0] = xs0;
             lse_vec<VE>(m, mL, s, xs, xs[0]);
             lmax = xs[0];
         }
-        // w[] holds one batch; after the floors, each slot is refilled with the next batch's vector as soon as it
-        // has been consumed, so a batch of loads is always in flight
-        uint4 w[kLoads];
-#pragma unroll
-        for (int u = 0; u < kLoads; ++u) {
-            const int64_t vi = (int64_t)u * kThreads + threadIdx.x;
-            if (vi < nvec) w[u] = ldg_stream_u4(vb + vi);
-        }
+        // w[] holds one batch (the first one issued before the previous row's select); after the floors, each slot
+        // is refilled with the next batch's vector as soon as it has been consumed
         // first batch: (max, sum) and the lane maximum
         if (nbatch > 0) {
 #pragma unroll
@@ -439,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         {
             const int64_t sample = min(nvec, (int64_t)kBatch) * VE + (hb - c0) + (c1 - tb);
             const int64_t np = c1 - c0;
-            int r = (int)((5LL * k * sample + 2 * np - 1) / (2 * np));
+            int r = (int)((7LL * k * sample + 2 * np - 1) / (2 * np));
             r = max(r, 1);
             uint64_t r1[1] = {((uint64_t)ord_f32(lmax) << 32) | (uint64_t)(~(uint32_t)threadIdx.x)};
             warp_sort_desc<1>(r1);
@@ -563,6 +580,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
             }
         }
 
+        if (row + 1 < row_end) first_loads(row + 1);  // in flight during this row's select and publish
         // ---- the piece's (max, sum)
         {
             float mm = m, ss = s;
