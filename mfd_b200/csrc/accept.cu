@@ -261,7 +261,8 @@ __device__ __forceinline__ uint64_t weight_sum(const uint16_t* x, int64_t c0, in
 
 constexpr int kSampleThreads = 768;
 constexpr int kSampleWarps = kSampleThreads / 32;
-constexpr int kMaxRounds = 64;  // rows up to 64 rounds x 768 threads x 8 elements = 393216 logits
+constexpr int kMaxRounds = 64;
+constexpr int kUnroll = 4;      // rounds whose loads are in flight together  // rows up to 64 rounds x 768 threads x 8 elements = 393216 logits
 
 __device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
 #pragma unroll
@@ -291,17 +292,21 @@ __device__ __forceinline__ uint64_t vec8_weight(uint4 w, float m, float inv_t) {
 
 // The weight of a logit depends only on its bf16 bit pattern (m and T are fixed per row), so each row first
 // tabulates fixed40 over the patterns it can contain and pass 2 looks weights up instead of evaluating the
-// exponential 150k times.  Table: magnitudes [lo, hi_p] of positive patterns, then [lo, hi_n] of negative ones.
-//   * below lo (|x| < tau) every pattern has the weight of x = 0: with m != 0, tau = 2^(e_m - 26) is under a
-//     quarter ulp of m, so fsub(x, m) == -m exactly; with m == 0, tau = 2^(e_T - 28) keeps |x / T| < 2^-26, where
-//     the polynomial rounds to exactly 1.0, as it does for x = 0;
-//   * positive patterns above m cannot occur (m is the row max);
-//   * negative magnitudes at or beyond 90 T + |m| have (x - m) / T < -88 after rounding: weight 0.
-// Every table entry is fixed40 itself, so pass 2 sums exactly the values the direct evaluation would.
+// exponential 150k times.  Table: for each sign, H + 1 entries indexed by t = clamp(magnitude - lo + 1, 0, H):
+//   * t = 0, magnitudes below lo (|x| < tau): every such pattern has the weight of x = 0: with m != 0,
+//     tau = 2^(e_m - 26) is under a quarter ulp of m, so fsub(x, m) == -m exactly; with m == 0, tau = 2^(e_T - 28)
+//     keeps |x / T| < 2^-26, where the polynomial rounds to exactly 1.0, as it does for x = 0;
+//   * t = 1 .. H - 1, magnitudes lo .. hi with hi = the bf16 magnitude at or above 90 T + |m|: fixed40 of the
+//     pattern (positive patterns above m cannot occur: m is the row max);
+//   * t = H, magnitudes beyond hi: (x - m) / T < -88 after rounding for negatives, weight 0 (positives cannot
+//     occur), as for the infinities and NaNs, whose direct weight is 0 too.
+// The clamp runs on both halves of a 32-bit word at once (16-bit SIMD add + min with relu).  Every entry is
+// fixed40 itself, an integer below 2^41, so a thread adds its looked-up weights exactly in double (partial sums stay
+// below 2^53) on the FP64 pipe, and pass 2 sums exactly the values the direct evaluation would.
 constexpr int kTableCap = 12 * 1024;  // entries; rows needing more are evaluated directly
 
 struct RowTable {
-    int lo, hi_p, hi_n, npos;  // magnitude range limits and the positive-part size; npos < 0: no table
+    int lo, H;  // magnitude offset and clamp limit; H < 0: no table
 };
 
 __device__ __forceinline__ int bf16_mag_ceil(float v) {  // smallest bf16 magnitude pattern >= v (v >= 0, finite)
@@ -313,7 +318,8 @@ __device__ __forceinline__ int bf16_mag_ceil(float v) {  // smallest bf16 magnit
 
 __device__ RowTable plan_table(float m, float inv_t) {
     RowTable t;
-    t.npos = -1;
+    t.H = -1;
+    t.lo = 0;
     if (!isfinite(m) || !(inv_t > 0.f) || !isfinite(inv_t)) return t;
     const float T = 1.0f / inv_t;
     float tau;
@@ -326,12 +332,12 @@ __device__ RowTable plan_table(float m, float inv_t) {
     } else {
         return t;  // a tiny nonzero max: evaluate directly
     }
-    t.lo = (int)(__float_as_uint(tau) >> 16);  // tau is a power of two: exact as bf16
-    t.hi_p = m > 0.f ? (int)(__float_as_uint(m) >> 16) : t.lo - 1;
-    t.hi_n = bf16_mag_ceil(90.0f * T + fabsf(m));
-    const int np = max(t.hi_p - t.lo + 1, 0), nn = max(t.hi_n - t.lo + 1, 0);
-    if (np + nn + 2 > kTableCap) return t;
-    t.npos = np;
+    const int lo = (int)(__float_as_uint(tau) >> 16);  // tau is a power of two: exact as bf16 (lo >= 0x80)
+    const int hi = bf16_mag_ceil(90.0f * T + fabsf(m));
+    const int H = max(hi - lo + 2, 1);
+    if (2 * (H + 1) > kTableCap) return t;
+    t.lo = lo;
+    t.H = H;
     return t;
 }
 
@@ -341,7 +347,7 @@ __device__ RowTable plan_table(float m, float inv_t) {
 // warp's 256-logit weight sum.  Warp 0 scans the (round, warp) sums in row order to find the one holding
 // floor(u * Z) and searches its 256 logits.  All sums are integers, so no order changes the result.
 __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
-    extern __shared__ __align__(16) uint64_t table[];  // [kTableCap]
+    extern __shared__ __align__(16) double table[];  // [2][H + 1] (<= kTableCap)
     __shared__ uint64_t wsum[kMaxRounds * kSampleWarps];
     __shared__ float wmax[kSampleWarps];
     __shared__ int flag;
@@ -354,16 +360,23 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     const bool aligned = (((uintptr_t)x) & 15u) == 0;
     const int64_t nv = (V + 7) / 8;
     const int rounds = (int)((nv + kSampleThreads - 1) / kSampleThreads);
-    // ---- pass 1: max
-    float mx = -INFINITY;
-    for (int r = 0; r < rounds; ++r) {
-        const int64_t v = (int64_t)r * kSampleThreads + threadIdx.x;
-        if (v >= nv) break;
-        const uint4 w = load_vec8(x, v, V, aligned);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    // ---- pass 1: max (bf16 pairs), kUnroll rounds' loads in flight per thread; absent elements read as -inf
+    __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
+    for (int r0 = 0; r0 < rounds; r0 += kUnroll) {
+        uint4 w[kUnroll];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) mx = fmaxf(mx, fmaxf(bf16lo(ws[q]), bf16hi(ws[q])));
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t v = (int64_t)(r0 + u) * kSampleThreads + threadIdx.x;
+            w[u] = v < nv ? load_vec8(x, v, V, aligned) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) mx2 = __hmax2(mx2, *reinterpret_cast<const __nv_bfloat162*>(&ws[q]));
+        }
     }
+    float mx = fmaxf(__low2float(mx2), __high2float(mx2));
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MFD_FULL_MASK, mx, o));
     if (lane == 0) wmax[warp] = mx;
@@ -374,46 +387,60 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     const float inv_t = __frcp_rn(p.temperature);
     // ---- the row's weight table
     const RowTable tb = plan_table(m, inv_t);
-    const int n_tab = tb.npos >= 0 ? tb.npos + max(tb.hi_n - tb.lo + 1, 0) : 0;
-    if (tb.npos >= 0) {
-        for (int i = threadIdx.x; i < n_tab + 2; i += kSampleThreads) {
+    if (tb.H >= 0) {
+        const int half = tb.H + 1;
+        for (int i = threadIdx.x; i < 2 * half; i += kSampleThreads) {
+            const int sg = i >= half ? 1 : 0, t = i - sg * half;
             uint64_t e;
-            if (i < tb.npos) {
-                e = fixed40(__uint_as_float((uint32_t)(tb.lo + i) << 16), m, inv_t);
-            } else if (i < n_tab) {
-                e = fixed40(__uint_as_float((uint32_t)(0x8000 | (tb.lo + i - tb.npos)) << 16), m, inv_t);
-            } else if (i == n_tab) {
+            if (t == 0) {
                 e = fixed40(0.0f, m, inv_t);  // every magnitude below tau
+            } else if (t < tb.H) {
+                const uint32_t pat = ((uint32_t)sg << 15) | (uint32_t)(tb.lo + t - 1);
+                const float v = __uint_as_float(pat << 16);
+                e = (sg == 0 && v > m) ? 0ull : fixed40(v, m, inv_t);  // (positives above m cannot occur)
             } else {
-                e = 0ull;  // beyond the cut (and impossible patterns)
+                e = 0ull;  // beyond the cut, infinities, NaNs
             }
-            table[i] = e;
+            table[i] = (double)e;  // exact: e < 2^41
         }
         __syncthreads();
     }
-    auto weight = [&](uint32_t bits) -> uint64_t {  // bits: one bf16 pattern; selects only, no branches
-        const int mag = (int)(bits & 0x7FFFu);
-        const bool neg = (bits & 0x8000u) != 0u;
-        const int i = mag - tb.lo;
-        const int hi = neg ? tb.hi_n : tb.hi_p;
-        const int base = neg ? tb.npos : 0;
-        const int idx = i < 0 ? n_tab : (mag <= hi ? base + i : n_tab + 1);
-        return table[idx];
-    };
-    auto vec_weight = [&](uint4 w) -> uint64_t {
-        if (tb.npos < 0) return vec8_weight(w, m, inv_t);
+    const uint32_t add2 = (uint32_t)(uint16_t)(1 - tb.lo) * 0x10001u;  // both halves: 1 - lo
+    const uint32_t lim2 = (uint32_t)(uint16_t)max(tb.H, 0) * 0x10001u;  // both halves: H
+    const int half_entries = tb.H + 1;
+    // the weight of 8 logits as an exact double (an integer below 2^44)
+    auto vec_weight = [&](uint4 w) -> double {
+        if (tb.H < 0) return (double)vec8_weight(w, m, inv_t);
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        uint64_t z = 0;
+        double z = 0.0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) z += weight(ws[q] & 0xFFFFu) + weight(ws[q] >> 16);
+        for (int q = 0; q < 4; ++q) {
+            // t for both halves at once: clamp(magnitude - lo + 1, 0, H)
+            const uint32_t t2 = __viaddmin_s16x2_relu(ws[q] & 0x7FFF7FFFu, add2, lim2);
+            const int i_lo = (int)(t2 & 0xFFFFu) + (int)((ws[q] >> 15) & 1u) * half_entries;
+            const int i_hi = (int)(t2 >> 16) + (int)(ws[q] >> 31) * half_entries;
+            z += table[i_lo];
+            z += table[i_hi];
+        }
         return z;
     };
     // ---- pass 2: the weight of each (round, warp) block of 256 logits
-    for (int r = 0; r < rounds; ++r) {
-        const int64_t v = (int64_t)r * kSampleThreads + threadIdx.x;
-        const uint64_t z = v < nv ? vec_weight(load_vec8(x, v, V, aligned)) : 0ull;
-        const uint64_t ws = warp_sum_u64(z);
-        if (lane == 0) wsum[r * kSampleWarps + warp] = ws;
+    for (int r0 = 0; r0 < rounds; r0 += kUnroll) {
+        uint4 w[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t v = (int64_t)(r0 + u) * kSampleThreads + threadIdx.x;
+            w[u] = v < nv ? load_vec8(x, v, V, aligned) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            if (r0 + u >= rounds) break;
+            // a block of 256 weights sums below 2^52: exact in double; absent elements (-inf) weigh 0
+            double z = vec_weight(w[u]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(MFD_FULL_MASK, z, o);
+            if (lane == 0) wsum[(r0 + u) * kSampleWarps + warp] = (uint64_t)z;
+        }
     }
     __syncthreads();
     if (warp == 0) {
