@@ -190,6 +190,31 @@ int mfd_tree_prep(const void* x, const void* conv_state, const int32_t* conv_ind
                   int64_t conv_dim, int64_t kernel, int64_t num_k_heads, int64_t num_heads, int64_t head_dim,
                   float scale, void* q, void* k, void* v, void* stream);
 
+/*
+ * Commit step, KV moves in a token-major pool (SGLang).  buffers: a device array of num_buffers base addresses
+ * (every layer's K and V buffer), each holding slots of slot_bytes (a multiple of 8; the bases 16-byte aligned when
+ * slot_bytes is a multiple of 16).  For request b and i < width, slot move_src[b, i] moves to move_tgt[b, i] in
+ * every buffer when the two differ; every source is read before any store (a path slot can be another move's
+ * target).  move_src, move_tgt [bs, width] int64 on the device.  One launch for all buffers.
+ * Replaces: patch:1769-1841 (DDTreeKVCompactor / _ddtree_compact_kv_kernel).
+ */
+int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes, const int64_t* move_src,
+                        const int64_t* move_tgt, int64_t bs, int64_t width, void* stream);
+
+/*
+ * Commit step, HF cache compaction.  buffers: a device array of num_buffers base addresses of cache tensors viewed
+ * as [outer, rows, row_bytes] (outer_stride and row_stride in bytes, multiples of 8).  Row past_length + keep[i]
+ * moves to past_length + i for i < keep_count in every buffer and outer index; nothing happens when the appended
+ * window rows - past_length is empty, or keep_count is 0 or the whole window (as the reference returns early).
+ * keep [keep_count] int64 on the device; status (optional device int) receives MFD_ERR_INVALID for a keep index
+ * outside the window (that move is skipped).
+ * Replaces: inference/hf/ddtree.py:33-61 (compact_tail_inplace), 385-403 (_compact_appended_window), applied by
+ *           406-436 (compact_dynamic_cache) to every layer's keys and values.
+ */
+int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, int64_t outer, int64_t outer_stride, int64_t rows,
+                     int64_t row_stride, int64_t row_bytes, int64_t past_length, const int64_t* keep,
+                     int64_t keep_count, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

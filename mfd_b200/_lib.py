@@ -53,6 +53,8 @@ _SIGS = {
                              c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mfd_tree_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp,
                               c_vp, c_vp]),
+    "mfd_commit_kv_moves": (c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp]),
+    "mfd_compact_tail": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]),
 }
 
 MFD_F32, MFD_BF16, MFD_I32, MFD_I64 = 0, 1, 2, 3

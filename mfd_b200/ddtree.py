@@ -8,6 +8,8 @@ Same names, arguments, return types and edge cases as the reference:
   multi_mode_draft_mask(context_length, num_modes, block_size, dtype, device)   ddtree.py:360-365
   follow_verified_tree(child_maps, posterior [1, n])                ddtree.py:368-382
   enable_cpp_tree / enable_mode_attention                           ddtree.py:95-112
+  compact_dynamic_cache(past_key_values, past_length, keep_current_indices)   ddtree.py:406-436
+  _compact_appended_window(cache_tensor, past_length, keep_current_indices)  ddtree.py:385-403
 
 The builders run the logits step (mfd_topk_logz) and the exact heap (mfd_build_trees) on the GPU and
 return CPU tensors as the reference does (its callers index them on the host).  The fourth value is a Tree
@@ -189,3 +191,35 @@ def follow_verified_tree(child_maps, posterior: torch.Tensor):
         accepted_indices.append(current_index)
         next_token = int(posterior_tokens[current_index])
     return accepted_indices, next_token
+
+
+# ----------------------------------------------------------------------------------------------- commit step
+
+def _compact_appended_window(cache_tensor: torch.Tensor, past_length: int, keep_current_indices: torch.Tensor) -> None:
+    """Rows past_length + keep[i] -> past_length + i along dim -2, in place (inference/hf/ddtree.py:385-403): a
+    no-op when the appended window is empty, keep is empty or keep covers the whole window."""
+    ops.compact_tail([cache_tensor], past_length, keep_current_indices)
+
+
+def compact_dynamic_cache(past_key_values, past_length: int, keep_current_indices: list[int]) -> None:
+    """Keep only the accepted rows of the appended tree window in every layer's keys and values, then crop the
+    cache to past_length + len(keep) (inference/hf/ddtree.py:406-436).  All layers' K and V move in one launch."""
+    if len(keep_current_indices) == 0:
+        past_key_values.crop(past_length)
+        return
+    if hasattr(past_key_values, "key_cache") and hasattr(past_key_values, "value_cache"):
+        tensors = list(past_key_values.key_cache) + list(past_key_values.value_cache)
+    elif hasattr(past_key_values, "layers"):
+        tensors = []
+        for layer in past_key_values.layers:
+            if not hasattr(layer, "keys") or layer.keys is None or layer.keys.numel() == 0:
+                continue
+            tensors += [layer.keys, layer.values]
+    else:
+        raise RuntimeError("Unsupported DynamicCache layout for DDTree cache compaction.")
+    by_device: dict = {}
+    for t in tensors:
+        by_device.setdefault(t.device, []).append(t)
+    for group in by_device.values():
+        ops.compact_tail(group, past_length, keep_current_indices)
+    past_key_values.crop(past_length + len(keep_current_indices))

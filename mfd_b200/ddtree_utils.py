@@ -8,6 +8,7 @@
                        positions_out, mask_out, max_depth)                        patch:1670-1703
   ddtree_follow(*, posterior, verify_ids, parents, window, prefix_lens, <outs>)   patch:1844-1885
   ancestor_visibility_reference(parents)                                          patch:1938-1948
+  DDTreeKVCompactor(kv_pool)(move_src=, move_tgt=)                              patch:1769-1841
 
 The host builder of the reference (C++ on CPU, fed through pinned buffers) becomes the GPU builder, so the
 draft top-k, tree build, verify inputs and walk all stay on the device.
@@ -148,3 +149,35 @@ def ancestor_visibility_reference(parents: torch.Tensor) -> torch.Tensor:
             vis[i, j] = True
             j = p[j] if j > 0 else -1
     return vis
+
+
+class DDTreeKVCompactor:
+    """Commit-time KV moves of DDTree rounds on a token-major pool (patch:1769-1841): only the moves that change a
+    slot, every source read before any store, all of the pool's buffers in one launch (mfd_commit_kv_moves).
+    kv_pool needs `data_ptrs` (device int64 tensor of buffer base addresses) and `data_strides` (bytes per slot,
+    one value, a multiple of 8)."""
+
+    def __init__(self, kv_pool):
+        strides = {int(s) for s in kv_pool.data_strides.tolist()}
+        if len(strides) != 1 or next(iter(strides)) % 8:
+            raise ValueError(f"DDTree KV compaction needs one slot stride (multiple of 8 bytes), got {strides}")
+        self.data_ptrs = kv_pool.data_ptrs
+        self.slot_bytes = next(iter(strides))
+
+    @staticmethod
+    def supports(kv_pool) -> bool:
+        """A plain token-major pool: one slot stride, no per-head layout switch, no scale buffers (the conditions of
+        patch:1797-1807, read from the pool's attributes rather than its class)."""
+        try:
+            strides = {int(s) for s in kv_pool.data_strides.tolist()}
+        except AttributeError:
+            return False
+        return (len(strides) == 1 and next(iter(strides)) % 8 == 0 and not getattr(kv_pool, "use_hnd", False)
+                and not getattr(kv_pool, "use_native_move_kv_cache", False)
+                and getattr(kv_pool, "native_k_scale_buffer", None) is None
+                and getattr(kv_pool, "k_scale_buffer", None) is None and getattr(kv_pool, "layer_num", 1) > 0)
+
+    def __call__(self, *, move_src: torch.Tensor, move_tgt: torch.Tensor) -> None:
+        if move_src.shape[0] == 0:
+            return
+        ops.commit_kv_moves(self.data_ptrs, self.slot_bytes, move_src, move_tgt)

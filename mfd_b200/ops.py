@@ -317,3 +317,69 @@ def tree_prep(x: torch.Tensor, conv_state: torch.Tensor, conv_index: torch.Tenso
                                   k.data_ptr(), v.data_ptr(), stream_ptr(dev))
     check(rc, "mfd_tree_prep")
     return q, k, v
+
+
+# ----------------------------------------------------------------------------------------------- commit step
+
+def _pointer_array(tensors, dev) -> torch.Tensor:
+    return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=dev)
+
+
+def commit_kv_moves(buffers, slot_bytes: int, move_src: torch.Tensor, move_tgt: torch.Tensor) -> None:
+    """The commit step's KV moves in a token-major pool: for request b and i < width, slot move_src[b, i] moves to
+    move_tgt[b, i] in every buffer when they differ, every source read before any store.  buffers: a list of
+    CUDA tensors (one per layer K / V buffer, slot_bytes per slot) or a device int64 tensor of base addresses
+    (the pool's data_ptrs).  move_src, move_tgt [bs, width] int64 on the device.  One launch."""
+    dev = require_cuda(move_src, move_tgt)
+    if isinstance(buffers, torch.Tensor) and buffers.dtype == torch.int64 and buffers.dim() == 1:
+        ptrs = buffers.to(dev)
+    else:
+        buffers = list(buffers)
+        align = 16 if slot_bytes % 16 == 0 else 8
+        for t in buffers:
+            if not t.is_cuda or t.data_ptr() % align:
+                raise RuntimeError(f"commit_kv_moves: buffers must be CUDA tensors aligned to {align} bytes")
+        ptrs = _pointer_array(buffers, dev)
+    src = move_src.to(torch.int64).contiguous()
+    tgt = move_tgt.to(torch.int64).contiguous()
+    if src.shape != tgt.shape or src.dim() != 2:
+        raise RuntimeError("commit_kv_moves: move_src and move_tgt must both be [bs, width]")
+    rc = _lib.lib().mfd_commit_kv_moves(ptrs.data_ptr(), ptrs.numel(), int(slot_bytes), src.data_ptr(),
+                                        tgt.data_ptr(), src.shape[0], src.shape[1], stream_ptr(dev))
+    check(rc, "mfd_commit_kv_moves")
+
+
+def compact_tail(tensors, past_length: int, keep, status: torch.Tensor | None = None) -> None:
+    """Row past_length + keep[i] -> past_length + i along dim -2 of every tensor (HF caches [..., S, D]), in place,
+    all tensors of one layout in one launch; no-op when the appended window is empty or keep is empty or keeps the
+    whole window (the reference's early returns).  keep: a list of ints or a device int64 tensor."""
+    tensors = [t for t in tensors if t is not None and t.numel() > 0]
+    if not tensors:
+        return
+    dev = require_cuda(*tensors)
+    if isinstance(keep, torch.Tensor):
+        keep_t = keep.to(device=dev, dtype=torch.int64).contiguous()
+    else:
+        keep_l = [int(i) for i in keep]
+        S = tensors[0].shape[-2]
+        if any(i < 0 or past_length + i >= S for i in keep_l):
+            raise RuntimeError("compact_tail: keep index outside the appended window")
+        keep_t = torch.tensor(keep_l, dtype=torch.int64, device=dev)
+    groups: dict = {}
+    for t in tensors:
+        if t.dim() < 2 or t.stride(-1) != 1:
+            raise RuntimeError("compact_tail: tensors need a contiguous last dim")
+        outer = t.numel() // (t.shape[-2] * t.shape[-1])
+        try:
+            v = t.view(outer, t.shape[-2], t.shape[-1]) if t.dim() != 3 or outer != t.shape[0] else t
+        except RuntimeError as e:
+            raise RuntimeError("compact_tail: the dims before the last two must collapse into one stride") from e
+        es = t.element_size()
+        key = (tuple(v.shape), v.stride(0) * es, v.stride(1) * es, v.shape[2] * es)
+        groups.setdefault(key, []).append(v)
+    L = _lib.lib()
+    for (shape, outer_stride, row_stride, row_bytes), views in groups.items():
+        ptrs = _pointer_array(views, dev)
+        rc = L.mfd_compact_tail(ptrs.data_ptr(), ptrs.numel(), shape[0], outer_stride, shape[1], row_stride, row_bytes,
+                                int(past_length), keep_t.data_ptr(), keep_t.numel(), ptr(status), stream_ptr(dev))
+        check(rc, "mfd_compact_tail")

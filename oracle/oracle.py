@@ -347,3 +347,31 @@ def tree_prep(x, conv_state, conv_index, conv_w, num_k_heads, num_v_heads, head_
         return a / np.sqrt((a * a).sum(-1, keepdims=True, dtype=np.float32) + np.float32(1e-6), dtype=np.float32)
 
     return bf16_round(l2n(q) * np.float32(scale)), bf16_round(l2n(k)), bf16_round(v)
+
+
+def compact_tail(cache, past_length, keep):
+    """The commit step's cache compaction (inference/hf/ddtree.py:385-403, the index_select path): rows
+    past + keep[i] of dim -2 move to past + i; nothing when the appended window is empty, keep is empty or keep has
+    the window's length.  Returns a new array."""
+    cache = np.asarray(cache)
+    keep = [int(i) for i in keep]
+    cur = cache.shape[-2] - past_length
+    out = cache.copy()
+    if cur <= 0 or len(keep) == 0 or len(keep) == cur:
+        return out
+    tail = cache[..., past_length:, :]
+    out[..., past_length:past_length + len(keep), :] = tail[..., keep, :]
+    return out
+
+
+def commit_kv_moves(pool, move_src, move_tgt):
+    """Token-major pool moves (sglang-v0.5.22-mfd.patch:1769-1841): pool [buffers, slots, ...]; for request b the
+    moves (src, tgt) of row b with src != tgt, every source read before any store.  Requests are taken in order
+    (they own disjoint slots in the callers).  Returns a new array."""
+    out = np.array(pool, copy=True)
+    for b in range(move_src.shape[0]):
+        moves = [(int(s), int(t)) for s, t in zip(move_src[b], move_tgt[b]) if int(s) != int(t)]
+        vals = [out[:, s].copy() for s, _ in moves]
+        for (_, t), v in zip(moves, vals):
+            out[:, t] = v
+    return out

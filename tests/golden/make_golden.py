@@ -12,6 +12,8 @@ Sources of truth, all the reference's own code (imported read-only, never copied
   - inference/hf/mode_attention.py `reference` (float32 masked SDPA);
   - inference/hf/ddtree.py compile_ddtree_tree (the additive verify mask) + torch SDPA in float64;
   - tests/test_gdn_tree_math.py's tree_case inputs and its node-by-node recurrence.
+  - inference/hf/ddtree.py _compact_appended_window / compact_dynamic_cache (the commit step's cache
+    compaction, its index_select path) on CPU tensors and a transformers DynamicCache.
 Inputs are seeded; each fixture stores inputs and expected outputs.  Top-k on CPU leaves equal values in
 unspecified order, so end-to-end (logits -> tree) fixtures use continuous float32 logits (no ties) and the
 tie-heavy cases enter at the candidate level (top-k already given), exactly as the reference's own
@@ -253,6 +255,38 @@ def tree_context_case():
          chain_parents=np.array(cp, np.int64), chain_vis=cv.numpy())
 
 
+def compact_case():
+    """The commit step's cache compaction: ddtree._compact_appended_window (its index_select path) on cache tensors
+    with monotone and permuted keep lists, an empty list and a whole-window list (both early returns), and
+    compact_dynamic_cache on a transformers DynamicCache of two layers."""
+    ddtree._CPP_COMPACT_ENABLED = False
+    g = torch.Generator().manual_seed(17)
+    cases = [((2, 3, 50, 16), 30, [0, 2, 5, 7]), ((1, 4, 40, 8), 25, [6, 1, 0, 9, 3]), ((2, 2, 20, 4), 12, []),
+             ((1, 2, 24, 8), 16, [7, 6, 5, 4, 3, 2, 1, 0]), ((3, 1, 33, 32), 0, [4, 5, 30])]
+    flat = {}
+    for i, (shape, past, keep) in enumerate(cases):
+        x = torch.randn(*shape, generator=g)
+        y = x.clone()
+        ddtree._compact_appended_window(y, past, torch.tensor(keep, dtype=torch.long))
+        flat.update({f"c{i}_in": x.numpy(), f"c{i}_past": np.int64(past), f"c{i}_keep": np.array(keep, np.int64),
+                     f"c{i}_out": y.numpy()})
+    from transformers import DynamicCache
+
+    cache = DynamicCache()
+    ks = [torch.randn(1, 2, 14, 8, generator=g) for _ in range(2)]
+    vs = [torch.randn(1, 2, 14, 8, generator=g) for _ in range(2)]
+    for layer in range(2):
+        cache.update(ks[layer].clone(), vs[layer].clone(), layer)
+    ddtree.compact_dynamic_cache(cache, 9, [0, 3, 4])
+    for layer in range(2):
+        flat[f"dyn_k{layer}_in"], flat[f"dyn_v{layer}_in"] = ks[layer].numpy(), vs[layer].numpy()
+        flat[f"dyn_k{layer}_out"] = cache.layers[layer].keys.numpy()
+        flat[f"dyn_v{layer}_out"] = cache.layers[layer].values.numpy()
+    flat["dyn_past"], flat["dyn_keep"] = np.int64(9), np.array([0, 3, 4], np.int64)
+    flat["dyn_len"] = np.int64(cache.get_seq_length())
+    save("compact_cache.npz", **flat)
+
+
 if __name__ == "__main__":
     build_ref.build()
     mixture_end_to_end()
@@ -263,3 +297,4 @@ if __name__ == "__main__":
     verify_attention_case()
     gdn_case()
     tree_context_case()
+    compact_case()

@@ -1,0 +1,122 @@
+"""GPU parity of the commit step's KV moves (mfd_commit_kv_moves, mfd_compact_tail) against the oracle and the
+reference's own cache compaction (golden fixture).  Bit-exact: the kernels only move bytes."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._golden import load
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def test_compact_tail_vs_reference_fixture():
+    from mfd_b200 import ddtree, ops
+    f = load("compact_cache.npz")
+    i = 0
+    while f"c{i}_in" in f:
+        x = torch.from_numpy(f[f"c{i}_in"]).to(DEV)
+        ddtree._compact_appended_window(x, int(f[f"c{i}_past"]), torch.from_numpy(f[f"c{i}_keep"]).to(DEV))
+        assert np.array_equal(x.cpu().numpy(), f[f"c{i}_out"]), i
+        i += 1
+    assert ops.compact_tail is not None and i == 5
+
+
+class _Layer:
+    def __init__(self, k, v):
+        self.keys, self.values = k, v
+
+
+class _Cache:
+    """The `layers` form of a DynamicCache (keys / values per layer and crop), as compact_dynamic_cache reads it."""
+
+    def __init__(self, ks, vs):
+        self.layers = [_Layer(k, v) for k, v in zip(ks, vs)]
+
+    def crop(self, n):
+        for layer in self.layers:
+            layer.keys = layer.keys[..., :n, :]
+            layer.values = layer.values[..., :n, :]
+
+
+def test_compact_dynamic_cache_vs_reference_fixture():
+    from mfd_b200 import ddtree
+    f = load("compact_cache.npz")
+    ks = [torch.from_numpy(f[f"dyn_k{i}_in"]).to(DEV) for i in range(2)]
+    vs = [torch.from_numpy(f[f"dyn_v{i}_in"]).to(DEV) for i in range(2)]
+    cache = _Cache(ks, vs)
+    ddtree.compact_dynamic_cache(cache, int(f["dyn_past"]), [int(i) for i in f["dyn_keep"]])
+    for i in range(2):
+        assert cache.layers[i].keys.shape[-2] == int(f["dyn_len"])
+        assert np.array_equal(cache.layers[i].keys.cpu().numpy(), f[f"dyn_k{i}_out"])
+        assert np.array_equal(cache.layers[i].values.cpu().numpy(), f[f"dyn_v{i}_out"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_compact_tail_many_layers_one_launch(dtype):
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(3)
+    tensors = [torch.randn(2, 8, 97, 128, generator=g).to(dtype) for _ in range(6)]
+    past = 32
+    keep = [0, 1, 3, 4, 9, 17, 30, 64]  # an accepted path of the 65-node window
+    ref = [oracle.compact_tail(t.float().numpy(), past, keep) for t in tensors]
+    dev = [t.to(DEV) for t in tensors]
+    ops.compact_tail(dev, past, keep)
+    for r, d in zip(ref, dev):
+        assert np.array_equal(d.float().cpu().numpy(), r)
+
+
+def test_compact_tail_edges():
+    from mfd_b200 import ops
+    x = torch.randn(1, 2, 30, 8, device=DEV)
+    y = x.clone()
+    ops.compact_tail([y], 20, [])  # empty keep: no change
+    assert torch.equal(x, y)
+    ops.compact_tail([y], 20, list(range(9, -1, -1)))  # keeps the whole window: no change (early return)
+    assert torch.equal(x, y)
+    ops.compact_tail([y], 30, [])  # empty window
+    assert torch.equal(x, y)
+    with pytest.raises(RuntimeError):
+        ops.compact_tail([y], 20, [10])  # outside the window
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.compact_tail([y], 20, torch.tensor([0, 12], device=DEV), status=st)  # device keep, out of range: flagged
+    assert int(st.item()) != 0
+
+
+@pytest.mark.parametrize("slot_bytes", [2048, 40])
+def test_commit_kv_moves_vs_oracle(slot_bytes):
+    """Three requests owning disjoint slot ranges; move lists with no-ops, a chain of overlapping moves and the
+    zeros past the path (as ddtree_follow writes them); 16-byte and 8-byte slot units."""
+    from mfd_b200 import ddtree_utils, ops
+    g = torch.Generator().manual_seed(slot_bytes)
+    nbuf, nslots, width = 5, 300, 16
+    words = slot_bytes // 8
+    pool = torch.randint(-2**62, 2**62, (nbuf, nslots, words), generator=g, dtype=torch.int64)
+    src = np.zeros((3, width), np.int64)
+    tgt = np.zeros((3, width), np.int64)
+    for b, base in enumerate((10, 110, 200)):
+        path = [base + 40 + j for j in (0, 3, 4, 9, 12)]
+        for i, s in enumerate(path):
+            src[b, i], tgt[b, i] = s, base + 40 + i  # window slot of node -> slot of position i
+        src[b, 5], tgt[b, 5] = base + 2, base + 2   # a no-op
+        src[b, 6], tgt[b, 6] = base + 44, base + 45  # chain: 44 -> 45 while 45 -> ... above
+    ref = oracle.commit_kv_moves(pool.numpy(), src, tgt)
+    bufs = [pool[i].clone().to(DEV) for i in range(nbuf)]
+    ops.commit_kv_moves(bufs, slot_bytes, torch.from_numpy(src).to(DEV), torch.from_numpy(tgt).to(DEV))
+    for i in range(nbuf):
+        assert np.array_equal(bufs[i].cpu().numpy(), ref[i]), i
+
+    class Pool:  # the attributes DDTreeKVCompactor reads from SGLang's MHATokenToKVPool
+        pass
+
+    kv_pool = Pool()
+    bufs2 = [pool[i].clone().to(DEV) for i in range(nbuf)]
+    kv_pool.data_ptrs = torch.tensor([t.data_ptr() for t in bufs2], dtype=torch.int64, device=DEV)
+    kv_pool.data_strides = torch.tensor([slot_bytes] * nbuf, dtype=torch.int64)
+    assert ddtree_utils.DDTreeKVCompactor.supports(kv_pool)
+    ddtree_utils.DDTreeKVCompactor(kv_pool)(move_src=torch.from_numpy(src).to(DEV),
+                                            move_tgt=torch.from_numpy(tgt).to(DEV))
+    for i in range(nbuf):
+        assert np.array_equal(bufs2[i].cpu().numpy(), ref[i]), i
