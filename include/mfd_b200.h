@@ -215,6 +215,29 @@ int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, int64_t outer
                      int64_t row_stride, int64_t row_bytes, int64_t past_length, const int64_t* keep,
                      int64_t keep_count, int* status, void* stream);
 
+/*
+ * Commit step of the Gated-DeltaNet layers: every layer's recurrent state (in place) becomes the state at the
+ * deepest accepted node a = path[path_len - 1]:
+ *   S_a = e^{G_a} S0 + sum_{j in path} e^{G_a - G_j} k_j u_j^T   (value head h reads key head h / (H / HK)).
+ * Per layer (device arrays of base addresses): states [H, Dk, Dv] (state_dtype MFD_F32 or MFD_BF16), u [n, H, Dv]
+ * float32, k [n, HK, Dk] bf16, g_cum [n, H] float32 (the cumulative decays G), all contiguous.  path [path_len]
+ * int64 on the device (1..128 nodes).  Dv <= 256.
+ * Replaces: inference/hf/qwen35_tree.py:122-137 (commit, the state part, over the stacked layers).
+ */
+int mfd_gdn_commit(const uint64_t* states, int state_dtype, const uint64_t* u, const uint64_t* k, const uint64_t* g_cum,
+                   int64_t layers, const int64_t* path, int64_t path_len, int64_t n, int64_t num_heads,
+                   int64_t num_k_heads, int64_t dk, int64_t dv, void* stream);
+
+/*
+ * Commit step of the causal-conv windows: per layer and channel c, column t of conv_states [conv_dim, kernel]
+ * becomes window[t] < kernel ? the old column window[t] : x[window[t] - kernel][c] (x [n, conv_dim], same
+ * element type, elem_bytes 2 or 4), the whole window read before it is written.  window [kernel] int32 on the
+ * device (the accepted node's window, TreeContext.conv_index); kernel <= 8.
+ * Replaces: inference/hf/qwen35_tree.py:138-146 (commit, the conv part).
+ */
+int mfd_conv_commit(const uint64_t* conv_states, const uint64_t* x, int64_t elem_bytes, int64_t layers,
+                    int64_t conv_dim, int64_t kernel, const int32_t* window, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,9 @@ _SIGS = {
                               c_vp, c_vp]),
     "mfd_commit_kv_moves": (c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp]),
     "mfd_compact_tail": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]),
+    "mfd_gdn_commit": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                               c_vp]),
+    "mfd_conv_commit": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
 }
 
 MFD_F32, MFD_BF16, MFD_I32, MFD_I64 = 0, 1, 2, 3

@@ -383,3 +383,56 @@ def compact_tail(tensors, past_length: int, keep, status: torch.Tensor | None = 
         rc = L.mfd_compact_tail(ptrs.data_ptr(), ptrs.numel(), shape[0], outer_stride, shape[1], row_stride, row_bytes,
                                 int(past_length), keep_t.data_ptr(), keep_t.numel(), ptr(status), stream_ptr(dev))
         check(rc, "mfd_compact_tail")
+
+
+def gdn_commit(states, us, ks, gs, path) -> None:
+    """Every layer's recurrent state (in place) -> the state at the deepest accepted node path[-1]:
+    S_a = e^{G_a} S0 + sum_{j in path} e^{G_a - G_j} k_j u_j^T.  states: per layer [H, Dk, Dv] (or [1, H, Dk, Dv])
+    float32 / bf16; us [n, H, Dv] float32, ks [n, HK, Dk] bf16, gs [n, H] float32 per layer; path: list or device
+    int64 tensor.  One launch for all layers."""
+    states = list(states)
+    if not states:
+        return
+    dev = require_cuda(*states)
+    H, Dk, Dv = states[0].shape[-3:]
+    n, HK = ks[0].shape[0], ks[0].shape[1]
+    sdt = states[0].dtype
+    if sdt not in (torch.float32, torch.bfloat16):
+        raise RuntimeError("gdn_commit: states must be float32 or bfloat16")
+    for s_, u_, k_, g_ in zip(states, us, ks, gs):
+        if (not s_.is_contiguous() or s_.dtype != sdt or tuple(s_.shape[-3:]) != (H, Dk, Dv) or s_.numel() != H * Dk * Dv
+                or u_.dtype != torch.float32 or not u_.is_contiguous() or tuple(u_.shape) != (n, H, Dv)
+                or k_.dtype != torch.bfloat16 or not k_.is_contiguous() or tuple(k_.shape) != (n, HK, Dk)
+                or g_.dtype != torch.float32 or not g_.is_contiguous() or tuple(g_.shape) != (n, H)):
+            raise RuntimeError("gdn_commit: per-layer tensors must be contiguous with the documented shapes/dtypes")
+    path_t = path.to(device=dev, dtype=torch.int64).contiguous() if isinstance(path, torch.Tensor) else \
+        torch.tensor([int(i) for i in path], dtype=torch.int64, device=dev)
+    arr = lambda ts: _pointer_array(ts, dev)  # noqa: E731
+    pa, pu, pk, pg = arr(states), arr(us), arr(ks), arr(gs)
+    rc = _lib.lib().mfd_gdn_commit(pa.data_ptr(), MFD_F32 if sdt == torch.float32 else MFD_BF16, pu.data_ptr(),
+                                   pk.data_ptr(), pg.data_ptr(), len(states), path_t.data_ptr(), path_t.numel(), n, H,
+                                   HK, Dk, Dv, stream_ptr(dev))
+    check(rc, "mfd_gdn_commit")
+
+
+def conv_commit(conv_states, xs, window) -> None:
+    """Every layer's conv window (in place): column t = old column window[t] (< kernel) or x[window[t] - kernel].
+    conv_states per layer [conv_dim, kernel] (or [1, conv_dim, kernel]); xs per layer [n, conv_dim] of the same
+    dtype; window: the accepted node's window (list or device int tensor).  One launch for all layers."""
+    conv_states = list(conv_states)
+    if not conv_states:
+        return
+    dev = require_cuda(*conv_states)
+    conv_dim, kernel = conv_states[0].shape[-2:]
+    for c_, x_ in zip(conv_states, xs):
+        if (not c_.is_contiguous() or not x_.is_contiguous() or x_.dtype != c_.dtype or x_.shape[-1] != conv_dim
+                or tuple(c_.shape[-2:]) != (conv_dim, kernel)):
+            raise RuntimeError("conv_commit: conv states [conv_dim, kernel] and inputs [n, conv_dim] of one dtype")
+    win = window.to(device=dev, dtype=torch.int32).contiguous() if isinstance(window, torch.Tensor) else \
+        torch.tensor([int(i) for i in window], dtype=torch.int32, device=dev)
+    # the pointer arrays stay bound until the launch is enqueued (a freed temporary's block could be handed to the
+    # next array, whose upload would overwrite it before the kernel runs)
+    pc, px = _pointer_array(conv_states, dev), _pointer_array(list(xs), dev)
+    rc = _lib.lib().mfd_conv_commit(pc.data_ptr(), px.data_ptr(), conv_states[0].element_size(), len(conv_states),
+                                    conv_dim, kernel, win.data_ptr(), stream_ptr(dev))
+    check(rc, "mfd_conv_commit")

@@ -4,7 +4,7 @@ TreeContext / tree_verify / chain_tree keep the reference's signatures (qwen35_t
 ancestor matrices of the tree and each node's causal-conv window gathered through parent pointers
 (oldest first, indices into [cached conv state ; nodes]).  _tree_forward / install route a patched layer's
 GDN core through mfd_b200.tree_gdn_kernel.tree_gdn (the B200 kernel); commit (the state at the deepest
-accepted node) follows qwen35_tree.py:122-148.
+accepted node and its conv window, qwen35_tree.py:122-148) runs the mfd_gdn_commit / mfd_conv_commit kernels.
 """
 
 from __future__ import annotations
@@ -95,6 +95,29 @@ def install(target) -> int:
         module._tree_patched = True
         count += 1
     return count
+
+
+@torch.no_grad()
+def commit(cache, ctx: TreeContext, accepted: list[int], past_length: int, compact_attention) -> None:
+    """Advance every GDN layer to the deepest accepted node and keep only the accepted KV (qwen35_tree.py:122-148):
+    the states S_a of all layers in one launch (ops.gdn_commit) and their conv windows in another (ops.conv_commit),
+    in place in the cache's own state tensors; then compact_attention(cache, past_length, accepted)."""
+    from . import ops
+
+    layers = sorted(ctx.stash)
+    if layers:
+        last = accepted[-1]
+        n = ctx.anc.shape[0]
+        if any(not (0 <= int(a) < n) for a in accepted):
+            raise RuntimeError("commit: accepted node outside the tree")
+        states = [cache.layers[i].recurrent_states for i in layers]
+        convs = [cache.layers[i].conv_states for i in layers]
+        ops.gdn_commit([s_[0] if s_.dim() == 4 else s_ for s_ in states], [ctx.stash[i][0] for i in layers],
+                       [ctx.stash[i][1] for i in layers], [ctx.stash[i][2] for i in layers], accepted)
+        ops.conv_commit([c_[0] if c_.dim() == 3 else c_ for c_ in convs], [ctx.stash[i][3] for i in layers],
+                        ctx.conv_index[last])
+    ctx.stash.clear()
+    compact_attention(cache, past_length, accepted)
 
 
 @torch.no_grad()

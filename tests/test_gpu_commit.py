@@ -120,3 +120,98 @@ def test_commit_kv_moves_vs_oracle(slot_bytes):
                                             move_tgt=torch.from_numpy(tgt).to(DEV))
     for i in range(nbuf):
         assert np.array_equal(bufs2[i].cpu().numpy(), ref[i]), i
+
+
+# ------------------------------------------------------------------------------------------------ GDN commit
+
+@pytest.mark.parametrize("state_dtype", [torch.float32, torch.bfloat16])
+def test_gdn_commit_matches_node_state_of_the_oracle(state_dtype):
+    """Three layers: each state becomes S at the deepest accepted node, the oracle's per-node state (the formula
+    of inference/hf/qwen35_tree.py:134-137 for every node), within 1e-3 of the state's scale (bf16: its rounding)."""
+    from mfd_b200 import ops
+    from tests.test_gdn import gdn_inputs, random_parents
+    n, H, HK, D = 65, 8, 4, 128
+    parents = random_parents(n, 5)
+    leaf = n - 1
+    path = [leaf]
+    while parents[path[-1]] >= 0:
+        path.append(int(parents[path[-1]]))
+    path = path[::-1]
+    states, us, ks, gs, refs = [], [], [], [], []
+    for layer in range(3):
+        q, k, v, G, beta, s0 = gdn_inputs(n, H, HK, D, parents, 40 + layer, s0_std=0.05)
+        ru, _, rst = oracle.tree_gdn(q.float().numpy(), k.float().numpy(), v.float().numpy(), G.numpy(),
+                                     beta.numpy(), s0.numpy(), parents, emit_states=True)
+        states.append(s0.to(state_dtype).to(DEV))
+        us.append(torch.from_numpy(ru).float().to(DEV))
+        ks.append(k.bfloat16().to(DEV))
+        gs.append(G.float().to(DEV))
+        refs.append(rst[leaf])
+    ops.gdn_commit(states, us, ks, gs, path)
+    for s_, r in zip(states, refs):
+        tol = (1e-3 if state_dtype == torch.float32 else 1e-2) * float(np.abs(r).max())
+        np.testing.assert_allclose(s_.float().cpu().numpy(), r, rtol=0, atol=tol)
+
+
+def test_conv_commit_matches_window_gather():
+    from mfd_b200 import ops, qwen35_tree
+    from tests.test_gdn import random_parents
+    n, conv_dim, kernel = 65, 384, 4
+    parents = list(random_parents(n, 7))
+    ctx = qwen35_tree.TreeContext(parents, torch.from_numpy(oracle.visibility(np.array(parents))).bool(), kernel, DEV)
+    g = torch.Generator().manual_seed(1)
+    for node in (0, 5, n - 1):
+        convs = [torch.randn(conv_dim, kernel, generator=g).bfloat16() for _ in range(2)]
+        xs = [torch.randn(n, conv_dim, generator=g).bfloat16() for _ in range(2)]
+        win = ctx.conv_index_cpu[node]
+        refs = [torch.stack([c[:, i] if i < kernel else x[i - kernel] for i in win], dim=-1) for c, x in zip(convs, xs)]
+        dc = [c.to(DEV) for c in convs]
+        ops.conv_commit(dc, [x.to(DEV) for x in xs], ctx.conv_index[node])
+        for d, r in zip(dc, refs):
+            assert torch.equal(d.cpu(), r), node
+
+
+def test_qwen35_commit_end_to_end():
+    """qwen35_tree.commit on a cache of two GDN layers: states and conv windows as the reference's commit computes
+    them (its torch formula, here qwen35_tree.commit_state and a gather), then compact_attention is called."""
+    from mfd_b200 import qwen35_tree
+    from tests.test_gdn import gdn_inputs, random_parents
+    n, H, HK, D, kernel = 33, 4, 2, 128, 4
+    parents = list(random_parents(n, 9))
+    ctx = qwen35_tree.TreeContext(parents, torch.from_numpy(oracle.visibility(np.array(parents))).bool(), kernel, DEV)
+    conv_dim = (2 * HK + H) * D
+    g = torch.Generator().manual_seed(2)
+
+    class Layer:
+        pass
+
+    class Cache:
+        layers = {}
+
+    cache = Cache()
+    expect = {}
+    leaf = n - 1
+    accepted = [leaf]
+    while parents[accepted[-1]] >= 0:
+        accepted.append(int(parents[accepted[-1]]))
+    accepted = accepted[::-1]
+    for li in (1, 3):
+        q, k, v, G, beta, s0 = gdn_inputs(n, H, HK, D, np.array(parents), li)
+        u = torch.randn(n, H, D, generator=g)
+        x = torch.randn(n, conv_dim, generator=g).bfloat16()
+        layer = Layer()
+        layer.recurrent_states = s0[None].clone().to(DEV)
+        layer.conv_states = torch.randn(1, conv_dim, kernel, generator=g).bfloat16().to(DEV)
+        cache.layers[li] = layer
+        ctx.stash[li] = (u.to(DEV), k.bfloat16().to(DEV), G.float().to(DEV), x.to(DEV))
+        win = ctx.conv_index_cpu[accepted[-1]]
+        conv_old = layer.conv_states[0].cpu()
+        expect[li] = (qwen35_tree.commit_state(s0.to(DEV), u.to(DEV), k.bfloat16().to(DEV), G.to(DEV), accepted).cpu(),
+                      torch.stack([conv_old[:, i] if i < kernel else x[i - kernel] for i in win], dim=-1))
+    called = []
+    qwen35_tree.commit(cache, ctx, accepted, 100, lambda c, past, acc: called.append((past, list(acc))))
+    assert called == [(100, accepted)] and ctx.stash == {}
+    for li, (s_ref, c_ref) in expect.items():
+        torch.testing.assert_close(cache.layers[li].recurrent_states[0].cpu(), s_ref, rtol=0,
+                                   atol=1e-5 * float(s_ref.abs().max()))
+        assert torch.equal(cache.layers[li].conv_states[0].cpu(), c_ref)
