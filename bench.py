@@ -4,7 +4,8 @@
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
     python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
     python bench.py --kernel K                             (one kernel of the batch step alone, L2 flushed between
-                                                            launches: logits_step, tree_build, attention, accept)
+                                                            launches: logits_step, tree_build, attention, accept;
+                                                            or a commit-step kernel: commit_kv, gdn_commit)
 
 Workload (synthetic, seeded per global request id so any partition computes the same
 requests): 32 requests per GPU per step (32/64/128/256 requests at 1/2/4/8 GPUs), each with drafter logits
@@ -325,6 +326,57 @@ def e2e(dev, reqs, prefixes, steps: int, ws: int, chunk: int = 8):
             "d2h_bytes_per_step": out_bytes * ws, "requests_per_step": len(sample) * ws, "ms_per_step": round(ms, 3)}
 
 
+def commit_line(name: str, steps: int, warmup: int, requests: int):
+    """The commit step's kernels alone (synthetic stand-ins of a hybrid target; L2 flushed per launch):
+      commit_kv  -- token-major pool moves: `requests` requests x 16-wide move lists with 8 accepted moves each,
+                    32 buffers (K and V of 16 attention layers) of 2 KB slots (8 KV heads x 128 x bf16);
+      gdn_commit -- 36 GDN layers, states [32, 128, 128] float32, an 8-node accepted path of a 65-node tree, plus
+                    the conv windows [6144, 4] bf16 (mfd_conv_commit)."""
+    from mfd_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    if name == "commit_kv":
+        width, moves, nbuf, slot = 16, 8, 32, 2048
+        per_req = 80
+        slots = requests * per_req
+        bufs = [torch.empty(slots, slot // 2, dtype=torch.bfloat16, device=dev).normal_(generator=g) for _ in range(nbuf)]
+        src = torch.zeros(requests, width, dtype=torch.int64)
+        tgt = torch.zeros(requests, width, dtype=torch.int64)
+        for b in range(requests):
+            base = b * per_req
+            for i in range(moves):
+                src[b, i], tgt[b, i] = base + 10 + 2 * i + 1, base + 10 + i  # node slot -> position slot
+        src, tgt = src.to(dev), tgt.to(dev)
+        ptrs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device=dev)
+        us = timed_us(lambda: ops.commit_kv_moves(ptrs, slot, src, tgt), steps, warmup, flush)
+        alg = requests * moves * nbuf * slot * 2
+        work = f"{requests} requests x {moves} moves x {nbuf} buffers x {slot} B slots"
+    else:
+        layers, H, HK, D, n, plen, conv_dim, kernel = 36, 32, 16, 128, 65, 8, 6144, 4
+        states = [torch.empty(H, D, D, device=dev).normal_(generator=g) for _ in range(layers)]
+        us_ = [torch.empty(n, H, D, device=dev).normal_(generator=g) for _ in range(layers)]
+        ks = [torch.empty(n, HK, D, device=dev).normal_(generator=g).bfloat16() for _ in range(layers)]
+        gs = [torch.empty(n, H, device=dev).uniform_(-2, 0, generator=g) for _ in range(layers)]
+        convs = [torch.empty(conv_dim, kernel, device=dev).normal_(generator=g).bfloat16() for _ in range(layers)]
+        xs = [torch.empty(n, conv_dim, device=dev).normal_(generator=g).bfloat16() for _ in range(layers)]
+        path = torch.tensor([0, 1, 3, 7, 12, 20, 31, 40], dtype=torch.int64, device=dev)
+        window = torch.tensor([kernel + 12, kernel + 20, kernel + 31, kernel + 40], dtype=torch.int32, device=dev)
+
+        def fn():
+            ops.gdn_commit(states, us_, ks, gs, path)
+            ops.conv_commit(convs, xs, window)
+
+        us = timed_us(fn, steps, warmup, flush)
+        alg = layers * (H * D * D * 4 * 2 + plen * (H * D * 4 + HK * D * 2) + conv_dim * kernel * 2 * 2)
+        work = f"{layers} GDN layers x [{H}, {D}, {D}] f32 states, {plen}-node path, conv [{conv_dim}, {kernel}] bf16"
+    return {"kernel": name, "workload": work, "us_per_launch": round(us, 2), "algorithmic_bytes": alg,
+            "achieved_gbs": round(alg / us / 1e3, 1), "peak_hbm_gbs": peaks()["hbm_gbs"],
+            "frac_of_hbm": round(alg / us / 1e3 / peaks()["hbm_gbs"], 4), "l2": "flushed (256 MB write) per launch"}
+
+
 def kernel_line(name: str, steps: int, warmup: int, requests: int):
     """One kernel of the batch step alone, on the batch workload of one GPU (the profiling case of its ncu
     summaries): device time per launch with the L2 flushed (256 MB write) before each."""
@@ -559,7 +611,8 @@ def main():
     ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
     ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
-    ap.add_argument("--kernel", default=None, choices=["logits_step", "tree_build", "attention", "accept"],
+    ap.add_argument("--kernel", default=None,
+                    choices=["logits_step", "tree_build", "attention", "accept", "commit_kv", "gdn_commit"],
                     help="time one kernel of the batch step alone (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -592,7 +645,8 @@ def main():
         return
 
     if args.kernel is not None:
-        print(json.dumps(kernel_line(args.kernel, args.steps, args.warmup, args.requests_per_gpu)))
+        fn = commit_line if args.kernel in ("commit_kv", "gdn_commit") else kernel_line
+        print(json.dumps(fn(args.kernel, args.steps, args.warmup, args.requests_per_gpu)))
         return
 
     if args.config is not None:

@@ -195,7 +195,7 @@ int mfd_tree_prep(const void* x, const void* conv_state, const int32_t* conv_ind
  * (every layer's K and V buffer), each holding slots of slot_bytes (a multiple of 8; the bases 16-byte aligned when
  * slot_bytes is a multiple of 16).  For request b and i < width, slot move_src[b, i] moves to move_tgt[b, i] in
  * every buffer when the two differ; every source is read before any store (a path slot can be another move's
- * target).  move_src, move_tgt [bs, width] int64 on the device.  One launch for all buffers.
+ * target).  move_src, move_tgt [bs, width] int64 on the device (width <= 1024).  One launch for all buffers.
  * Replaces: patch:1769-1841 (DDTreeKVCompactor / _ddtree_compact_kv_kernel).
  */
 int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes, const int64_t* move_src,
@@ -206,8 +206,8 @@ int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t sl
  * as [outer, rows, row_bytes] (outer_stride and row_stride in bytes, multiples of 8).  Row past_length + keep[i]
  * moves to past_length + i for i < keep_count in every buffer and outer index; nothing happens when the appended
  * window rows - past_length is empty, or keep_count is 0 or the whole window (as the reference returns early).
- * keep [keep_count] int64 on the device; status (optional device int) receives MFD_ERR_INVALID for a keep index
- * outside the window (that move is skipped).
+ * keep [keep_count] int64 on the device (keep_count <= 1024); status (optional device int) receives
+ * MFD_ERR_INVALID for a keep index outside the window (that move is skipped).
  * Replaces: inference/hf/ddtree.py:33-61 (compact_tail_inplace), 385-403 (_compact_appended_window), applied by
  *           406-436 (compact_dynamic_cache) to every layer's keys and values.
  */
@@ -221,7 +221,7 @@ int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, int64_t outer
  *   S_a = e^{G_a} S0 + sum_{j in path} e^{G_a - G_j} k_j u_j^T   (value head h reads key head h / (H / HK)).
  * Per layer (device arrays of base addresses): states [H, Dk, Dv] (state_dtype MFD_F32 or MFD_BF16), u [n, H, Dv]
  * float32, k [n, HK, Dk] bf16, g_cum [n, H] float32 (the cumulative decays G), all contiguous.  path [path_len]
- * int64 on the device (1..128 nodes).  Dv <= 256.
+ * int64 on the device (1..128 nodes).  Dv a multiple of 4, <= 256; the state bases 16-byte aligned.
  * Replaces: inference/hf/qwen35_tree.py:122-137 (commit, the state part, over the stacked layers).
  */
 int mfd_gdn_commit(const uint64_t* states, int state_dtype, const uint64_t* u, const uint64_t* k, const uint64_t* g_cum,

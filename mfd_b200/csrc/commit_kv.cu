@@ -22,6 +22,7 @@ namespace ckv {
 
 constexpr int kThreads = 128;
 constexpr int kSmemCap = 96 * 1024;  // staging bytes per CTA (moves x tile)
+constexpr int kMaxMoves = 1024;      // move-list width
 
 struct Params {
     const uint64_t* bufs;    // [nbufs] base addresses
@@ -43,37 +44,50 @@ template <typename U>
 __global__ void __launch_bounds__(kThreads) moves_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     U* stage = reinterpret_cast<U*>(smem_raw);  // [L][tile_units]
+    __shared__ int64_t mv_s[kMaxMoves], mv_t[kMaxMoves];  // the group's effective moves
+    __shared__ int n_moves;
     const int64_t g = blockIdx.x;
     const int buf = blockIdx.y;
     const int64_t u0 = (int64_t)blockIdx.z * p.tile_units;
     const int64_t nu = min((int64_t)p.tile_units, p.slot_units - u0);
     unsigned char* base = reinterpret_cast<unsigned char*>(p.bufs[buf]) + g * p.group_stride;
-    auto move_of = [&](int i, int64_t& s, int64_t& t) -> bool {
+    // the move list, read once in parallel and compacted to the moves that change a slot
+    if (threadIdx.x == 0) n_moves = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.L; i += kThreads) {
+        int64_t s, t;
+        bool ok;
         if (p.keep) {
-            s = p.past + p.keep[i];
+            const int64_t kp = p.keep[i];
+            s = p.past + kp;
             t = p.past + i;
-            if (p.rows > 0 && (p.keep[i] < 0 || s >= p.rows)) {
-                if (p.status) atomicExch(p.status, (int)MFD_ERR_INVALID);
-                return false;
-            }
+            ok = !(p.rows > 0 && (kp < 0 || s >= p.rows));
+            if (!ok && p.status) atomicExch(p.status, (int)MFD_ERR_INVALID);
         } else {
             s = p.src[g * p.list_stride + i];
             t = p.tgt[g * p.list_stride + i];
+            ok = true;
         }
-        return s != t && s >= 0 && t >= 0;
-    };
-    for (int i = 0; i < p.L; ++i) {
-        int64_t s, t;
-        if (!move_of(i, s, t)) continue;  // (uniform over the CTA)
-        const U* from = reinterpret_cast<const U*>(base + s * p.slot_stride) + u0;
-        for (int64_t v = threadIdx.x; v < nu; v += kThreads) stage[(size_t)i * p.tile_units + v] = from[v];
+        if (ok && s != t && s >= 0 && t >= 0) {
+            const int slot = atomicAdd(&n_moves, 1);  // order within the list does not matter: sources are staged
+            mv_s[slot] = s;
+            mv_t[slot] = t;
+        }
     }
     __syncthreads();
-    for (int i = 0; i < p.L; ++i) {
-        int64_t s, t;
-        if (!move_of(i, s, t)) continue;
-        U* to = reinterpret_cast<U*>(base + t * p.slot_stride) + u0;
-        for (int64_t v = threadIdx.x; v < nu; v += kThreads) to[v] = stage[(size_t)i * p.tile_units + v];
+    const int nm = n_moves;
+    // every source of the tile into shared memory (all loads of a thread issued before it waits on any), then
+    // every target
+    for (int64_t e = threadIdx.x; e < (int64_t)nm * nu; e += kThreads) {
+        const int i = (int)(e / nu);
+        const int64_t v = e - (int64_t)i * nu;
+        stage[(size_t)i * p.tile_units + v] = reinterpret_cast<const U*>(base + mv_s[i] * p.slot_stride)[u0 + v];
+    }
+    __syncthreads();
+    for (int64_t e = threadIdx.x; e < (int64_t)nm * nu; e += kThreads) {
+        const int i = (int)(e / nu);
+        const int64_t v = e - (int64_t)i * nu;
+        reinterpret_cast<U*>(base + mv_t[i] * p.slot_stride)[u0 + v] = stage[(size_t)i * p.tile_units + v];
     }
 }
 
@@ -93,23 +107,18 @@ static int launch(Params p, int64_t groups, int64_t nbufs, int64_t slot_bytes, b
     }
     const size_t smem = (size_t)p.L * tile * unit;
     dim3 grid((unsigned)groups, (unsigned)nbufs, (unsigned)tiles);
-    if (aligned16) {
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(moves_kernel<uint4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
-                cudaSuccess) {
-            set_error("%s: cannot raise the shared-memory limit", fn);
-            return MFD_ERR_CUDA;
-        }
-        moves_kernel<uint4><<<grid, kThreads, smem, stream>>>(p);
-    } else {
-        if (smem > 48 * 1024 &&
-            cudaFuncSetAttribute(moves_kernel<uint2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) !=
-                cudaSuccess) {
-            set_error("%s: cannot raise the shared-memory limit", fn);
-            return MFD_ERR_CUDA;
-        }
-        moves_kernel<uint2><<<grid, kThreads, smem, stream>>>(p);
+    // the staging buffer plus the static move lists can pass the 48 KB default: opt in (per device, cheap)
+    cudaError_t e = aligned16
+                        ? cudaFuncSetAttribute(moves_kernel<uint4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap)
+                        : cudaFuncSetAttribute(moves_kernel<uint2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+    if (e != cudaSuccess) {
+        set_error("%s: cannot raise the shared-memory limit: %s", fn, cudaGetErrorString(e));
+        return MFD_ERR_CUDA;
     }
+    if (aligned16)
+        moves_kernel<uint4><<<grid, kThreads, smem, stream>>>(p);
+    else
+        moves_kernel<uint2><<<grid, kThreads, smem, stream>>>(p);
     MFD_CHECK_LAUNCH(fn);
     return MFD_OK;
 }
@@ -122,9 +131,9 @@ using namespace mfd;
 extern "C" int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes,
                                    const int64_t* move_src, const int64_t* move_tgt, int64_t bs, int64_t width,
                                    void* stream) {
-    if (bs < 0 || width < 0 || num_buffers < 0 || slot_bytes <= 0 || slot_bytes % 8 || width > 4096) {
+    if (bs < 0 || width < 0 || num_buffers < 0 || slot_bytes <= 0 || slot_bytes % 8 || width > ckv::kMaxMoves) {
         set_error("mfd_commit_kv_moves: invalid sizes bs=%lld width=%lld buffers=%lld slot_bytes=%lld (a multiple "
-                  "of 8, width <= 4096)",
+                  "of 8, width <= 1024)",
                   (long long)bs, (long long)width, (long long)num_buffers, (long long)slot_bytes);
         return MFD_ERR_INVALID;
     }
@@ -150,7 +159,7 @@ extern "C" int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, in
                                 int64_t rows, int64_t row_stride, int64_t row_bytes, int64_t past_length,
                                 const int64_t* keep, int64_t keep_count, int* status, void* stream) {
     if (num_buffers < 0 || outer < 0 || rows < 0 || past_length < 0 || past_length > rows || keep_count < 0 ||
-        row_bytes <= 0 || row_bytes % 8 || row_stride % 8 || outer_stride % 8 || keep_count > 4096) {
+        row_bytes <= 0 || row_bytes % 8 || row_stride % 8 || outer_stride % 8 || keep_count > ckv::kMaxMoves) {
         set_error("mfd_compact_tail: invalid sizes (buffers %lld, outer %lld, rows %lld, past %lld, keep %lld, row "
                   "bytes %lld)",
                   (long long)num_buffers, (long long)outer, (long long)rows, (long long)past_length,

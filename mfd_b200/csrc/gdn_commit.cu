@@ -26,6 +26,9 @@ struct Params {
     int p, n, H, HK, Dk, Dv;
 };
 
+// CTA = (head, 16 state rows, layer).  Load phase: wk[j][r] = e^{G_a - G_j} k_j[r] and u_j for the path nodes into
+// shared memory.  Then each thread owns float4 chunks of state rows: per path node one broadcast wk and one 16-byte
+// u load feed four FMAs; the state is read and written as coalesced float4 (or 4 x bf16).
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads) state_commit_kernel(Params prm) {
     extern __shared__ __align__(16) float sh[];
@@ -33,10 +36,8 @@ __global__ void __launch_bounds__(kThreads) state_commit_kernel(Params prm) {
     const int p = prm.p, Dk = prm.Dk, Dv = prm.Dv, H = prm.H;
     const int hk = h / (H / prm.HK);
     const int rows = min(kRows, Dk - r0);
-    const int pp = (p + 3) & ~3;
-    float* w = sh;              // [p]: e^{G_a - G_j}
-    float* kk = w + pp;         // [p][kRows]
-    float* uu = kk + pp * kRows;  // [p][Dv]
+    float* wk = sh;                // [p][kRows]
+    float* uu = wk + p * kRows;    // [p][Dv] (16-byte aligned: p * kRows is a multiple of 4)
     __shared__ float ea;
     const float* g = reinterpret_cast<const float*>(prm.g[layer]);
     const float* u = reinterpret_cast<const float*>(prm.u[layer]);
@@ -44,27 +45,55 @@ __global__ void __launch_bounds__(kThreads) state_commit_kernel(Params prm) {
     const int64_t last = prm.path[p - 1];
     const float Ga = g[last * H + h];
     if (threadIdx.x == 0) ea = expf(Ga);
-    for (int j = threadIdx.x; j < p; j += kThreads) w[j] = expf(Ga - g[prm.path[j] * H + h]);
     for (int e = threadIdx.x; e < p * kRows; e += kThreads) {
         const int j = e / kRows, r = e % kRows;
-        kk[e] = r < rows ? __bfloat162float(k[(prm.path[j] * prm.HK + hk) * (int64_t)Dk + r0 + r]) : 0.f;
+        const int64_t node = prm.path[j];
+        const float w = expf(Ga - g[node * H + h]);
+        wk[e] = r < rows ? w * __bfloat162float(k[(node * prm.HK + hk) * (int64_t)Dk + r0 + r]) : 0.f;
     }
-    for (int e = threadIdx.x; e < p * Dv; e += kThreads) {
-        const int j = e / Dv, c = e % Dv;
-        uu[e] = u[(prm.path[j] * H + h) * (int64_t)Dv + c];
+    const int nch = Dv >> 2;  // float4 chunks per row
+    for (int e = threadIdx.x; e < p * nch; e += kThreads) {
+        const int j = e / nch, cc = e % nch;
+        reinterpret_cast<float4*>(uu)[e] = reinterpret_cast<const float4*>(u + (prm.path[j] * H + h) * (int64_t)Dv)[cc];
     }
     __syncthreads();
     unsigned char* sbase = reinterpret_cast<unsigned char*>(prm.states[layer]);
-    for (int e = threadIdx.x; e < rows * Dv; e += kThreads) {
-        const int r = e / Dv, c = e % Dv;
-        const int64_t idx = ((int64_t)h * Dk + r0 + r) * Dv + c;
-        float s0;
-        if (BF16) s0 = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(sbase)[idx]);
-        else s0 = reinterpret_cast<const float*>(sbase)[idx];
-        float acc = ea * s0;
-        for (int j = 0; j < p; ++j) acc = __fmaf_rn(w[j] * kk[j * kRows + r], uu[j * Dv + c], acc);
-        if (BF16) reinterpret_cast<__nv_bfloat16*>(sbase)[idx] = __float2bfloat16_rn(acc);
-        else reinterpret_cast<float*>(sbase)[idx] = acc;
+    for (int e = threadIdx.x; e < rows * nch; e += kThreads) {
+        const int r = e / nch, cc = e % nch;
+        const int64_t idx = ((int64_t)h * Dk + r0 + r) * Dv + 4 * cc;
+        float a[4];
+        if (BF16) {
+            const uint2 v = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(sbase) + idx);
+            a[0] = bf16lo(v.x);
+            a[1] = bf16hi(v.x);
+            a[2] = bf16lo(v.y);
+            a[3] = bf16hi(v.y);
+        } else {
+            const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(sbase) + idx);
+            a[0] = v.x;
+            a[1] = v.y;
+            a[2] = v.z;
+            a[3] = v.w;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) a[q] *= ea;
+        for (int j = 0; j < p; ++j) {
+            const float c = wk[j * kRows + r];
+            const float4 uv = reinterpret_cast<const float4*>(uu)[j * nch + cc];
+            a[0] = __fmaf_rn(c, uv.x, a[0]);
+            a[1] = __fmaf_rn(c, uv.y, a[1]);
+            a[2] = __fmaf_rn(c, uv.z, a[2]);
+            a[3] = __fmaf_rn(c, uv.w, a[3]);
+        }
+        if (BF16) {
+            uint2 v;
+            __nv_bfloat162 lo = __floats2bfloat162_rn(a[0], a[1]), hi = __floats2bfloat162_rn(a[2], a[3]);
+            v.x = *reinterpret_cast<uint32_t*>(&lo);
+            v.y = *reinterpret_cast<uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(sbase) + idx) = v;
+        } else {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(sbase) + idx) = make_float4(a[0], a[1], a[2], a[3]);
+        }
     }
 }
 
@@ -100,9 +129,9 @@ extern "C" int mfd_gdn_commit(const uint64_t* states, int state_dtype, const uin
                               const uint64_t* g_cum, int64_t layers, const int64_t* path, int64_t path_len, int64_t n,
                               int64_t num_heads, int64_t num_k_heads, int64_t dk, int64_t dv, void* stream) {
     if (layers < 0 || path_len < 1 || path_len > gcm::kMaxPath || n < 1 || num_heads < 1 || num_k_heads < 1 ||
-        num_heads % num_k_heads || dk < 1 || dv < 1 || dv > 256 || dk > 65535 * gcm::kRows) {
+        num_heads % num_k_heads || dk < 1 || dv < 4 || dv > 256 || dv % 4 || dk > 65535 * gcm::kRows) {
         set_error("mfd_gdn_commit: invalid sizes layers=%lld path=%lld (1..%d) n=%lld H=%lld HK=%lld Dk=%lld "
-                  "Dv=%lld (<= 256)",
+                  "Dv=%lld (a multiple of 4, <= 256)",
                   (long long)layers, (long long)path_len, gcm::kMaxPath, (long long)n, (long long)num_heads,
                   (long long)num_k_heads, (long long)dk, (long long)dv);
         return MFD_ERR_INVALID;
@@ -122,8 +151,7 @@ extern "C" int mfd_gdn_commit(const uint64_t* states, int state_dtype, const uin
     }
     gcm::Params p{states, u, k, g_cum, path, (int)path_len, (int)n, (int)num_heads, (int)num_k_heads, (int)dk,
                   (int)dv};
-    const int64_t pp = (path_len + 3) & ~3LL;
-    const size_t smem = sizeof(float) * (size_t)(pp + pp * gcm::kRows + path_len * dv);
+    const size_t smem = sizeof(float) * (size_t)(path_len * gcm::kRows + path_len * dv);
     dim3 grid((unsigned)num_heads, (unsigned)((dk + gcm::kRows - 1) / gcm::kRows), (unsigned)layers);
     cudaError_t e;
     if (state_dtype == MFD_BF16) {

@@ -321,8 +321,21 @@ def tree_prep(x: torch.Tensor, conv_state: torch.Tensor, conv_index: torch.Tenso
 
 # ----------------------------------------------------------------------------------------------- commit step
 
-def _pointer_array(tensors, dev) -> torch.Tensor:
-    return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=dev)
+_PTR_CACHE: dict = {}
+
+
+def _pointer_array(tensors, dev, extra=()) -> torch.Tensor:
+    """A device int64 array of the tensors' base addresses (then `extra` values), cached by its contents: a call
+    on the same buffers (a serving loop, a captured graph) copies nothing to the device."""
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
+           tuple(t.data_ptr() for t in tensors) + tuple(int(v) for v in extra))
+    arr = _PTR_CACHE.get(key)
+    if arr is None:
+        if len(_PTR_CACHE) >= 256:
+            _PTR_CACHE.clear()
+        arr = torch.tensor(list(key[1]), dtype=torch.int64, device=dev)
+        _PTR_CACHE[key] = arr
+    return arr
 
 
 def commit_kv_moves(buffers, slot_bytes: int, move_src: torch.Tensor, move_tgt: torch.Tensor) -> None:
@@ -405,13 +418,24 @@ def gdn_commit(states, us, ks, gs, path) -> None:
                 or k_.dtype != torch.bfloat16 or not k_.is_contiguous() or tuple(k_.shape) != (n, HK, Dk)
                 or g_.dtype != torch.float32 or not g_.is_contiguous() or tuple(g_.shape) != (n, H)):
             raise RuntimeError("gdn_commit: per-layer tensors must be contiguous with the documented shapes/dtypes")
-    path_t = path.to(device=dev, dtype=torch.int64).contiguous() if isinstance(path, torch.Tensor) else \
-        torch.tensor([int(i) for i in path], dtype=torch.int64, device=dev)
-    arr = lambda ts: _pointer_array(ts, dev)  # noqa: E731
-    pa, pu, pk, pg = arr(states), arr(us), arr(ks), arr(gs)
-    rc = _lib.lib().mfd_gdn_commit(pa.data_ptr(), MFD_F32 if sdt == torch.float32 else MFD_BF16, pu.data_ptr(),
-                                   pk.data_ptr(), pg.data_ptr(), len(states), path_t.data_ptr(), path_t.numel(), n, H,
-                                   HK, Dk, Dv, stream_ptr(dev))
+        if s_.data_ptr() % 16 or u_.data_ptr() % 16 or Dv % 4:
+            raise RuntimeError("gdn_commit: states and u need 16-byte aligned bases and Dv a multiple of 4")
+    # one device array: the four per-layer address lists, then the path (a device path tensor is used as given)
+    nl = len(states)
+    on_device = isinstance(path, torch.Tensor)
+    if on_device:
+        path_t, plist = path.to(device=dev, dtype=torch.int64).contiguous(), ()
+    else:
+        plist = tuple(int(i) for i in path)
+        if not plist or any(not (0 <= i < n) for i in plist):
+            raise RuntimeError("gdn_commit: the path must be a non-empty list of nodes of the tree")
+    arr = _pointer_array(list(states) + list(us) + list(ks) + list(gs), dev, plist)
+    base = arr.data_ptr()
+    path_ptr = path_t.data_ptr() if on_device else base + 8 * 4 * nl
+    plen = path_t.numel() if on_device else len(plist)
+    rc = _lib.lib().mfd_gdn_commit(base, MFD_F32 if sdt == torch.float32 else MFD_BF16, base + 8 * nl,
+                                   base + 16 * nl, base + 24 * nl, nl, path_ptr, plen, n, H, HK, Dk, Dv,
+                                   stream_ptr(dev))
     check(rc, "mfd_gdn_commit")
 
 
@@ -430,9 +454,9 @@ def conv_commit(conv_states, xs, window) -> None:
             raise RuntimeError("conv_commit: conv states [conv_dim, kernel] and inputs [n, conv_dim] of one dtype")
     win = window.to(device=dev, dtype=torch.int32).contiguous() if isinstance(window, torch.Tensor) else \
         torch.tensor([int(i) for i in window], dtype=torch.int32, device=dev)
-    # the pointer arrays stay bound until the launch is enqueued (a freed temporary's block could be handed to the
-    # next array, whose upload would overwrite it before the kernel runs)
-    pc, px = _pointer_array(conv_states, dev), _pointer_array(list(xs), dev)
-    rc = _lib.lib().mfd_conv_commit(pc.data_ptr(), px.data_ptr(), conv_states[0].element_size(), len(conv_states),
+    # (the pointer array is cached, so it stays alive while the kernel reads it)
+    pa = _pointer_array(conv_states + list(xs), dev)
+    nl = len(conv_states)
+    rc = _lib.lib().mfd_conv_commit(pa.data_ptr(), pa.data_ptr() + 8 * nl, conv_states[0].element_size(), nl,
                                     conv_dim, kernel, win.data_ptr(), stream_ptr(dev))
     check(rc, "mfd_conv_commit")
