@@ -86,8 +86,18 @@ struct Params {
     unsigned int* tickets;   // [bs]
 };
 
-// walk request b along its verified path (one warp); SGLang follow-kernel outputs
-__device__ void walk_request(const Params& p, int64_t b) {
+// Shared-memory staging for the walk: a request's parents, tokens and posterior (widths up to kWalkStage), so
+// that each step of the walk costs shared-memory reads instead of dependent L2 round trips.
+constexpr int kWalkStage = 256;
+struct WalkStage {
+    int64_t tok[kWalkStage];
+    int64_t post[kWalkStage];
+    int32_t par[kWalkStage];
+};
+
+// walk request b along its verified path (one warp); SGLang follow-kernel outputs.  `st`: shared staging
+// (used when the width fits), or null.
+__device__ void walk_request(const Params& p, int64_t b, WalkStage* st) {
     const int lane = threadIdx.x & 31;
     const int64_t W = p.width;
     const int64_t* par = p.parents + b * p.parents_stride;
@@ -95,13 +105,24 @@ __device__ void walk_request(const Params& p, int64_t b) {
     const int64_t* post = p.posterior + b * W;
     const int64_t L = p.out_len;
     const int64_t limit = p.max_steps < 0 ? W : p.max_steps;
+    const bool staged = st != nullptr && W <= kWalkStage;
+    if (staged) {
+        for (int j = lane; j < (int)W; j += 32) {
+            const int64_t pj = __ldcg(par + j);
+            st->par[j] = (pj < -1 || pj >= W) ? -2 : (int32_t)pj;  // out-of-range parents match no node
+            st->tok[j] = __ldcg(tok + j);
+            st->post[j] = __ldcg(post + j);
+        }
+        __syncwarp();
+    }
     int64_t cur = 0, n = 0;
     for (int64_t step = 0; step < limit; ++step) {
-        const int64_t t = __ldcg(post + cur);
+        const int64_t t = staged ? st->post[cur] : __ldcg(post + cur);
         int64_t child = -1;
         for (int64_t base = 1; base < W && child < 0; base += 32) {
             const int64_t j = base + lane;
-            const bool hit = j < W && __ldcg(par + j) == cur && __ldcg(tok + j) == t;
+            const bool hit = j < W && (staged ? (st->par[j] == (int32_t)cur && st->tok[j] == t)
+                                              : (__ldcg(par + j) == cur && __ldcg(tok + j) == t));
             const uint32_t bal = __ballot_sync(MFD_FULL_MASK, hit);
             if (bal) child = base + (__ffs(bal) - 1);
         }
@@ -116,7 +137,7 @@ __device__ void walk_request(const Params& p, int64_t b) {
         }
         cur = child;
     }
-    const int64_t bon = __ldcg(post + cur);
+    const int64_t bon = staged ? st->post[cur] : __ldcg(post + cur);
     if (lane == 0) {
         if (p.accepted) p.accepted[b * L + 0] = 0;
         if (p.hidden_index) p.hidden_index[b * L + 0] = b * W;
@@ -196,6 +217,7 @@ constexpr int kGreedyThreads = 256;
 __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     __shared__ uint64_t red[kGreedyThreads / 32];
     __shared__ int flag;
+    __shared__ WalkStage stage;
     const int64_t row = blockIdx.x / p.parts;
     const int part = blockIdx.x % p.parts;
     const int64_t b = row / p.width;
@@ -239,7 +261,7 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     __syncthreads();
     if (!flag) return;
     __threadfence();
-    if (threadIdx.x < 32) walk_request(p, b);
+    if (threadIdx.x < 32) walk_request(p, b, &stage);
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
@@ -519,14 +541,15 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     __syncthreads();
     if (!flag) return;
     __threadfence();
-    if (threadIdx.x < 32) walk_request(p, b);
+    if (threadIdx.x < 32) walk_request(p, b, sizeof(WalkStage) <= kTableCap * sizeof(double) ? reinterpret_cast<WalkStage*>(table) : nullptr);
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
 // walk only, posterior given (SGLang ddtree_follow)
 __global__ void follow_kernel(Params p) {
+    __shared__ WalkStage stage;
     const int64_t b = (int64_t)blockIdx.x;
-    if (threadIdx.x < 32) walk_request(p, b);
+    if (threadIdx.x < 32) walk_request(p, b, &stage);
 }
 
 }  // namespace accept

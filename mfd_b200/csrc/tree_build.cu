@@ -399,170 +399,501 @@ __global__ void __launch_bounds__(kThreads) build_trees_kernel(Params p) {
 }
 
 // ------------------------------------------------------------------ mixture heap in one thread
-// The same pop order from a binary min-heap kept by one thread in shared memory (keys are unique, so any exact
-// priority queue pops the same sequence): a pop is a sift-down of about log2(live) levels and a push a sift-up,
+// The same pop order from a 4-ary min-heap kept by one thread in shared memory (keys are unique, so any exact
+// priority queue pops the same sequence): a pop is a sift-down of about log4(live) levels and a push a sift-up,
 // with the (parent, token) dedup in a shared-memory hash -- no warp-wide collective on the critical path.
-__global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int b = blockIdx.x;
-    const int K = p.K, L = p.L, k = p.k, B = p.B, W = B + 1;
-    const int cap = K * W;  // live entries never exceed K (B + 1)
-    unsigned char* q = smem_raw;
-    auto take = [&](size_t bytes) {
-        unsigned char* r = q;
-        q += (bytes + 15) & ~(size_t)15;
-        return r;
-    };
-    ulonglong2* he = (ulonglong2*)take(16 * (size_t)cap);  // 4-ary heap: (comparator key, logw bits)
-    uint64_t* hash = (uint64_t*)take(8 * (size_t)p.hcap);
-    float* s_lp = (float*)take(4 * (size_t)K * L * k);
-    int32_t* s_ids = (int32_t*)take(4 * (size_t)K * L * k);
-    int32_t* ntok = (int32_t*)take(4 * (size_t)W);
-    int16_t* npar = (int16_t*)take(2 * (size_t)W);
-    uint8_t* ndep = (uint8_t*)take((size_t)W);
-    float* prior = (float*)take(4 * (size_t)K);
+struct MixSmem {
+    ulonglong2* he;   // [K (B + 1)] heap entries: (comparator key, logw bits)
+    uint64_t* hash;   // [hcap] (token, parent) -> node
+    float* lp;        // [K][L][k]
+    int32_t* ids;     // [K][L][k]
+    int32_t* ntok;    // [B + 1]
+    int16_t* npar;    // [B + 1]
+    uint8_t* ndep;    // [B + 1]
+    float* prior;     // [K]
+};
+
+__device__ __forceinline__ unsigned char* smem_take(unsigned char*& q, size_t bytes) {
+    unsigned char* r = q;
+    q += (bytes + 15) & ~(size_t)15;
+    return r;
+}
+
+__device__ MixSmem carve_mixture(const Params& p, unsigned char*& q) {
+    const int K = p.K, L = p.L, k = p.k, W = p.B + 1;
+    MixSmem s;
+    s.he = (ulonglong2*)smem_take(q, 16 * (size_t)K * W);
+    s.hash = (uint64_t*)smem_take(q, 8 * (size_t)p.hcap);
+    s.lp = (float*)smem_take(q, 4 * (size_t)K * L * k);
+    s.ids = (int32_t*)smem_take(q, 4 * (size_t)K * L * k);
+    s.ntok = (int32_t*)smem_take(q, 4 * (size_t)W);
+    s.npar = (int16_t*)smem_take(q, 2 * (size_t)W);
+    s.ndep = (uint8_t*)smem_take(q, (size_t)W);
+    s.prior = (float*)smem_take(q, 4 * (size_t)K);
+    return s;
+}
+// host mirror of carve_mixture's size
+static size_t mixture_smem_bytes(int K, int L, int k, int B, int hcap) {
+    auto r16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
+    const size_t W = (size_t)B + 1;
+    return r16(16 * (size_t)K * W) + r16(8 * (size_t)hcap) + 2 * r16(4 * (size_t)K * L * k) + r16(4 * W) +
+           r16(2 * W) + r16(W) + r16(4 * (size_t)K);
+}
+
+// Stage tree b's candidate tables and prior in shared memory, clear the dedup hash, set the root node.  All
+// threads of the CTA take part; the caller synchronises afterwards.
+__device__ void stage_mixture(const Params& p, int b, const MixSmem& s) {
+    const int K = p.K, L = p.L, k = p.k;
+    const int nt = blockDim.x;
     const float* glp = p.lp + (size_t)b * K * L * k;
     const void* gids = p.ids_i64 ? (const void*)((const int64_t*)p.ids + (size_t)b * K * L * k)
                                  : (const void*)((const int32_t*)p.ids + (size_t)b * K * L * k);
     const int n_el = K * L * k;
     if ((n_el % 4) == 0 && (((uintptr_t)glp) & 15u) == 0 && (((uintptr_t)gids) & 15u) == 0) {
-        for (int c = threadIdx.x; c < n_el / 4; c += kThreads) {
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_lp + 4 * c)), "l"(glp + 4 * c));
+        for (int c = threadIdx.x; c < n_el / 4; c += nt) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s.lp + 4 * c)), "l"(glp + 4 * c));
             if (!p.ids_i64)
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s_ids + 4 * c)),
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(s.ids + 4 * c)),
                              "l"((const int32_t*)gids + 4 * c));
         }
         asm volatile("cp.async.commit_group;");
         if (p.ids_i64) {
             const longlong2* g2 = (const longlong2*)gids;
 #pragma unroll 4
-            for (int c = threadIdx.x; c < n_el / 2; c += kThreads) {
+            for (int c = threadIdx.x; c < n_el / 2; c += nt) {
                 const longlong2 v = __ldg(g2 + c);
-                s_ids[2 * c] = (int32_t)v.x;
-                s_ids[2 * c + 1] = (int32_t)v.y;
+                s.ids[2 * c] = (int32_t)v.x;
+                s.ids[2 * c + 1] = (int32_t)v.y;
             }
         }
         asm volatile("cp.async.wait_all;");
     } else {
-        for (int i = threadIdx.x; i < n_el; i += kThreads) {
-            s_lp[i] = glp[i];
-            s_ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[i] : ((const int32_t*)gids)[i];
+        for (int i = threadIdx.x; i < n_el; i += nt) {
+            s.lp[i] = glp[i];
+            s.ids[i] = p.ids_i64 ? (int32_t)((const int64_t*)gids)[i] : ((const int32_t*)gids)[i];
         }
     }
-    for (int i = threadIdx.x; i < p.hcap; i += kThreads) hash[i] = kEmptyHash;
-    for (int i = threadIdx.x; i < K; i += kThreads) prior[i] = p.prior ? p.prior[(size_t)b * K + i] : 0.f;
+    for (int i = threadIdx.x; i < p.hcap; i += nt) s.hash[i] = kEmptyHash;
+    for (int i = threadIdx.x; i < K; i += nt) s.prior[i] = p.prior ? p.prior[(size_t)b * K + i] : 0.f;
     if (threadIdx.x == 0) {
-        ntok[0] = 0;
-        npar[0] = -1;
-        ndep[0] = 0;
+        s.ntok[0] = 0;
+        s.npar[0] = -1;
+        s.ndep[0] = 0;
     }
-    __syncthreads();
-    __shared__ int sh_count, sh_fail;
-    if (threadIdx.x == 0) {
-        int n = 0;  // live entries
-        auto mix_comp = [&](double w, int m, uint32_t ax) -> uint64_t {
-            float key = -(__double2float_rn(w) + prior[m]);
-            key = key + 0.0f;  // -0.0 and +0.0 compare equal in the reference: fold them
-            return ((uint64_t)ord_f32(key) << 32) | ax;
-        };
-        // a 4-ary min-heap of 16-byte entries: children of i are 4i+1 .. 4i+4, so about 3 levels for the at most
-        // K (B + 1) live entries, and the four children of a level are loaded together
-        auto push = [&](uint64_t c, double w) {
-            int i = n++;
-            while (i > 0) {
-                const int par = (i - 1) >> 2;
-                const ulonglong2 pe = he[par];
-                if (pe.x <= c) break;
-                he[i] = pe;
-                i = par;
-            }
-            he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
-        };
-        // replace the root by (c, w) and sift it down
-        auto replace_top = [&](uint64_t c, double w) {
-            int i = 0;
-            for (;;) {
-                const int l = 4 * i + 1;
-                if (l >= n) break;
-                ulonglong2 e[4];
+}
+
+// The mixture key of an entry: -(float(logw) + prior[mode]) (hf/tree_build_ext.py:167), -0.0 folded into +0.0
+// (they compare equal in the reference), as an orderable uint32.
+__device__ __forceinline__ uint32_t mix_key(double w, float prior_m) {
+    float key = -(__double2float_rn(w) + prior_m);
+    key = key + 0.0f;
+    return ord_f32(key);
+}
+
+// The reference's mixture heap (hf/tree_build_ext.py:158-203), run by one thread over the staged tables.
+// Returns the node count; *fail is set when the dedup hash overflows.
+__device__ int serial_mixture(const Params& p, const MixSmem& s, int* fail) {
+    const int K = p.K, L = p.L, k = p.k, B = p.B;
+    ulonglong2* he = s.he;
+    int n = 0;  // live entries
+    auto comp = [&](double w, int m, uint32_t ax) -> uint64_t { return ((uint64_t)mix_key(w, s.prior[m]) << 32) | ax; };
+    // a 4-ary min-heap of 16-byte entries: children of i are 4i+1 .. 4i+4, so about 3 levels for the at most
+    // K (B + 1) live entries, and the four children of a level are loaded together
+    auto push = [&](uint64_t c, double w) {
+        int i = n++;
+        while (i > 0) {
+            const int par = (i - 1) >> 2;
+            const ulonglong2 pe = he[par];
+            if (pe.x <= c) break;
+            he[i] = pe;
+            i = par;
+        }
+        he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
+    };
+    // replace the root by (c, w) and sift it down
+    auto replace_top = [&](uint64_t c, double w) {
+        int i = 0;
+        for (;;) {
+            const int l = 4 * i + 1;
+            if (l >= n) break;
+            ulonglong2 e[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) e[t] = l + t < n ? he[l + t] : make_ulonglong2(~0ull, 0ull);
-                int j = l;
-                ulonglong2 best = e[0];
+            for (int t = 0; t < 4; ++t) e[t] = l + t < n ? he[l + t] : make_ulonglong2(~0ull, 0ull);
+            int j = l;
+            ulonglong2 best = e[0];
 #pragma unroll
-                for (int t = 1; t < 4; ++t)
-                    if (e[t].x < best.x) {
-                        best = e[t];
-                        j = l + t;
-                    }
-                if (c <= best.x) break;
-                he[i] = best;
-                i = j;
-            }
-            he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
-        };
-        int count = 0, fail = 0;
-        if (B > 0 && L > 0)
-            for (int m = 0; m < K; ++m) {
-                const double w = (double)s_lp[(m * L) * k];
-                push(mix_comp(w, m, pack_aux(m, 0, 1, 0)), w);
-            }
-        while (n > 0 && count < B) {
-            const ulonglong2 top = he[0];
-            const uint64_t M = top.x;
-            const double lwp = __longlong_as_double((long long)top.y);
-            const uint32_t ax = (uint32_t)M;
-            const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
-            const int row = (m * L + dep - 1) * k;
-            const int32_t token = s_ids[row + rk];
-            const bool has_sib = rk + 1 < k, has_child = dep < L;
-            const float lp_r = s_lp[row + rk];
-            const float lp_r1 = has_sib ? s_lp[row + rk + 1] : 0.f;
-            const float lp_c = has_child ? s_lp[row + k] : 0.f;
-            // node: dedup by (parent, token)
-            const uint64_t want = ((uint64_t)(uint32_t)token << 32) | ((uint64_t)(uint32_t)par << 16);
-            uint32_t h = (uint32_t)(((uint64_t)(uint32_t)token * 0x9E3779B1u) ^ ((uint32_t)par * 0x85EBCA77u));
-            int current = -1;
-            for (int t = 0; t < p.hcap; ++t) {
-                const uint32_t hs = (h + (uint32_t)t) & (uint32_t)(p.hcap - 1);
-                const uint64_t v = hash[hs];
-                if (v == kEmptyHash) {
-                    current = count + 1;
-                    hash[hs] = want | (uint64_t)(uint32_t)current;
-                    ntok[current] = token;
-                    npar[current] = (int16_t)par;
-                    ndep[current] = (uint8_t)dep;
-                    ++count;
-                    break;
+            for (int t = 1; t < 4; ++t)
+                if (e[t].x < best.x) {
+                    best = e[t];
+                    j = l + t;
                 }
-                if ((v & ~0xffffull) == want) {
-                    current = (int)(v & 0xffffu);
-                    break;
-                }
-            }
-            if (current < 0) {
-                fail = 1;
+            if (c <= best.x) break;
+            he[i] = best;
+            i = j;
+        }
+        he[i] = make_ulonglong2(c, (unsigned long long)__double_as_longlong(w));
+    };
+    int count = 0;
+    *fail = 0;
+    if (B > 0 && L > 0)
+        for (int m = 0; m < K; ++m) {
+            const double w = (double)s.lp[(m * L) * k];
+            push(comp(w, m, pack_aux(m, 0, 1, 0)), w);
+        }
+    while (n > 0 && count < B) {
+        const ulonglong2 top = he[0];
+        const uint64_t M = top.x;
+        const double lwp = __longlong_as_double((long long)top.y);
+        const uint32_t ax = (uint32_t)M;
+        const int m = ax >> 28, par = (ax >> 16) & 0xfff, dep = (ax >> 11) & 31, rk = ax & 0x7ff;
+        const int row = (m * L + dep - 1) * k;
+        const int32_t token = s.ids[row + rk];
+        const bool has_sib = rk + 1 < k, has_child = dep < L;
+        const float lp_r = s.lp[row + rk];
+        const float lp_r1 = has_sib ? s.lp[row + rk + 1] : 0.f;
+        const float lp_c = has_child ? s.lp[row + k] : 0.f;
+        // node: dedup by (parent, token)
+        const uint64_t want = ((uint64_t)(uint32_t)token << 32) | ((uint64_t)(uint32_t)par << 16);
+        uint32_t h = (uint32_t)(((uint64_t)(uint32_t)token * 0x9E3779B1u) ^ ((uint32_t)par * 0x85EBCA77u));
+        int current = -1;
+        for (int t = 0; t < p.hcap; ++t) {
+            const uint32_t hs = (h + (uint32_t)t) & (uint32_t)(p.hcap - 1);
+            const uint64_t v = s.hash[hs];
+            if (v == kEmptyHash) {
+                current = count + 1;
+                s.hash[hs] = want | (uint64_t)(uint32_t)current;
+                s.ntok[current] = token;
+                s.npar[current] = (int16_t)par;
+                s.ndep[current] = (uint8_t)dep;
+                ++count;
                 break;
             }
-            // successors: the sibling replaces the popped root, the child is pushed
-            if (has_sib) {
-                const double slw = (lwp - (double)lp_r) + (double)lp_r1;
-                replace_top(mix_comp(slw, m, pack_aux(m, par, dep, rk + 1)), slw);
-            } else {
-                --n;
-                if (n > 0) replace_top(he[n].x, __longlong_as_double((long long)he[n].y));
-            }
-            if (has_child) {
-                const double clw = lwp + (double)lp_c;
-                push(mix_comp(clw, m, pack_aux(m, current, dep + 1, 0)), clw);
+            if ((v & ~0xffffull) == want) {
+                current = (int)(v & 0xffffu);
+                break;
             }
         }
-        sh_count = count;
+        if (current < 0) {
+            *fail = 1;
+            break;
+        }
+        // successors: the sibling replaces the popped root, the child is pushed
+        if (has_sib) {
+            const double slw = (lwp - (double)lp_r) + (double)lp_r1;
+            replace_top(comp(slw, m, pack_aux(m, par, dep, rk + 1)), slw);
+        } else {
+            --n;
+            if (n > 0) replace_top(he[n].x, __longlong_as_double((long long)he[n].y));
+        }
+        if (has_child) {
+            const double clw = lwp + (double)lp_c;
+            push(comp(clw, m, pack_aux(m, current, dep + 1, 0)), clw);
+        }
+    }
+    return count;
+}
+
+__global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int sh_count, sh_fail;
+    const int b = blockIdx.x;
+    unsigned char* q = smem_raw;
+    const MixSmem s = carve_mixture(p, q);
+    stage_mixture(p, b, s);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int fail = 0;
+        sh_count = serial_mixture(p, s, &fail);
         sh_fail = fail;
     }
     __syncthreads();
     if (sh_fail && threadIdx.x == 0 && p.status) atomicExch(p.status, (int)MFD_ERR_CAPACITY);
-    write_tree_outputs(p, b, sh_count, ntok, npar, ndep);
+    write_tree_outputs(p, b, sh_count, s.ntok, s.npar, s.ndep);
+}
+
+// ------------------------------------------------------------------ mixture tree, one warp per mode
+// The heap pops entries in the order of the tuple (key, mode, parent, depth, rank).  An entry's successors (its
+// sibling and its first child) never have a smaller key than the entry itself, so the pop order is that sorted
+// order, and restricted to one mode it is the best-first enumeration of that mode alone -- except where two live
+// entries of one mode have equal keys (their order then depends on global node ids).  This kernel therefore:
+//   1. runs the K modes' enumerations at once, one warp per mode: the mode's live entries (one per open sibling
+//      group, at most B + 1) sit in registers, three per lane, and a pop is a warp-wide minimum (redux.sync) and
+//      two successor updates; each mode pops at most B entries, enough because the first B distinct nodes of the
+//      mixture contain at most B entries of any mode;
+//   2. ranks every popped entry in the merged order (key, then mode) by binary searches in the other modes' lists;
+//   3. merges equal prefixes exactly, depth by depth: an entry's prefix is (its parent's prefix, its token), named
+//      by the merged position of its first occurrence, through a shared-memory hash with atomicCAS / atomicMin;
+//   4. numbers the first occurrences in merged order: the first B are the nodes, in the heap's pop order.
+// A mode whose warp minimum is not unique (an exact key tie), or a successor with a smaller key than its
+// generator (double rounding of equal log-probabilities), sends the whole tree to serial_mixture, which replays
+// the reference heap exactly.  Limits: K <= 16, B <= 95 (three groups per lane).
+constexpr int kFastThreads = 512;
+constexpr int kFastSlots = 3;
+constexpr uint32_t kNoKey = 0xffffffffu;
+constexpr int kFastMaxB = 32 * kFastSlots - 1;
+
+struct FastSmem {
+    uint32_t* ekey;   // [K][B] popped keys, in each mode's pop order (non-decreasing)
+    int32_t* etok;    // [K][B] token
+    int16_t* epl;     // [K][B] pop index of the parent entry in the same mode (-1: the root)
+    uint8_t* edep;    // [K][B] depth
+    int16_t* epos;    // [K][B] merged position
+    int16_t* ecan;    // [K][B] merged position of the first occurrence of the entry's prefix
+    int16_t* eslot;   // [K][B] dedup hash slot
+    int16_t* pnid;    // [K B] node id by merged position (0: not a node)
+    uint64_t* dkey;   // [dcap] dedup keys ((parent prefix + 1) << 32 | token)
+    int32_t* dval;    // [dcap] least merged position holding the key
+};
+
+__device__ FastSmem carve_fast(const Params& p, unsigned char*& q, int dcap) {
+    const size_t KB = (size_t)p.K * p.B;
+    FastSmem f;
+    f.dkey = (uint64_t*)smem_take(q, 8 * (size_t)dcap);
+    f.dval = (int32_t*)smem_take(q, 4 * (size_t)dcap);
+    f.ekey = (uint32_t*)smem_take(q, 4 * KB);
+    f.etok = (int32_t*)smem_take(q, 4 * KB);
+    f.epl = (int16_t*)smem_take(q, 2 * KB);
+    f.epos = (int16_t*)smem_take(q, 2 * KB);
+    f.ecan = (int16_t*)smem_take(q, 2 * KB);
+    f.eslot = (int16_t*)smem_take(q, 2 * KB);
+    f.pnid = (int16_t*)smem_take(q, 2 * KB);
+    f.edep = (uint8_t*)smem_take(q, KB);
+    return f;
+}
+static size_t fast_smem_bytes(int K, int B, int dcap) {
+    auto r16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
+    const size_t KB = (size_t)K * B;
+    return r16(8 * (size_t)dcap) + r16(4 * (size_t)dcap) + 2 * r16(4 * KB) + 5 * r16(2 * KB) + r16(KB);
+}
+__host__ __device__ inline int fast_dcap(int K, int B) {
+    int d = 64;
+    while (d < 2 * K * B) d <<= 1;
+    return d;
+}
+
+__global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ int sh_cnt[16], sh_off[17], sh_maxdep[16];
+    __shared__ int sh_bad, sh_count, sh_fail, sh_wsum[kFastThreads / 32];
+    const int b = blockIdx.x;
+    const int K = p.K, L = p.L, k = p.k, B = p.B;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int dcap = fast_dcap(K, B);
+    unsigned char* q = smem_raw;
+    const MixSmem s = carve_mixture(p, q);
+    const FastSmem f = carve_fast(p, q, dcap);
+    stage_mixture(p, b, s);
+    for (int i = threadIdx.x; i < dcap; i += kFastThreads) {
+        f.dkey[i] = kEmptyHash;
+        f.dval[i] = 0x7fffffff;
+    }
+    if (threadIdx.x == 0) sh_bad = 0;
+    __syncthreads();
+
+    // ---- 1. per-mode best-first enumeration, warp m = mode m
+    if (warp < K) {
+        const int m = warp;
+        const float pr = s.prior[m];
+        // three live-entry slots per lane, as scalars (slot t of lane l holds group 32 t + l)
+        uint32_t k0 = kNoKey, k1 = kNoKey, k2 = kNoKey;
+        double w0 = 0.0, w1 = 0.0, w2 = 0.0;
+        int r0 = 0, r1 = 0, r2 = 0, d0 = 0, d1 = 0, d2 = 0, q0 = 0, q1 = 0, q2 = 0;
+        if (lane == 0) {  // group 0: the root's children, rank 0 first
+            w0 = (double)s.lp[(m * L) * k];
+            k0 = mix_key(w0, pr);
+            d0 = 1;
+            q0 = -1;
+        }
+        int groups = 1, i = 0, bad = 0, maxdep = 0;
+        uint32_t* ekey = f.ekey + m * B;
+        for (; i < B; ++i) {
+            const uint32_t lmin = min(k0, min(k1, k2));
+            const uint32_t wmin = __reduce_min_sync(MFD_FULL_MASK, lmin);
+            if (wmin == kNoKey) break;
+            const int mine = (k0 == wmin) + (k1 == wmin) + (k2 == wmin);
+            const uint32_t bal = __ballot_sync(MFD_FULL_MASK, mine > 0);
+            if (__popc(bal) > 1 || __any_sync(MFD_FULL_MASK, mine > 1)) {  // an exact tie inside the mode
+                bad = 1;
+                break;
+            }
+            const int owner = __ffs(bal) - 1;
+            double plw = 0.0;
+            int pdep = 0;
+            if (lane == owner) {
+                const int sl = k0 == wmin ? 0 : (k1 == wmin ? 1 : 2);
+                const double w = sl == 0 ? w0 : (sl == 1 ? w1 : w2);
+                const int r = sl == 0 ? r0 : (sl == 1 ? r1 : r2);
+                const int d = sl == 0 ? d0 : (sl == 1 ? d1 : d2);
+                const int par = sl == 0 ? q0 : (sl == 1 ? q1 : q2);
+                const int row = (m * L + d - 1) * k;
+                const float lp_r = s.lp[row + r];
+                ekey[i] = wmin;
+                f.etok[m * B + i] = s.ids[row + r];
+                f.epl[m * B + i] = (int16_t)par;
+                f.edep[m * B + i] = (uint8_t)d;
+                uint32_t nk = kNoKey;
+                double nw = 0.0;
+                if (r + 1 < k) {  // the sibling: (logw - lp[rank]) + lp[rank + 1] in double
+                    nw = (w - (double)lp_r) + (double)s.lp[row + r + 1];
+                    nk = mix_key(nw, pr);
+                    if (nk < wmin) bad = 1;
+                }
+                if (sl == 0) { k0 = nk; w0 = nw; r0 = r + 1; }
+                else if (sl == 1) { k1 = nk; w1 = nw; r1 = r + 1; }
+                else { k2 = nk; w2 = nw; r2 = r + 1; }
+                plw = w;
+                pdep = d;
+            }
+            plw = __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(plw), owner));
+            pdep = __shfl_sync(MFD_FULL_MASK, pdep, owner);
+            maxdep = max(maxdep, pdep);
+            if (pdep < L) {  // the popped entry's first child opens a new group: logw + lp[depth][0]
+                const int g = groups++;
+                if (lane == (g & 31)) {
+                    const double cw = plw + (double)s.lp[(m * L + pdep) * k];
+                    const uint32_t ck = mix_key(cw, pr);
+                    if (ck < wmin) bad = 1;
+                    const int sl = g >> 5;
+                    if (sl == 0) { k0 = ck; w0 = cw; r0 = 0; d0 = pdep + 1; q0 = i; }
+                    else if (sl == 1) { k1 = ck; w1 = cw; r1 = 0; d1 = pdep + 1; q1 = i; }
+                    else { k2 = ck; w2 = cw; r2 = 0; d2 = pdep + 1; q2 = i; }
+                }
+            }
+        }
+        bad = __any_sync(MFD_FULL_MASK, bad);
+        if (lane == 0) {
+            sh_cnt[m] = i;
+            sh_maxdep[m] = maxdep;
+            if (bad) atomicOr(&sh_bad, 1);
+        }
+    }
+    __syncthreads();
+    if (sh_bad) {  // replay the reference heap in one thread
+        if (threadIdx.x == 0) {
+            int fail = 0;
+            sh_count = serial_mixture(p, s, &fail);
+            sh_fail = fail;
+        }
+        __syncthreads();
+        if (sh_fail && threadIdx.x == 0 && p.status) atomicExch(p.status, (int)MFD_ERR_CAPACITY);
+        if (threadIdx.x < kThreads) write_tree_outputs(p, b, sh_count, s.ntok, s.npar, s.ndep);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        int o = 0, md = 0;
+        for (int m = 0; m < K; ++m) {
+            sh_off[m] = o;
+            o += sh_cnt[m];
+            md = max(md, sh_maxdep[m]);
+        }
+        sh_off[K] = o;
+        sh_maxdep[0] = md;
+    }
+    __syncthreads();
+    const int N = sh_off[K];
+    const int maxdep = sh_maxdep[0];
+    auto locate = [&](int e, int& m, int& i) {  // flat entry -> (mode, pop index)
+        m = 0;
+        while (m + 1 < K && sh_off[m + 1] <= e) ++m;
+        i = e - sh_off[m];
+    };
+
+    // ---- 2. merged positions: (key, mode) order
+    for (int e = threadIdx.x; e < N; e += kFastThreads) {
+        int m, i;
+        locate(e, m, i);
+        const uint32_t kv = f.ekey[m * B + i];
+        int pos = i;
+        for (int m2 = 0; m2 < K; ++m2) {
+            if (m2 == m) continue;
+            const uint32_t* ek = f.ekey + m2 * B;
+            int lo = 0, hi = sh_cnt[m2];  // count of keys < kv (m2 > m) or <= kv (m2 < m)
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                const uint32_t v = ek[mid];
+                if (v < kv || (m2 < m && v == kv)) lo = mid + 1;
+                else hi = mid;
+            }
+            pos += lo;
+        }
+        f.epos[m * B + i] = (int16_t)pos;
+    }
+    __syncthreads();
+
+    // ---- 3. equal prefixes, depth by depth
+    for (int d = 1; d <= maxdep; ++d) {
+        for (int e = threadIdx.x; e < N; e += kFastThreads) {
+            int m, i;
+            locate(e, m, i);
+            const int x = m * B + i;
+            if (f.edep[x] != d) continue;
+            const int pc = f.epl[x] < 0 ? -1 : (int)f.ecan[m * B + f.epl[x]];
+            const uint64_t dk = ((uint64_t)(uint32_t)(pc + 1) << 32) | (uint32_t)f.etok[x];
+            uint32_t h = (uint32_t)((dk * 0x9E3779B97F4A7C15ull) >> 32) & (uint32_t)(dcap - 1);
+            for (int t = 0; t < dcap; ++t) {
+                const unsigned long long prev =
+                    atomicCAS((unsigned long long*)&f.dkey[h], (unsigned long long)kEmptyHash, (unsigned long long)dk);
+                if (prev == kEmptyHash || prev == dk) break;
+                h = (h + 1) & (uint32_t)(dcap - 1);
+            }
+            atomicMin(&f.dval[h], (int)f.epos[x]);
+            f.eslot[x] = (int16_t)h;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < N; e += kFastThreads) {
+            int m, i;
+            locate(e, m, i);
+            const int x = m * B + i;
+            if (f.edep[x] == d) f.ecan[x] = (int16_t)f.dval[f.eslot[x]];
+        }
+        __syncthreads();
+    }
+
+    // ---- 4. node ids: first occurrences numbered in merged order
+    for (int e = threadIdx.x; e < N; e += kFastThreads) {
+        int m, i;
+        locate(e, m, i);
+        const int x = m * B + i;
+        f.pnid[f.epos[x]] = (int16_t)(f.ecan[x] == f.epos[x] ? 1 : 0);
+    }
+    __syncthreads();
+    {
+        const int per = (N + kFastThreads - 1) / kFastThreads;
+        const int p0 = min(N, (int)threadIdx.x * per), p1 = min(N, p0 + per);
+        int local = 0;
+        for (int x = p0; x < p1; ++x) local += f.pnid[x];
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(MFD_FULL_MASK, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) sh_wsum[warp] = incl;
+        __syncthreads();
+        int base = 0;
+        for (int w = 0; w < warp; ++w) base += sh_wsum[w];
+        int run = base + incl - local;
+        for (int x = p0; x < p1; ++x) {
+            const int fl = f.pnid[x];
+            f.pnid[x] = (int16_t)(fl ? run + 1 : 0);
+            run += fl;
+        }
+        if (threadIdx.x == kFastThreads - 1) sh_count = min(run, B);
+    }
+    __syncthreads();
+    const int count = sh_count;
+    for (int e = threadIdx.x; e < N; e += kFastThreads) {
+        int m, i;
+        locate(e, m, i);
+        const int x = m * B + i;
+        const int nid = f.pnid[f.epos[x]];
+        if (nid == 0 || nid > count) continue;
+        s.ntok[nid] = f.etok[x];
+        s.ndep[nid] = f.edep[x];
+        s.npar[nid] = (int16_t)(f.epl[x] < 0 ? 0 : f.pnid[f.ecan[m * B + f.epl[x]]]);
+    }
+    __syncthreads();
+    if (threadIdx.x < kThreads) write_tree_outputs(p, b, count, s.ntok, s.npar, s.ndep);
 }
 
 struct Plan {
@@ -650,8 +981,23 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
     p.anc = anc_bits;
     p.vis = visibility;
     p.status = status;
-    const size_t h1_smem = (size_t)16 * num_modes * W + (size_t)pl.hcap * 8 + (size_t)8 * num_modes * depth_limit * topk +
-                           (size_t)W * 7 + (size_t)num_modes * 4 + 160;
+    const size_t h1_smem = tree::mixture_smem_bytes((int)num_modes, (int)depth_limit, (int)topk, (int)budget, pl.hcap) + 64;
+    if (!single && depth_limit > 0 && budget > 0 && num_modes <= 16 && budget <= tree::kFastMaxB) {
+        // one warp per mode, exact merge (the serial heap replays trees with exact key ties)
+        const int dcap = tree::fast_dcap((int)num_modes, (int)budget);
+        const size_t fsmem = h1_smem + tree::fast_smem_bytes((int)num_modes, (int)budget, dcap);
+        if (fsmem <= 220 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(tree::mixture_fast_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
+            if (e != cudaSuccess) {
+                set_error("mfd_build_trees: %s", cudaGetErrorString(e));
+                return MFD_ERR_CUDA;
+            }
+            tree::mixture_fast_kernel<<<(unsigned)bs, tree::kFastThreads, fsmem, (cudaStream_t)stream>>>(p);
+            MFD_CHECK_LAUNCH("mfd_build_trees");
+            return MFD_OK;
+        }
+    }
     if (!single && depth_limit > 0 && budget > 0 && h1_smem <= 220 * 1024) {  // the mixture heap in one thread
         cudaError_t e = cudaFuncSetAttribute(tree::mixture_heap1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)h1_smem);

@@ -190,3 +190,55 @@ def test_single_mode_heap_matches_reference_on_ties():
         tok, dep, par = oracle.build_single(lp.numpy(), ids.numpy(), 16)
         assert np.array_equal(got[0].numpy(), tok) and np.array_equal(got[1].numpy(), dep)
         assert list(got[2]) == par.tolist()
+
+
+def _candidate_tables(g, K, L, k, vocab, kind):
+    """Sorted per-(mode, depth) candidate log-probabilities [K, L, k] f32 and distinct ids per row [K, L, k] i64,
+    drawn from a small vocabulary so that modes share prefixes (duplicates across modes)."""
+    scale = {"peaked": 4.0, "flat": 0.3}.get(kind, 1.5)
+    x = torch.randn(K, L, vocab, generator=g) * scale
+    if kind == "peaked":
+        x[..., 0] += 12.0
+    lp_full = torch.log_softmax(x, -1)
+    top, idx = torch.topk(lp_full, k, dim=-1)
+    perm = torch.stack([torch.randperm(vocab, generator=g) for _ in range(K * L)]).view(K, L, vocab)
+    ids = torch.gather(perm, 2, idx)
+    if kind == "quantized":  # exact ties inside modes (the heap's global tie-breaks decide)
+        top = (top * 2).round() / 2
+    if kind == "dup_modes" and K > 1:  # identical modes: every entry ties across modes
+        top[1] = top[0]
+        ids[1] = ids[0]
+    return top.float().contiguous(), ids.long().contiguous()
+
+
+@pytest.mark.parametrize("K,L,k,B", [(8, 16, 64, 64), (8, 15, 64, 64), (1, 16, 64, 64), (2, 3, 5, 40),
+                                     (3, 5, 16, 95), (16, 16, 32, 64), (8, 4, 64, 96), (8, 16, 64, 200),
+                                     (5, 1, 7, 30), (4, 31, 3, 50), (8, 16, 1, 10)])
+@pytest.mark.parametrize("kind", ["normal", "peaked", "flat", "quantized", "dup_modes"])
+def test_mixture_builder_sweep_vs_oracle(K, L, k, B, kind):
+    """Mixture trees over shapes on both sides of the one-warp-per-mode builder's limits (K <= 16, B <= 95),
+    with shared prefixes across modes, exact ties across modes (identical modes) and inside modes (quantized
+    log-probabilities, replayed by the serial heap), random priors: bit-exact against the oracle heap."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(K * 7919 + L * 131 + k * 17 + B + len(kind))
+    bs = 5
+    lps, idss, priors = [], [], []
+    for t in range(bs):
+        lp, ids = _candidate_tables(g, K, L, k, max(k, 24), kind)
+        lps.append(lp)
+        idss.append(ids)
+        priors.append(torch.log_softmax(torch.randn(K, generator=g), -1) if t % 2 else torch.zeros(K))
+    lp = torch.stack(lps)
+    ids = torch.stack(idss)
+    pr = torch.stack(priors).float()
+    tree, counts, _, _ = ops.build_trees(lp.to(DEV), ids.to(DEV).to(torch.int32), pr.to(DEV), B)
+    tree = tree.cpu().numpy()
+    counts = counts.cpu().numpy()
+    for t in range(bs):
+        tok, dep, par = oracle.build_mixture(lp[t].numpy(), ids[t].numpy(), pr[t].numpy(), B)
+        n = len(tok)
+        assert counts[t] == n, (t, counts[t], n)
+        assert np.array_equal(tree[t, 0, 1:n + 1], tok), t
+        assert np.array_equal(tree[t, 1, 1:n + 1], dep), t
+        assert np.array_equal(tree[t, 2, :n + 1], par), t
+        assert (tree[t, 2, n + 1:] == -1).all() and (tree[t, 0, n + 1:] == 0).all()
