@@ -145,18 +145,46 @@ int mfd_verify_inputs(const int64_t* root_tokens, const int64_t* prefix_lens, co
  * Replaces: the target's SDPA call with the compile_ddtree_tree mask (inference/hf/ddtree.py:352-356,
  *           598-605); SGLang's flashinfer custom-mask prefill (patch:86-142, 558-592); with a block-diagonal
  *           visibility, the drafter's mode_block_attention (inference/hf/mode_attention.py:120-150).
- * Workspace: mfd_tree_attention_workspace(bs, n, H, Hkv, splits) bytes, zeroed before its first use (its ticket
- * words return to zero after every call).  Its first int32 (at the 256-byte aligned base) is a sticky device status:
- * 1 once a bounded wait in the kernel gave up, 2 if a CTA's shared-memory base was misaligned beyond the slack it
- * reserves (that CTA did no work); the caller reads and clears it.
+ * Workspace: mfd_tree_attention_workspace(bs, n, H, Hkv, splits) bytes, zeroed before its first use; its first
+ * int32 (at the 256-byte aligned base) is a sticky device status: 1 once a bounded wait in the kernel gave up, 2 if
+ * a CTA's shared-memory base was misaligned beyond the slack it reserves (that CTA did no work); the caller reads
+ * and clears it.  Tickets (splits > 1): mfd_tree_attention_tickets(bs, n, H, Hkv) zeroed words of a ticket-only
+ * buffer, left zero again (as for mfd_topk_logz); the workspace itself may be reused with any sizes.
  */
 size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads, int64_t splits);
+int64_t mfd_tree_attention_tickets(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads);
 int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int64_t sq_h, const void* k, int64_t sk_b,
                        int64_t sk_h, int64_t sk_s, const void* v, int64_t sv_b, int64_t sv_h, int64_t sv_s,
                        int64_t max_keys, const int32_t* prefix_lens, int64_t prefix_len, const uint64_t* anc_bits,
                        int64_t anc_words, int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads,
                        int64_t head_dim, float scale, int64_t splits, void* out, int64_t so_b, int64_t so_n,
-                       int64_t so_h, void* workspace, size_t workspace_bytes, void* stream);
+                       int64_t so_h, void* workspace, size_t workspace_bytes, unsigned int* tickets,
+                       int64_t tickets_len, void* stream);
+
+/*
+ * Paged multi-mode draft attention of a serving batch: bs requests, each with num_modes blocks of block_size
+ * queries side by side (n = num_modes * block_size rows per request, mode-major).  Query i of request b attends to
+ * the request's context -- rows req_to_token[req_pool_indices[b] * r2t_stride + j] of k_cache / v_cache for
+ * j < ctx_lens[b] (clamped to [0, r2t_cols]; req_pool_indices clamped to [0, r2t_rows)) -- and to the block keys
+ * of its own mode, rows b n + j of k_new / v_new, as block_bits says ([n, bits_words] bitsets, one set for every
+ * request: row i sees block key j when bit j of row i is set).  q, out [bs n, H, 128] (token stride sq_t / so_t,
+ * head stride sq_h / so_h); k_new, v_new [bs n, Hkv, 128] and k_cache, v_cache [num_slots, Hkv, 128] bf16 with
+ * the KV heads of a token contiguous (head stride 128, token strides multiples of 8, K and V alike);
+ * req_to_token int32, req_pool_indices and ctx_lens int64, all on the device.  Slot ids are clamped to
+ * [0, num_slots).  The grid depends only on the sizes and `splits`; the lengths are read on the device.
+ * Workspace and tickets: as for mfd_tree_attention with (bs, n, H, Hkv, splits).
+ * Replaces: SGLang's paged_mode_block_attention (patch:897-962) and its Triton split / merge / fused kernels
+ *           (patch:627-880), called by PagedModeAttention (patch:991-1026).
+ */
+int mfd_paged_mode_attention(const void* q, int64_t sq_t, int64_t sq_h, const void* k_new, int64_t skn_t,
+                             int64_t skn_h, const void* v_new, int64_t svn_t, int64_t svn_h, const void* k_cache,
+                             int64_t skc_t, int64_t skc_h, const void* v_cache, int64_t svc_t, int64_t svc_h,
+                             int64_t num_slots, const int32_t* req_to_token, int64_t r2t_rows, int64_t r2t_cols,
+                             int64_t r2t_stride, const int64_t* req_pool_indices, const int64_t* ctx_lens,
+                             const uint64_t* block_bits, int64_t bits_words, int64_t bs, int64_t num_modes,
+                             int64_t block_size, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                             float scale, int64_t splits, void* out, int64_t so_t, int64_t so_h, void* workspace,
+                             size_t workspace_bytes, unsigned int* tickets, int64_t tickets_len, void* stream);
 
 /*
  * Tree verification of one gated-delta-rule layer from the committed state S0 (fla layout, o = S^T q):

@@ -46,9 +46,14 @@ _SIGS = {
     "mfd_verify_inputs": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                                   c_vp]),
     "mfd_tree_attention_workspace": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "mfd_tree_attention_tickets": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
     "mfd_tree_attention": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64,
                                    c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_i64,
-                                   c_vp, c_i64, c_i64, c_i64, c_vp, c_size, c_vp]),
+                                   c_vp, c_i64, c_i64, c_i64, c_vp, c_size, c_vp, c_i64, c_vp]),
+    "mfd_paged_mode_attention": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
+                                         c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp,
+                                         c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_i64, c_vp,
+                                         c_i64, c_i64, c_vp, c_size, c_vp, c_i64, c_vp]),
     "mfd_tree_gdn": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                              c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mfd_tree_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp,

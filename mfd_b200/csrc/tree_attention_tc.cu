@@ -10,8 +10,10 @@
 // lengths (up to 64 requests) the CTAs of the longest requests are launched first, so the short ones fill the tail.
 //
 // Warp roles (576 threads):
-//   warp 0       TMA producer: Q once, then 128-key K and V tiles into a 3-stage ring (128-byte swizzle, the
-//                canonical UMMA K-major / MN-major layouts; no multicast)
+//   warp 0       producer: Q once by TMA, then 128-key K and V tiles into a 3-stage ring (128-byte swizzle, the
+//                canonical UMMA K-major / MN-major layouts; no multicast) -- by TMA from dense [bs, Hkv, S, 128]
+//                caches, or, in paged mode (SGLang's paged mode attention), gathered row by row with 16-byte
+//                cp.async through the request's req_to_token row into the same swizzled layout
 //   warp 1       MMA issuer: S[i%2] = Q K_i^T (M=128, N=128, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
 //                (M=128, N=128, K=16 x 8, A = P read from TMEM, V MN-major), so the scores of tile i are computed
 //                while the softmax works on tile i-1
@@ -30,12 +32,12 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "tree_attention_tc.cuh"
 
 namespace mfd {
 namespace tca {
 
 constexpr int D = 128;
-constexpr int kM = 128;        // rows per CTA (one M-tile)
 constexpr int kKt = 128;       // keys per tile
 constexpr int kStages = 3;     // K/V ring depth
 constexpr int kParts = 4;      // softmax warps per TMEM lane quarter, each taking 32 of a tile's 128 key columns
@@ -59,24 +61,6 @@ constexpr int kSmemSlack = kSmemMax - kSmemUsed < 1024 ? kSmemMax - kSmemUsed : 
 constexpr int kSmemBytes = kSmemUsed + kSmemSlack;
 static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemMax, "shared memory");
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
-
-struct Params {
-    __nv_bfloat16* out;  // [bs, n, H, D]
-    int64_t so_b, so_n, so_h;
-    const int32_t* prefix;  // [bs] prefix lengths (device) or null
-    int prefix_const;
-    const uint64_t* anc;  // [bs, n, words]
-    int words;
-    int n, H, Hkv, G;
-    int mtiles;        // M-tiles per (request, KV head) = ceil(n G / 128)
-    float scale_log2;  // scale * log2(e)
-    int splits;
-    float* o_part;          // [splits, bs, Hkv, mtiles * 128, D]
-    float* lse_part;        // [splits, bs, Hkv, mtiles * 128]
-    unsigned int* tickets;  // [bs, Hkv, mtiles], zero between launches
-    int* status;            // sticky: 1 once a bounded wait gave up
-    int bs;
-};
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -244,12 +228,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int split = blockIdx.x / p.mtiles, mtile = blockIdx.x % p.mtiles;
     const int hk = blockIdx.y;
-    const int b = (p.prefix && p.bs > 1 && p.bs <= kMaxOrdered)
+    const int b = (!p.paged && p.prefix && p.bs > 1 && p.bs <= kMaxOrdered)
                       ? request_by_length_rank(p.prefix, p.bs, (int)blockIdx.z)
                       : (int)blockIdx.z;
     const int nrows = p.n * p.G;
     const int row0 = mtile * kM;
-    const int prefix = p.prefix ? p.prefix[b] : p.prefix_const;
+    // keys [0, prefix) are visible to every row; keys [prefix, prefix + n) are the tree (block) keys, visible by the
+    // ancestor bitsets.  Paged mode: the prefix is the request's context length, read on the device.
+    int prefix;
+    const int32_t* r2t_row = nullptr;
+    if (p.paged) {
+        const int64_t c = __ldg(p.ctx + b);
+        prefix = (int)(c < 0 ? 0 : (c > p.r2t_cols ? p.r2t_cols : c));
+        int64_t pool_row = __ldg(p.rpi + b);
+        pool_row = pool_row < 0 ? 0 : (pool_row >= p.r2t_rows ? p.r2t_rows - 1 : pool_row);
+        r2t_row = p.r2t + pool_row * p.r2t_stride;
+    } else {
+        prefix = p.prefix ? p.prefix[b] : p.prefix_const;
+    }
     const int total = prefix + p.n;
     int chunk = (total + p.splits - 1) / p.splits;
     chunk = (chunk + kKt - 1) / kKt * kKt;
@@ -275,13 +271,64 @@ __global__ void __launch_bounds__(kThreads, 1)
                         key0, hk, b);
         }
     };
+    // paged: warp 0 gathers each 128-key tile with 16-byte cp.async copies into the same 128-byte-swizzled layout the
+    // tiled TMA load produces (granule c of key row r at r * 128 + ((c ^ (r & 7)) << 4) in each d-half).  Context
+    // keys come from the caches through the request's req_to_token row, block keys from k_new / v_new (keys past
+    // the end repeat the last block key and are masked).  One warp instruction moves 4 keys' half rows: lane l
+    // takes key 32 t + 4 j + (l >> 3), granule l & 7.
+    auto load_kv_paged = [&](int i) {
+        const int st = i % kStages;
+        const int key0 = k_lo + i * kKt;
+        int64_t roff[4];  // element offsets of keys key0 + lane + 32 t (row start of this KV head)
+        bool rcache[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int r = key0 + lane + 32 * t;
+            rcache[t] = r < prefix;
+            roff[t] = rcache[t] ? (int64_t)min(max(__ldg(r2t_row + r), 0), (int)(p.slots - 1)) * p.skc_t + hk * D
+                                : ((int64_t)b * p.n + min(r - prefix, p.n - 1)) * p.skn_t + hk * D;
+        }
+        const int c = lane & 7;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+#pragma unroll 2
+            for (int j = 0; j < 8; ++j) {
+                const int src = 4 * j + (lane >> 3);  // the lane holding this instruction's key
+                const int key = 32 * t + src;          // key within the tile
+                const int64_t off = (int64_t)__shfl_sync(MFD_FULL_MASK, (long long)roff[t], src);
+                const bool cache = __shfl_sync(MFD_FULL_MASK, (int)rcache[t], src) != 0;
+                const __nv_bfloat16* kr = (cache ? p.kc : p.kn) + off;
+                const __nv_bfloat16* vr = (cache ? p.vc : p.vn) + off;
+                const uint32_t sw = (uint32_t)(key * 128 + ((c ^ (key & 7)) << 4));
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t dk = sbase + kOffK + st * kKVBytes + h * (kKVBytes / 2) + sw;
+                    const uint32_t dv = sbase + kOffV + st * kKVBytes + h * (kKVBytes / 2) + sw;
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(kr + h * 64 + c * 8)
+                                 : "memory");
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(vr + h * 64 + c * 8)
+                                 : "memory");
+                }
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // the copies of tile j have landed: make them visible to the tensor cores (async proxy), then mark the stage full
+    auto publish_paged = [&](int j, bool last) {
+        if (last) asm volatile("cp.async.wait_group 0;" ::: "memory");
+        else asm volatile("cp.async.wait_group 1;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kBarKVFull + j % kStages]);
+    };
     if (threadIdx.x == 0 && ntiles > 0) {  // (a split past the keys loads nothing: every issued copy is waited for)
         const int nodes_per_tile = kM / p.G;
         mbar_expect_tx(&bars[kBarQ], kQBytes);
         for (int h = 0; h < 2; ++h)
             tma_load_4d(sbase + kOffQ + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G, mtile * nodes_per_tile,
                         b);
-        for (int i = 0; i < min(kStages, ntiles); ++i) load_kv(i);
+        if (!p.paged)
+            for (int i = 0; i < min(kStages, ntiles); ++i) load_kv(i);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
@@ -296,7 +343,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
+        if (p.paged) {
+            // tile i's copies are issued, then tile i - 1 is published (two tiles' copies in flight); a stage is
+            // refilled only after the MMA released it
+            for (int i = 0; i < ntiles; ++i) {
+                if (i >= kStages) {
+                    bool w = true;
+                    if (lane == 0) w = mbar_wait(&bars[kBarKVEmpty + i % kStages], ((i / kStages) - 1) & 1, kTries);
+                    ok &= __shfl_sync(MFD_FULL_MASK, (int)w, 0) != 0;
+                    if (!ok) break;
+                }
+                load_kv_paged(i);
+                if (i >= 1) publish_paged(i - 1, false);
+            }
+            if (ok && ntiles > 0) publish_paged(ntiles - 1, true);
+            asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing in flight when the warp leaves
+        } else if (lane == 0) {
             for (int i = kStages; i < ntiles && ok; ++i) {
                 ok &= mbar_wait(&bars[kBarKVEmpty + i % kStages], ((i / kStages) - 1) & 1, kTries);
                 load_kv(i);
@@ -350,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = row0 + rt;             // packed row
         const bool live = r < nrows;
         const int node = live ? r / p.G : 0;
-        const uint64_t* anc_row = p.anc + ((size_t)b * p.n + node) * p.words;
+        const uint64_t* anc_row = p.anc + ((size_t)(p.paged ? 0 : b) * p.n + node) * p.words;  // paged: shared
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [kParts][128 rows]
         const int c_lo = part * 32;  // this warp's 32 of the tile's 128 key columns
@@ -615,36 +677,33 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t d1, uint64_t d2,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-struct Shape {
-    const void* q;
-    int64_t sq_b, sq_n, sq_h;
-    const void* k;
-    int64_t sk_b, sk_h, sk_s;
-    const void* v;
-    int64_t sv_b, sv_h, sv_s;
-    int64_t max_keys;
-};
-
 int launch(const Shape& sh, const Params& p, cudaStream_t stream) {
     CUtensorMap tq, tk, tv;
     const uint32_t nodes_per_tile = (uint32_t)(kM / p.G);
-    if (!make_map(&tq, sh.q, (uint64_t)p.H, (uint64_t)p.n, (uint64_t)p.bs, sh.sq_h, sh.sq_n, sh.sq_b, (uint32_t)p.G,
-                  nodes_per_tile) ||
-        !make_map(&tk, sh.k, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sk_s, sh.sk_h, sh.sk_b, kKt,
-                  1) ||
-        !make_map(&tv, sh.v, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sv_s, sh.sv_h, sh.sv_b, kKt,
-                  1)) {
-        set_error("mfd_tree_attention: could not encode the TMA tensor maps");
+    bool okm = make_map(&tq, sh.q, (uint64_t)p.H, (uint64_t)p.n, (uint64_t)p.bs, sh.sq_h, sh.sq_n, sh.sq_b,
+                        (uint32_t)p.G, nodes_per_tile);
+    if (p.paged) {  // K and V are gathered with cp.async; the maps are not read
+        tk = tq;
+        tv = tq;
+    } else {
+        okm = okm &&
+              make_map(&tk, sh.k, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sk_s, sh.sk_h, sh.sk_b,
+                       kKt, 1) &&
+              make_map(&tv, sh.v, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sv_s, sh.sv_h, sh.sv_b,
+                       kKt, 1);
+    }
+    if (!okm) {
+        set_error("%s: could not encode the TMA tensor maps", p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention");
         return MFD_ERR_CUDA;
     }
     cudaError_t e = cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) {
-        set_error("mfd_tree_attention: %s", cudaGetErrorString(e));
+        set_error("%s: %s", p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention", cudaGetErrorString(e));
         return MFD_ERR_CUDA;
     }
     dim3 grid((unsigned)(p.splits * p.mtiles), (unsigned)p.Hkv, (unsigned)p.bs);
     tree_attn_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
-    MFD_CHECK_LAUNCH("mfd_tree_attention");
+    MFD_CHECK_LAUNCH(p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention");
     return MFD_OK;
 }
 

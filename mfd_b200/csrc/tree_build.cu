@@ -617,16 +617,22 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
 // order, and restricted to one mode it is the best-first enumeration of that mode alone -- except where two live
 // entries of one mode have equal keys (their order then depends on global node ids).  This kernel therefore:
 //   1. runs the K modes' enumerations at once, one warp per mode: the mode's live entries (one per open sibling
-//      group, at most B + 1) sit in registers, three per lane, and a pop is a warp-wide minimum (redux.sync) and
-//      two successor updates; each mode pops at most B entries, enough because the first B distinct nodes of the
-//      mixture contain at most B entries of any mode;
-//   2. ranks every popped entry in the merged order (key, then mode) by binary searches in the other modes' lists;
-//   3. merges equal prefixes exactly, depth by depth: an entry's prefix is (its parent's prefix, its token), named
-//      by the merged position of its first occurrence, through a shared-memory hash with atomicCAS / atomicMin;
-//   4. numbers the first occurrences in merged order: the first B are the nodes, in the heap's pop order.
-// A mode whose warp minimum is not unique (an exact key tie), or a successor with a smaller key than its
-// generator (double rounding of equal log-probabilities), sends the whole tree to serial_mixture, which replays
-// the reference heap exactly.  Limits: K <= 16, B <= 95 (three groups per lane).
+//      group, at most B + 1) sit in registers, three per lane, and a pop is a warp-wide minimum (redux.sync), two
+//      ballots and the owner lane computing both successors.  Round 1 pops B / 4 entries per mode and merges them
+//      (steps 2-4); the B-th distinct prefix found bounds the tree's last node, so round 2 pops only the modes
+//      whose next entry precedes that bound, up to it (or up to B entries when round 1 found fewer than B
+//      prefixes -- B per mode always suffice, since the first B distinct nodes contain at most B entries of any
+//      mode), and merges again;
+//   2. ranks every popped entry in the merged order (key, then mode) by fixed-step searches in the other modes'
+//      lists, run side by side;
+//   3. merges equal prefixes: every popped entry carries a hash of its token path, entries are grouped through a
+//      shared-memory hash table (atomicCAS / atomicMin give each group its least merged position), and every
+//      grouped entry is compared token by token with that first occurrence;
+//   4. numbers the first occurrences in merged order by a block scan: the first B are the nodes, in the heap's
+//      pop order.
+// A mode whose warp minimum is not unique (an exact key tie), a successor with a smaller key than its generator
+// (double rounding of equal log-probabilities), or two different paths with one hash sends the whole tree to
+// serial_mixture, which replays the reference heap exactly.  Limits: K <= 16, B <= 95 (three groups per lane).
 constexpr int kFastThreads = 512;
 constexpr int kFastSlots = 3;
 constexpr uint32_t kNoKey = 0xffffffffu;
@@ -641,7 +647,9 @@ struct FastSmem {
     int16_t* ecan;    // [K][B] merged position of the first occurrence of the entry's prefix
     int16_t* eslot;   // [K][B] dedup hash slot
     int16_t* pnid;    // [K B] node id by merged position (0: not a node)
-    uint64_t* dkey;   // [dcap] dedup keys ((parent prefix + 1) << 32 | token)
+    int16_t* pent;    // [K B] entry (mode * B + pop index) by merged position
+    uint64_t* ehash;  // [K][B] hash of the entry's token path (root first)
+    uint64_t* dkey;   // [dcap] dedup keys (path hashes)
     int32_t* dval;    // [dcap] least merged position holding the key
 };
 
@@ -650,6 +658,8 @@ __device__ FastSmem carve_fast(const Params& p, unsigned char*& q, int dcap) {
     FastSmem f;
     f.dkey = (uint64_t*)smem_take(q, 8 * (size_t)dcap);
     f.dval = (int32_t*)smem_take(q, 4 * (size_t)dcap);
+    f.ehash = (uint64_t*)smem_take(q, 8 * KB);
+    f.pent = (int16_t*)smem_take(q, 2 * KB);
     f.ekey = (uint32_t*)smem_take(q, 4 * KB);
     f.etok = (int32_t*)smem_take(q, 4 * KB);
     f.epl = (int16_t*)smem_take(q, 2 * KB);
@@ -663,7 +673,8 @@ __device__ FastSmem carve_fast(const Params& p, unsigned char*& q, int dcap) {
 static size_t fast_smem_bytes(int K, int B, int dcap) {
     auto r16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
     const size_t KB = (size_t)K * B;
-    return r16(8 * (size_t)dcap) + r16(4 * (size_t)dcap) + 2 * r16(4 * KB) + 5 * r16(2 * KB) + r16(KB);
+    return r16(8 * (size_t)dcap) + r16(4 * (size_t)dcap) + r16(8 * KB) + r16(2 * KB) + 2 * r16(4 * KB) +
+           5 * r16(2 * KB) + r16(KB);
 }
 __host__ __device__ inline int fast_dcap(int K, int B) {
     int d = 64;
@@ -671,54 +682,69 @@ __host__ __device__ inline int fast_dcap(int K, int B) {
     return d;
 }
 
+// Hash of a token path, extended one token at a time (splitmix64 finaliser of the previous hash and the token).
+// It only groups candidate duplicates: every grouped pair is compared token by token before it is trusted.
+constexpr uint64_t kRootPath = 0x243F6A8885A308D3ull;
+__device__ __forceinline__ uint64_t path_hash(uint64_t h, int32_t token) {
+    uint64_t z = h ^ ((uint64_t)(uint32_t)token * 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return z == kEmptyHash ? z - 1 : z;
+}
+
 __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ int sh_cnt[16], sh_off[17], sh_maxdep[16];
-    __shared__ int sh_bad, sh_count, sh_fail, sh_wsum[kFastThreads / 32];
+    __shared__ int sh_cnt[16], sh_done[16];
+    __shared__ int sh_bad, sh_count, sh_total, sh_fail, sh_ntot, sh_wsum[kFastThreads / 32];
+    __shared__ uint32_t sh_ukey;
+    __shared__ int sh_umode;
     const int b = blockIdx.x;
     const int K = p.K, L = p.L, k = p.k, B = p.B;
+    const int KB = K * B;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int dcap = fast_dcap(K, B);
     unsigned char* q = smem_raw;
     const MixSmem s = carve_mixture(p, q);
     const FastSmem f = carve_fast(p, q, dcap);
     stage_mixture(p, b, s);
-    for (int i = threadIdx.x; i < dcap; i += kFastThreads) {
-        f.dkey[i] = kEmptyHash;
-        f.dval[i] = 0x7fffffff;
-    }
     if (threadIdx.x == 0) sh_bad = 0;
     __syncthreads();
 
-    // ---- 1. per-mode best-first enumeration, warp m = mode m
-    if (warp < K) {
-        const int m = warp;
-        const float pr = s.prior[m];
-        // three live-entry slots per lane, as scalars (slot t of lane l holds group 32 t + l)
-        uint32_t k0 = kNoKey, k1 = kNoKey, k2 = kNoKey;
-        double w0 = 0.0, w1 = 0.0, w2 = 0.0;
-        int r0 = 0, r1 = 0, r2 = 0, d0 = 0, d1 = 0, d2 = 0, q0 = 0, q1 = 0, q2 = 0;
-        if (lane == 0) {  // group 0: the root's children, rank 0 first
-            w0 = (double)s.lp[(m * L) * k];
-            k0 = mix_key(w0, pr);
-            d0 = 1;
-            q0 = -1;
-        }
-        int groups = 1, i = 0, bad = 0, maxdep = 0;
+    // ---- 1. per-mode best-first enumeration, warp m = mode m.  Three live-entry slots per lane, as scalars (slot
+    // t of lane l holds group 32 t + l); the state persists across the two rounds.
+    const int m = warp;
+    const float pr = warp < K ? s.prior[m] : 0.f;
+    uint32_t k0 = kNoKey, k1 = kNoKey, k2 = kNoKey;
+    double w0 = 0.0, w1 = 0.0, w2 = 0.0;
+    int r0 = 0, r1 = 0, r2 = 0, d0 = 0, d1 = 0, d2 = 0, q0 = 0, q1 = 0, q2 = 0;
+    if (warp < K && lane == 0) {  // group 0: the root's children, rank 0 first
+        w0 = (double)s.lp[(m * L) * k];
+        k0 = mix_key(w0, pr);
+        d0 = 1;
+        q0 = -1;
+    }
+    int groups = 1, npop = 0, bad = 0;
+    // pop while fewer than `limit` entries are out and the next entry precedes (ukey, umode) in the merged order
+    auto pop_run = [&](int limit, uint32_t ukey, int umode) {
         uint32_t* ekey = f.ekey + m * B;
-        for (; i < B; ++i) {
-            const uint32_t lmin = min(k0, min(k1, k2));
-            const uint32_t wmin = __reduce_min_sync(MFD_FULL_MASK, lmin);
-            if (wmin == kNoKey) break;
+        for (; npop < limit; ++npop) {
+            const int i = npop;
+            const uint32_t wmin = __reduce_min_sync(MFD_FULL_MASK, min(k0, min(k1, k2)));
+            if (wmin == kNoKey || wmin > ukey || (wmin == ukey && m > umode)) break;
             const int mine = (k0 == wmin) + (k1 == wmin) + (k2 == wmin);
             const uint32_t bal = __ballot_sync(MFD_FULL_MASK, mine > 0);
-            if (__popc(bal) > 1 || __any_sync(MFD_FULL_MASK, mine > 1)) {  // an exact tie inside the mode
+            const uint32_t multi = __ballot_sync(MFD_FULL_MASK, mine > 1);
+            if ((bal & (bal - 1)) | multi) {  // an exact tie inside the mode
                 bad = 1;
                 break;
             }
             const int owner = __ffs(bal) - 1;
-            double plw = 0.0;
-            int pdep = 0;
+            // the owner pops the entry and computes both successors: the sibling stays in its slot, the first child
+            // (a new group) goes to the lane and slot of group `groups`
+            uint32_t ck = kNoKey;
+            double cw = 0.0;
+            int cdep = 0;
             if (lane == owner) {
                 const int sl = k0 == wmin ? 0 : (k1 == wmin ? 1 : 2);
                 const double w = sl == 0 ? w0 : (sl == 1 ? w1 : w2);
@@ -727,47 +753,188 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
                 const int par = sl == 0 ? q0 : (sl == 1 ? q1 : q2);
                 const int row = (m * L + d - 1) * k;
                 const float lp_r = s.lp[row + r];
-                ekey[i] = wmin;
-                f.etok[m * B + i] = s.ids[row + r];
-                f.epl[m * B + i] = (int16_t)par;
-                f.edep[m * B + i] = (uint8_t)d;
+                const float lp_r1 = r + 1 < k ? s.lp[row + r + 1] : 0.f;
+                const float lp_c = d < L ? s.lp[(m * L + d) * k] : 0.f;
+                const int32_t tok = s.ids[row + r];
                 uint32_t nk = kNoKey;
                 double nw = 0.0;
                 if (r + 1 < k) {  // the sibling: (logw - lp[rank]) + lp[rank + 1] in double
-                    nw = (w - (double)lp_r) + (double)s.lp[row + r + 1];
+                    nw = (w - (double)lp_r) + (double)lp_r1;
                     nk = mix_key(nw, pr);
                     if (nk < wmin) bad = 1;
+                }
+                if (d < L) {  // the first child: logw + lp[depth][0]
+                    cw = w + (double)lp_c;
+                    ck = mix_key(cw, pr);
+                    if (ck < wmin) bad = 1;
+                    cdep = d + 1;
                 }
                 if (sl == 0) { k0 = nk; w0 = nw; r0 = r + 1; }
                 else if (sl == 1) { k1 = nk; w1 = nw; r1 = r + 1; }
                 else { k2 = nk; w2 = nw; r2 = r + 1; }
-                plw = w;
-                pdep = d;
+                ekey[i] = wmin;
+                f.etok[m * B + i] = tok;
+                f.epl[m * B + i] = (int16_t)par;
+                f.edep[m * B + i] = (uint8_t)d;
+                f.ehash[m * B + i] = path_hash(par < 0 ? kRootPath : f.ehash[m * B + par], tok);
             }
-            plw = __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(plw), owner));
-            pdep = __shfl_sync(MFD_FULL_MASK, pdep, owner);
-            maxdep = max(maxdep, pdep);
-            if (pdep < L) {  // the popped entry's first child opens a new group: logw + lp[depth][0]
+            cdep = __shfl_sync(MFD_FULL_MASK, cdep, owner);
+            if (cdep > 0) {
+                ck = __shfl_sync(MFD_FULL_MASK, ck, owner);
+                cw = __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(cw), owner));
                 const int g = groups++;
                 if (lane == (g & 31)) {
-                    const double cw = plw + (double)s.lp[(m * L + pdep) * k];
-                    const uint32_t ck = mix_key(cw, pr);
-                    if (ck < wmin) bad = 1;
                     const int sl = g >> 5;
-                    if (sl == 0) { k0 = ck; w0 = cw; r0 = 0; d0 = pdep + 1; q0 = i; }
-                    else if (sl == 1) { k1 = ck; w1 = cw; r1 = 0; d1 = pdep + 1; q1 = i; }
-                    else { k2 = ck; w2 = cw; r2 = 0; d2 = pdep + 1; q2 = i; }
+                    if (sl == 0) { k0 = ck; w0 = cw; r0 = 0; d0 = cdep; q0 = i; }
+                    else if (sl == 1) { k1 = ck; w1 = cw; r1 = 0; d1 = cdep; q1 = i; }
+                    else { k2 = ck; w2 = cw; r2 = 0; d2 = cdep; q2 = i; }
                 }
             }
         }
         bad = __any_sync(MFD_FULL_MASK, bad);
         if (lane == 0) {
-            sh_cnt[m] = i;
-            sh_maxdep[m] = maxdep;
+            sh_cnt[m] = npop;
             if (bad) atomicOr(&sh_bad, 1);
         }
-    }
+    };
+
+    // ---- 2-4. merge the popped lists (all threads).  Sets sh_total (distinct prefixes), sh_count, pnid and, when
+    // sh_total reaches B, (sh_ukey, sh_umode) = key and mode of the B-th distinct prefix's first occurrence.
+    // Merged position of entry (mode mm, pop index i): i plus, in every other mode, the number of its entries that
+    // precede (key, mm) -- keys below it, and equal keys of lower modes; the K searches run side by side
+    auto merged_pos = [&](int mm, int i, uint32_t kv) {
+        int pos = i;
+#pragma unroll
+        for (int m2 = 0; m2 < 16; ++m2) {
+            if (m2 >= K || m2 == mm) continue;
+            const uint32_t* ek = f.ekey + m2 * B;
+            const int cnt = sh_cnt[m2];
+            const uint64_t lim = (uint64_t)kv + (m2 < mm ? 1u : 0u);  // count keys < lim
+            int base = 0;
+#pragma unroll
+            for (int step = 64; step; step >>= 1)
+                if (base + step <= cnt && (uint64_t)ek[base + step - 1] < lim) base += step;
+            pos += base;
+        }
+        return pos;
+    };
+    // entry x's token path equals entry y's (same depth, the same tokens back to the root)
+    auto same_path = [&](int x, int y) {
+        if (f.edep[x] != f.edep[y]) return false;
+        while (x >= 0 && y >= 0) {
+            if (f.etok[x] != f.etok[y]) return false;
+            const int px = f.epl[x], py = f.epl[y];
+            x = px < 0 ? -1 : (x / B) * B + px;
+            y = py < 0 ? -1 : (y / B) * B + py;
+        }
+        return x < 0 && y < 0;
+    };
+    auto merge = [&]() {
+        for (int i = threadIdx.x; i < dcap; i += kFastThreads) {
+            f.dkey[i] = kEmptyHash;
+            f.dval[i] = 0x7fffffff;
+        }
+        if (threadIdx.x == 0) {
+            int o = 0;
+            for (int mm = 0; mm < K; ++mm) o += sh_cnt[mm];
+            sh_ntot = o;
+            sh_ukey = kNoKey;
+            sh_umode = K;
+        }
+        __syncthreads();
+        // positions, and each path's least position through the table of path hashes
+        for (int x = threadIdx.x; x < KB; x += kFastThreads) {
+            const int mm = x / B, i = x - mm * B;
+            if (i >= sh_cnt[mm]) continue;
+            const int pos = merged_pos(mm, i, f.ekey[x]);
+            f.epos[x] = (int16_t)pos;
+            f.pent[pos] = (int16_t)x;
+            const uint64_t hk = f.ehash[x];
+            uint32_t h = (uint32_t)(hk >> 32) & (uint32_t)(dcap - 1);
+            for (int t = 0; t < dcap; ++t) {
+                const unsigned long long prev =
+                    atomicCAS((unsigned long long*)&f.dkey[h], (unsigned long long)kEmptyHash, (unsigned long long)hk);
+                if (prev == kEmptyHash || prev == hk) break;
+                h = (h + 1) & (uint32_t)(dcap - 1);
+            }
+            atomicMin(&f.dval[h], pos);
+            f.eslot[x] = (int16_t)h;
+        }
+        __syncthreads();
+        // each entry's first occurrence, checked token by token (a hash collision sends the tree to the serial
+        // heap); first occurrences flagged by position
+        for (int x = threadIdx.x; x < KB; x += kFastThreads) {
+            const int mm = x / B, i = x - mm * B;
+            if (i >= sh_cnt[mm]) continue;
+            const int c = f.dval[f.eslot[x]];
+            f.ecan[x] = (int16_t)c;
+            const int pos = f.epos[x];
+            if (c != pos && !same_path(x, f.pent[c])) sh_bad = 1;
+            f.pnid[pos] = (int16_t)(c == pos ? 1 : 0);
+        }
+        __syncthreads();
+        const int N = sh_ntot;
+        {
+            const int per = (N + kFastThreads - 1) / kFastThreads;
+            const int p0 = min(N, (int)threadIdx.x * per), p1 = min(N, p0 + per);
+            int local = 0;
+            for (int x = p0; x < p1; ++x) local += f.pnid[x];
+            int incl = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(MFD_FULL_MASK, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane == 31) sh_wsum[warp] = incl;
+            __syncthreads();
+            int base = 0;
+            for (int w = 0; w < warp; ++w) base += sh_wsum[w];
+            int run = base + incl - local;
+            for (int x = p0; x < p1; ++x) {
+                const int fl = f.pnid[x];
+                f.pnid[x] = (int16_t)(fl ? run + 1 : 0);
+                if (fl && run + 1 == B) {  // the B-th distinct prefix's first occurrence
+                    const int e = f.pent[x];
+                    sh_ukey = f.ekey[e];
+                    sh_umode = e / B;
+                }
+                run += fl;
+            }
+            if (threadIdx.x == kFastThreads - 1) {
+                sh_total = run;
+                sh_count = min(run, B);
+            }
+        }
+        __syncthreads();
+    };
+
+    // round 1: every mode pops at most B / 4 (at least 8) entries; merge
+    const int probe = min(B, max(8, B / 4));
+    if (warp < K) pop_run(probe, kNoKey, K);
     __syncthreads();
+    if (!sh_bad) merge();
+    if (!sh_bad) {
+        // a mode is complete once its next entry follows the bound (or it has none); the bound is the B-th
+        // distinct prefix of round 1, so every entry the tree needs precedes it
+        const bool bounded = sh_total >= B;
+        const uint32_t ukey = bounded ? sh_ukey : kNoKey;
+        const int umode = bounded ? sh_umode : K;
+        if (warp < K) {
+            const uint32_t nxt = __reduce_min_sync(MFD_FULL_MASK, min(k0, min(k1, k2)));
+            const bool done = npop >= B || nxt == kNoKey || nxt > ukey || (nxt == ukey && m > umode);
+            if (lane == 0) sh_done[m] = done ? 1 : 0;
+        }
+        __syncthreads();
+        int all_done = 1;
+        for (int mm = 0; mm < K; ++mm) all_done &= sh_done[mm];
+        if (!all_done) {
+            // round 2: the incomplete modes pop up to the bound (or to B entries when round 1 found fewer than B
+            // distinct prefixes); merge again
+            if (warp < K && !sh_done[m]) pop_run(B, ukey, umode);
+            __syncthreads();
+            if (!sh_bad) merge();
+        }
+    }
     if (sh_bad) {  // replay the reference heap in one thread
         if (threadIdx.x == 0) {
             int fail = 0;
@@ -779,118 +946,15 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
         if (threadIdx.x < kThreads) write_tree_outputs(p, b, sh_count, s.ntok, s.npar, s.ndep);
         return;
     }
-    if (threadIdx.x == 0) {
-        int o = 0, md = 0;
-        for (int m = 0; m < K; ++m) {
-            sh_off[m] = o;
-            o += sh_cnt[m];
-            md = max(md, sh_maxdep[m]);
-        }
-        sh_off[K] = o;
-        sh_maxdep[0] = md;
-    }
-    __syncthreads();
-    const int N = sh_off[K];
-    const int maxdep = sh_maxdep[0];
-    auto locate = [&](int e, int& m, int& i) {  // flat entry -> (mode, pop index)
-        m = 0;
-        while (m + 1 < K && sh_off[m + 1] <= e) ++m;
-        i = e - sh_off[m];
-    };
-
-    // ---- 2. merged positions: (key, mode) order
-    for (int e = threadIdx.x; e < N; e += kFastThreads) {
-        int m, i;
-        locate(e, m, i);
-        const uint32_t kv = f.ekey[m * B + i];
-        int pos = i;
-        for (int m2 = 0; m2 < K; ++m2) {
-            if (m2 == m) continue;
-            const uint32_t* ek = f.ekey + m2 * B;
-            int lo = 0, hi = sh_cnt[m2];  // count of keys < kv (m2 > m) or <= kv (m2 < m)
-            while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                const uint32_t v = ek[mid];
-                if (v < kv || (m2 < m && v == kv)) lo = mid + 1;
-                else hi = mid;
-            }
-            pos += lo;
-        }
-        f.epos[m * B + i] = (int16_t)pos;
-    }
-    __syncthreads();
-
-    // ---- 3. equal prefixes, depth by depth
-    for (int d = 1; d <= maxdep; ++d) {
-        for (int e = threadIdx.x; e < N; e += kFastThreads) {
-            int m, i;
-            locate(e, m, i);
-            const int x = m * B + i;
-            if (f.edep[x] != d) continue;
-            const int pc = f.epl[x] < 0 ? -1 : (int)f.ecan[m * B + f.epl[x]];
-            const uint64_t dk = ((uint64_t)(uint32_t)(pc + 1) << 32) | (uint32_t)f.etok[x];
-            uint32_t h = (uint32_t)((dk * 0x9E3779B97F4A7C15ull) >> 32) & (uint32_t)(dcap - 1);
-            for (int t = 0; t < dcap; ++t) {
-                const unsigned long long prev =
-                    atomicCAS((unsigned long long*)&f.dkey[h], (unsigned long long)kEmptyHash, (unsigned long long)dk);
-                if (prev == kEmptyHash || prev == dk) break;
-                h = (h + 1) & (uint32_t)(dcap - 1);
-            }
-            atomicMin(&f.dval[h], (int)f.epos[x]);
-            f.eslot[x] = (int16_t)h;
-        }
-        __syncthreads();
-        for (int e = threadIdx.x; e < N; e += kFastThreads) {
-            int m, i;
-            locate(e, m, i);
-            const int x = m * B + i;
-            if (f.edep[x] == d) f.ecan[x] = (int16_t)f.dval[f.eslot[x]];
-        }
-        __syncthreads();
-    }
-
-    // ---- 4. node ids: first occurrences numbered in merged order
-    for (int e = threadIdx.x; e < N; e += kFastThreads) {
-        int m, i;
-        locate(e, m, i);
-        const int x = m * B + i;
-        f.pnid[f.epos[x]] = (int16_t)(f.ecan[x] == f.epos[x] ? 1 : 0);
-    }
-    __syncthreads();
-    {
-        const int per = (N + kFastThreads - 1) / kFastThreads;
-        const int p0 = min(N, (int)threadIdx.x * per), p1 = min(N, p0 + per);
-        int local = 0;
-        for (int x = p0; x < p1; ++x) local += f.pnid[x];
-        int incl = local;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(MFD_FULL_MASK, incl, o);
-            if (lane >= o) incl += y;
-        }
-        if (lane == 31) sh_wsum[warp] = incl;
-        __syncthreads();
-        int base = 0;
-        for (int w = 0; w < warp; ++w) base += sh_wsum[w];
-        int run = base + incl - local;
-        for (int x = p0; x < p1; ++x) {
-            const int fl = f.pnid[x];
-            f.pnid[x] = (int16_t)(fl ? run + 1 : 0);
-            run += fl;
-        }
-        if (threadIdx.x == kFastThreads - 1) sh_count = min(run, B);
-    }
-    __syncthreads();
     const int count = sh_count;
-    for (int e = threadIdx.x; e < N; e += kFastThreads) {
-        int m, i;
-        locate(e, m, i);
-        const int x = m * B + i;
+    for (int x = threadIdx.x; x < KB; x += kFastThreads) {
+        const int mm = x / B, i = x - mm * B;
+        if (i >= sh_cnt[mm]) continue;
         const int nid = f.pnid[f.epos[x]];
         if (nid == 0 || nid > count) continue;
         s.ntok[nid] = f.etok[x];
         s.ndep[nid] = f.edep[x];
-        s.npar[nid] = (int16_t)(f.epl[x] < 0 ? 0 : f.pnid[f.ecan[m * B + f.epl[x]]]);
+        s.npar[nid] = (int16_t)(f.epl[x] < 0 ? 0 : f.pnid[f.ecan[mm * B + f.epl[x]]]);
     }
     __syncthreads();
     if (threadIdx.x < kThreads) write_tree_outputs(p, b, count, s.ntok, s.npar, s.ndep);

@@ -238,21 +238,67 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, anc: torch
         splits = default_splits(bs, n, H, Hkv, max_keys)
     L = _lib.lib()
     ws = Workspace.get(dev, "attn", L.mfd_tree_attention_workspace(bs, n, H, Hkv, splits))
+    nt = L.mfd_tree_attention_tickets(bs, n, H, Hkv)
+    tk = Workspace.tickets(dev, nt)
     rc = L.mfd_tree_attention(q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), k.data_ptr(), k.stride(0),
                               k.stride(1), k.stride(2), v.data_ptr(), v.stride(0), v.stride(1), v.stride(2),
                               k.shape[2], ptr(pl_t), pl_c, anc.data_ptr(), anc.shape[-1], bs, n, H, Hkv, D,
                               float(scale), splits, out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
-                              ws.data_ptr(), ws.numel(), stream_ptr(dev))
+                              ws.data_ptr(), ws.numel(), tk.data_ptr(), tk.numel(), stream_ptr(dev))
     check(rc, "mfd_tree_attention")
     return out
 
 
-def tree_attention_status(device=None) -> int:
-    """The sticky status word at the head of the verify-attention workspace (the first int32 at its 256-byte aligned
-    base): 0; 1 once a bounded wait in the kernel gave up; 2 when a CTA found its shared-memory base misaligned
-    beyond the reserved slack and did no work.  0 when no attention call has run on the device."""
+def paged_mode_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+                         v_cache: torch.Tensor, req_to_token: torch.Tensor, req_pool_indices: torch.Tensor,
+                         ctx_lens: torch.Tensor, block_bits: torch.Tensor, num_modes: int, block_size: int,
+                         scale: float, splits: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """q [T, H, 128], k_new/v_new [T, Hkv, 128] (T = bs * K * block_size, mode-major per request); k_cache/v_cache
+    [slots, Hkv, 128]; request b's context is k_cache[req_to_token[req_pool_indices[b], :ctx_lens[b]]].
+    block_bits [1, K*block_size, words] int64: the block-diagonal visibility.  Returns [T, H, 128] bf16."""
+    dev = require_cuda(q, k_new, v_new, k_cache, v_cache, req_to_token, req_pool_indices, ctx_lens, block_bits)
+    T, H, D = q.shape
+    Hkv = k_new.shape[1]
+    n = num_modes * block_size
+    bs = T // n if n > 0 else 0
+    if T != bs * n:
+        raise RuntimeError(f"paged_mode_attention: {T} queries are not a multiple of num_modes * block_size = {n}")
+    for t in (q, k_new, v_new, k_cache, v_cache):
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError("paged_mode_attention: q, k, v and the caches must be bfloat16")
+    if req_to_token.dtype != torch.int32:
+        req_to_token = req_to_token.to(torch.int32)
+    if req_to_token.stride(1) != 1:
+        req_to_token = req_to_token.contiguous()
+    rpi = req_pool_indices[:bs].to(torch.int64).contiguous()
+    ctx = ctx_lens[:bs].to(torch.int64).contiguous()
+    if out is None:
+        out = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
+    if bs == 0:
+        return out
+    L = _lib.lib()
+    ws = Workspace.get(dev, "paged_attn", L.mfd_tree_attention_workspace(bs, n, H, Hkv, splits))
+    tk = Workspace.tickets(dev, L.mfd_tree_attention_tickets(bs, n, H, Hkv))
+    rc = L.mfd_paged_mode_attention(q.data_ptr(), q.stride(0), q.stride(1), k_new.data_ptr(), k_new.stride(0),
+                                    k_new.stride(1), v_new.data_ptr(), v_new.stride(0), v_new.stride(1),
+                                    k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), v_cache.data_ptr(),
+                                    v_cache.stride(0), v_cache.stride(1), k_cache.shape[0], req_to_token.data_ptr(),
+                                    req_to_token.shape[0], req_to_token.shape[1], req_to_token.stride(0),
+                                    rpi.data_ptr(), ctx.data_ptr(), block_bits.data_ptr(), block_bits.shape[-1], bs,
+                                    num_modes, block_size, H, Hkv, D, float(scale), splits, out.data_ptr(),
+                                    out.stride(0), out.stride(1), ws.data_ptr(), ws.numel(), tk.data_ptr(),
+                                    tk.numel(), stream_ptr(dev))
+    check(rc, "mfd_paged_mode_attention")
+    return out
+
+
+def tree_attention_status(device=None, purpose: str = "attn") -> int:
+    """The sticky status word at the head of an attention workspace (the first int32 at its 256-byte aligned base):
+    0; 1 once a bounded wait in the kernel gave up; 2 when a CTA found its shared-memory base misaligned beyond the
+    reserved slack and did no work.  0 when no such call has run on the device.  purpose "attn": tree_attention
+    and the dense mode attention; "paged_attn": paged_mode_attention."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    ws = Workspace._cache.get((dev.index if dev.index is not None else torch.cuda.current_device(), "attn"))
+    ws = Workspace._cache.get((dev.index if dev.index is not None else torch.cuda.current_device(), purpose))
     if ws is None:
         return 0
     off = (-ws.data_ptr()) % 256

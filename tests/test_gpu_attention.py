@@ -107,3 +107,31 @@ def test_tree_attention_many_requests_tied_prefixes(bs):
                                     D ** -0.5)
         assert np.abs(out[b] - ref).max() <= TOL, b
     assert ops.tree_attention_status() == 0
+
+
+def test_tree_attention_workspace_reused_across_sizes():
+    """One workspace serves calls of different sizes in any order: a call that fills it with split partials
+    (one request, 16 splits), then calls with more (request, KV head, M-tile) units and other split counts all
+    match the oracle (their tickets live in the ticket-only buffer, never on the earlier partials)."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(31)
+    n, H, Hkv, D = 65, 32, 8, 128
+    for bs, splits in [(1, 16), (5, 4), (2, 7), (6, 3)]:
+        S = 600 + n
+        prefixes = [int(x) for x in torch.randint(100, 600, (bs,), generator=g)]
+        q = torch.randn(bs, n, H, D, generator=g).to(torch.bfloat16)
+        k = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+        v = (torch.randn(bs, Hkv, S, D, generator=g) * 0.5).to(torch.bfloat16)
+        trees = [[-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)] for _ in range(bs)]
+        anc = torch.stack([anc_bits(t, 2) for t in trees]).to(DEV)
+        pl = torch.tensor(prefixes, dtype=torch.int32, device=DEV)
+        out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, pl, D ** -0.5, splits=splits)
+        out = out.float().cpu().numpy()
+        for b in range(bs):
+            P = prefixes[b]
+            kk = k[b].transpose(0, 1).float().numpy()
+            vv = v[b].transpose(0, 1).float().numpy()
+            ref = oracle.tree_attention(q[b].float().numpy(), kk[:P], vv[:P], kk[P:P + n], vv[P:P + n], trees[b],
+                                        D ** -0.5)
+            assert np.abs(out[b] - ref).max() <= TOL, (bs, splits, b)
+    assert ops.tree_attention_status() == 0
