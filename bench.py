@@ -3,9 +3,10 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests-per-gpu R]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
     python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
-    python bench.py --kernel K                             (one kernel of the batch step alone, L2 flushed between
-                                                            launches: logits_step, tree_build, attention, accept;
-                                                            or a commit-step kernel: commit_kv, gdn_commit)
+    python bench.py --kernel K                             (one kernel alone, L2 flushed between launches: a kernel
+                                                            of the batch step -- logits_step, tree_build, attention,
+                                                            accept --, of the commit step -- commit_kv, gdn_commit --,
+                                                            or the paged drafter attention, paged_mode_attn)
 
 Workload (synthetic, seeded per global request id so any partition computes the same
 requests): 32 requests per GPU per step (32/64/128/256 requests at 1/2/4/8 GPUs), each with drafter logits
@@ -278,12 +279,36 @@ def north_star(dev, steps: int, warmup: int):
         times.append(ev[0].elapsed_time(ev[4]) * 1e3)
         for j, name in enumerate(parts):
             parts[name].append(ev[j].elapsed_time(ev[j + 1]) * 1e3)
+    # the same four launches captured once in a CUDA graph and replayed (as a serving loop would run them): the
+    # replay has no host launch gaps between the kernels, which the eager step above can have
+    graph_times = []
+    try:
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step.run()
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        for _ in range(steps):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(2_000_000)
+            s.record()
+            graph.replay()
+            e.record()
+            torch.cuda.synchronize()
+            graph_times.append(s.elapsed_time(e) * 1e3)
+        del graph
+    except RuntimeError as exc:  # capture refused: report the eager step only
+        print(f"north_star: CUDA graph capture failed ({exc}); eager step only", file=sys.stderr)
     alg_bytes = batch.input_bytes()
-    us = statistics.mean(times)
+    us_eager = statistics.mean(times)
+    us = statistics.mean(graph_times) if graph_times else us_eager
     pk = peaks()
     roof_us = alg_bytes / (pk["hbm_gbs"] * 1e9) * 1e6
     return {
-        "us_per_step": round(us, 2), "us_median": round(statistics.median(times), 2),
+        "us_per_step": round(us, 2), "how": "CUDA graph replay" if graph_times else "eager launches",
+        "us_eager": round(us_eager, 2), "us_eager_median": round(statistics.median(times), 2),
         "parts_us": {k: round(statistics.mean(v), 2) for k, v in parts.items()},
         "algorithmic_bytes": alg_bytes, "roofline_us": round(roof_us, 2),
         "frac_of_hbm_roofline": round(roof_us / us, 4),
@@ -409,6 +434,54 @@ def kernel_line(name: str, steps: int, warmup: int, requests: int):
     return {"kernel": name, "requests": requests, "us_per_launch": round(us, 2), "algorithmic_bytes": alg,
             "achieved_gbs": round(alg / us / 1e3, 1), "peak_hbm_gbs": peaks()["hbm_gbs"],
             "frac_of_hbm": round(alg / us / 1e3 / peaks()["hbm_gbs"], 4), "l2": "flushed (256 MB write) per launch"}
+
+
+def paged_line(steps: int, warmup: int, requests: int):
+    """The SGLang paged mode attention of one draft layer for a serving batch: `requests` requests, K = 8 modes of
+    16-token blocks (128 queries x 32 heads each), contexts U(1024, 8192) held in a paged KV cache [slots, 8, 128]
+    whose slots are a random permutation (req_to_token indirection), block keys from this step's k/v.  Device time
+    per launch with the L2 flushed before each; algorithmic bytes = q, out, block k/v, every context key and value
+    and its slot id read once; FLOPs = 4 T H (ctx + 16) D per request."""
+    from mfd_b200.ddtree_mode_attention import paged_mode_block_attention
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Km, bsz = K_MODES, L_BLOCK
+    T1 = Km * bsz
+    ctxs = prefix_lengths(requests)
+    g = torch.Generator(device=dev).manual_seed(11)
+    slots = sum(ctxs) + 1024
+    k_cache = (torch.randn(slots, HKV, D, generator=g, device=dev) * 0.5).bfloat16()
+    v_cache = (torch.randn(slots, HKV, D, generator=g, device=dev) * 0.5).bfloat16()
+    perm = torch.randperm(slots, generator=g, device=dev).to(torch.int32)
+    r2t = torch.zeros(requests, max(ctxs) + 64, dtype=torch.int32, device=dev)
+    off = 0
+    for b, c in enumerate(ctxs):
+        r2t[b, :c] = perm[off:off + c]
+        off += c
+    T = requests * T1
+    q = torch.randn(T, H, D, generator=g, device=dev).bfloat16()
+    k_new = (torch.randn(T, HKV, D, generator=g, device=dev) * 0.5).bfloat16()
+    v_new = (torch.randn(T, HKV, D, generator=g, device=dev) * 0.5).bfloat16()
+    rpi = torch.arange(requests, dtype=torch.int64, device=dev)
+    ctx_t = torch.tensor(ctxs, dtype=torch.int64, device=dev)
+    out = torch.empty_like(q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    us = timed_us(lambda: paged_mode_block_attention(
+        q=q, k_new=k_new, v_new=v_new, k_cache=k_cache, v_cache=v_cache, req_to_token=r2t, req_pool_indices=rpi,
+        ctx_lens=ctx_t, num_modes=Km, block_size=bsz, scaling=D ** -0.5, num_ctx_splits=-1, out=out),
+        steps, warmup, flush)
+    alg = 2 * q.numel() * 2 + 2 * k_new.numel() * 2 + sum(2 * HKV * c * D * 2 for c in ctxs) + sum(ctxs) * 4
+    flops = sum(4 * T1 * H * (c + bsz) * D for c in ctxs)
+    pk = peaks()
+    return {"kernel": "paged_mode_attn", "requests": requests,
+            "workload": f"{requests} requests x {Km} modes x {bsz} queries x {H} heads, contexts U(1024, 8192) "
+                        f"(mean {sum(ctxs) / len(ctxs):.0f}) in a paged cache of {slots} slots",
+            "us_per_launch": round(us, 2), "algorithmic_bytes": alg, "flops": flops,
+            "achieved_gbs": round(alg / us / 1e3, 1), "frac_of_hbm": round(alg / us / 1e3 / pk["hbm_gbs"], 4),
+            "achieved_tflops": round(flops / us / 1e6, 1),
+            "frac_of_tensor": round(flops / us / 1e6 / pk["bf16_tflops"], 4),
+            "l2": "flushed (256 MB write) per launch"}
 
 
 # ------------------------------------------------------------------------------------------------ CPU reference
@@ -612,7 +685,8 @@ def main():
     ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
     ap.add_argument("--kernel", default=None,
-                    choices=["logits_step", "tree_build", "attention", "accept", "commit_kv", "gdn_commit"],
+                    choices=["logits_step", "tree_build", "attention", "accept", "commit_kv", "gdn_commit",
+                             "paged_mode_attn"],
                     help="time one kernel of the batch step alone (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -644,6 +718,9 @@ def main():
         print(json.dumps(line))
         return
 
+    if args.kernel == "paged_mode_attn":
+        print(json.dumps(paged_line(args.steps, args.warmup, args.requests_per_gpu)))
+        return
     if args.kernel is not None:
         fn = commit_line if args.kernel in ("commit_kv", "gdn_commit") else kernel_line
         print(json.dumps(fn(args.kernel, args.steps, args.warmup, args.requests_per_gpu)))

@@ -375,3 +375,24 @@ def commit_kv_moves(pool, move_src, move_tgt):
         for (_, t), v in zip(moves, vals):
             out[:, t] = v
     return out
+
+
+def paged_mode_attention(q, k_new, v_new, k_cache, v_cache, req_to_token, req_pool_indices, ctx_lens, num_modes,
+                         block_size, scale):
+    """SGLang paged_mode_block_attention_reference (sglang-v0.5.22-mfd.patch:965-989): per request, the context
+    rows k_cache[req_to_token[req_pool_indices[b], :ctx_lens[b]]] followed by the request's K*block_size new keys,
+    then the mode-block attention of mode_attention (block-diagonal over the new keys).
+    q [T, H, D], k_new/v_new [T, Hkv, D], caches [slots, Hkv, D] -> [T, H, D] float32."""
+    q = np.asarray(q, np.float32)
+    T, H, D = q.shape
+    KL = num_modes * block_size
+    out = np.empty((T, H, D), np.float32)
+    for b in range(T // KL):
+        ctx = int(ctx_lens[b])
+        slots = np.asarray(req_to_token[int(req_pool_indices[b]), :ctx], np.int64)
+        rows = slice(b * KL, (b + 1) * KL)
+        kk = np.concatenate([np.asarray(k_cache)[slots], np.asarray(k_new)[rows]], 0)  # [ctx + KL, Hkv, D]
+        vv = np.concatenate([np.asarray(v_cache)[slots], np.asarray(v_new)[rows]], 0)
+        out[rows] = mode_attention(q[rows].transpose(1, 0, 2), kk.transpose(1, 0, 2), vv.transpose(1, 0, 2),
+                                   num_modes, block_size, scale)
+    return out
