@@ -276,6 +276,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // keys come from the caches through the request's req_to_token row, block keys from k_new / v_new (keys past
     // the end repeat the last block key and are masked).  One warp instruction moves 4 keys' half rows: lane l
     // takes key 32 t + 4 j + (l >> 3), granule l & 7.
+    // slot ids of the next tile's keys key0 + lane + 32 t (context keys only), loaded one tile ahead so that the
+    // req_to_token read is off the chain of the tile being issued
+    int32_t next_slot[4];
+    auto fetch_slots = [&](int i) {
+        const int key0 = k_lo + i * kKt;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int r = key0 + lane + 32 * t;
+            next_slot[t] = (i < ntiles && r < prefix) ? __ldg(r2t_row + r) : 0;
+        }
+    };
     auto load_kv_paged = [&](int i) {
         const int st = i % kStages;
         const int key0 = k_lo + i * kKt;
@@ -285,9 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < 4; ++t) {
             const int r = key0 + lane + 32 * t;
             rcache[t] = r < prefix;
-            roff[t] = rcache[t] ? (int64_t)min(max(__ldg(r2t_row + r), 0), (int)(p.slots - 1)) * p.skc_t + hk * D
+            roff[t] = rcache[t] ? (int64_t)min(max(next_slot[t], 0), (int)(p.slots - 1)) * p.skc_t + hk * D
                                 : ((int64_t)b * p.n + min(r - prefix, p.n - 1)) * p.skn_t + hk * D;
         }
+        fetch_slots(i + 1);
         const int c = lane & 7;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -346,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.paged) {
             // tile i's copies are issued, then tile i - 1 is published (two tiles' copies in flight); a stage is
             // refilled only after the MMA released it
+            fetch_slots(0);
             for (int i = 0; i < ntiles; ++i) {
                 if (i >= kStages) {
                     bool w = true;
