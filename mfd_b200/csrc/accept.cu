@@ -4,10 +4,14 @@
 // Greedy: post[i] = first index of the row maximum (torch.argmax; inference/hf/model/utils.py:28-30,
 //   SGLang _target_tokens patch:2990-2991).
 // Stochastic (temperature T): the reference draws torch.multinomial(softmax(x/T)) (hf/model/utils.py:31-35),
-//   which is not reproducible.  This build's rule, identical on CPU and GPU bit for bit:
-//     m = max x;  e_i = exp32((x_i - m) * (1/T))  (Cody-Waite reduction + degree-7 Taylor polynomial, fmaf);
-//     E_i = trunc(e_i * 2^40) as uint64;  Z = sum E_i (integer: exact in any order);
-//     token = min { j : sum_{i<=j} E_i > floor(u * Z) }   for the node's uniform u in [0, 1).
+//   which is not reproducible.  This build's rule, identical on CPU (oracle/mfd_oracle.c, sample_row) and GPU
+//   bit for bit, is an inverse-CDF sample of softmax(x/T) whose every sum has a fixed order:
+//     blocks of 256 logits, lane l of a block holding 8 of them; per block the maximum M_b, the weights
+//     e_i = exp32((x_i - M_b) * (1/T)) (Cody-Waite reduction + degree-7 Taylor polynomial, fmaf), lane sums left to
+//     right and their butterfly sum S_b (float32); block weights w_b = S_b * exp32((M_b - m) / T) in double
+//     (m = row max); 32 runs of consecutive blocks summed left to right, the runs summed in order to Z; then the
+//     target u Z is located run -> block -> lane -> logit, each level summing left to right (a level that
+//     rounding leaves without a crossing yields its last logit of positive weight).
 // Walk: from node 0 follow the child whose token equals post[current] (inference/hf/ddtree.py:368-382,
 //   tree_build_ext.py:70-83; SGLang _ddtree_follow_kernel patch:1706-1766 and its outputs: accepted length,
 //   commit length, bonus, emitted tokens, KV move lists, hidden-row indices, new sequence lengths).
@@ -43,14 +47,61 @@ __device__ __forceinline__ float exp32_rule(float y) {
     q = __fmaf_rn(q, r, 1.0f);
     return ok ? __uint_as_float(__float_as_uint(q) + ((uint32_t)ni << 23)) : 0.0f;
 }
-// trunc(e * 2^40) for 0 <= e < 2 from e's fields: e = M * 2^(k - 23) with M the 24-bit significand, so
-// e * 2^40 = M * 2^(k + 17) (exact: the conversion truncates only the fraction); tiny e gives 0.
-__device__ __forceinline__ uint64_t fixed40(float x, float m, float inv_t) {
-    const uint32_t u = __float_as_uint(exp32_rule(__fmul_rn(__fsub_rn(x, m), inv_t)));
-    const int s = (int)(u >> 23) - 127 + 17;
-    const uint32_t M = (u & 0x7FFFFFu) | 0x800000u;
-    if (u == 0u) return 0ull;
-    return s >= 0 ? ((uint64_t)M << s) : (uint64_t)(M >> min(-s, 31));
+// Packed float32 pairs (Blackwell f32x2 arithmetic): every lane of add / sub / mul / fma .rn.f32x2 is the IEEE
+// round-to-nearest result of the scalar operation, so exp32_rule_x2 returns, per lane, exactly exp32_rule's bits
+// with half the floating-point instructions.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t dup2(float a) { return pk2(a, a); }
+// exp32_rule((x0 - m) * c) and exp32_rule((x1 - m) * c), the operations of exp32_rule on both lanes at once (a lane
+// whose argument is not above -87 is computed on and then replaced by 0, as exp32_rule returns)
+__device__ __forceinline__ void exp32_rule_x2(uint64_t x01, uint64_t m2, uint64_t c2, float& e0, float& e1) {
+    const uint64_t y = mul2(sub2(x01, m2), c2);
+    const uint64_t t = add2(mul2(y, dup2(1.44269504088896341f)), dup2(12582912.0f));
+    const uint64_t n = sub2(t, dup2(12582912.0f));
+    uint64_t r = fma2(n, dup2(-0.693359375f), y);
+    r = fma2(n, dup2(2.12194440e-4f), r);
+    uint64_t q = dup2(1.0f / 5040.0f);
+    q = fma2(q, r, dup2(1.0f / 720.0f));
+    q = fma2(q, r, dup2(1.0f / 120.0f));
+    q = fma2(q, r, dup2(1.0f / 24.0f));
+    q = fma2(q, r, dup2(1.0f / 6.0f));
+    q = fma2(q, r, dup2(0.5f));
+    q = fma2(q, r, dup2(1.0f));
+    q = fma2(q, r, dup2(1.0f));
+    float y0, y1, t0, t1, q0, q1;
+    upk2(y, y0, y1);
+    upk2(t, t0, t1);
+    upk2(q, q0, q1);
+    const int n0 = __float_as_int(t0) - 0x4B400000, n1 = __float_as_int(t1) - 0x4B400000;
+    e0 = y0 > -87.0f ? __uint_as_float(__float_as_uint(q0) + ((uint32_t)n0 << 23)) : 0.0f;
+    e1 = y1 > -87.0f ? __uint_as_float(__float_as_uint(q1) + ((uint32_t)n1 << 23)) : 0.0f;
 }
 
 struct Params {
@@ -286,33 +337,12 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
-// sum of the fixed-point weights of x[c0, c1) (one thread, sequential, vector loads when aligned)
-__device__ __forceinline__ uint64_t weight_sum(const uint16_t* x, int64_t c0, int64_t c1, float m, float inv_t) {
-    uint64_t z = 0;
-    int64_t c = c0;
-    if ((((uintptr_t)(x + c)) & 15u) == 0) {
-        for (; c + 8 <= c1; c += 8) {
-            const uint4 w = *reinterpret_cast<const uint4*>(x + c);
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) z += fixed40(bf16lo(ws[q]), m, inv_t) + fixed40(bf16hi(ws[q]), m, inv_t);
-        }
-    }
-    for (; c < c1; ++c) z += fixed40(bf16_at(x + c), m, inv_t);
-    return z;
-}
-
 constexpr int kSampleThreads = 768;
 constexpr int kSampleWarps = kSampleThreads / 32;
-constexpr int kMaxRounds = 64;
-constexpr int kUnroll = 4;      // rounds whose loads are in flight together  // rows up to 64 rounds x 768 threads x 8 elements = 393216 logits
+constexpr int kMaxRounds = 64;  // rows up to 64 rounds x 768 threads x 8 logits = 393216 logits
+constexpr int kUnroll = 4;      // rounds whose loads are in flight together
 
-__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += shfl_xor_u64(v, o);
-    return v;
-}
-// the weights of vector v (elements 8v .. 8v+7 of the row) and its float maximum; absent elements weigh 0
+// the 8 logits of vector v (elements 8v .. 8v+7 of the row); absent elements read as -inf
 __device__ __forceinline__ uint4 load_vec8(const uint16_t* x, int64_t v, int64_t V, bool aligned) {
     const int64_t e0 = v * 8;
     if (aligned && e0 + 8 <= V) return ldg_stream_u4(x + e0);
@@ -325,74 +355,23 @@ __device__ __forceinline__ uint4 load_vec8(const uint16_t* x, int64_t v, int64_t
     }
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
-__device__ __forceinline__ uint64_t vec8_weight(uint4 w, float m, float inv_t) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    uint64_t z = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) z += fixed40(bf16lo(ws[q]), m, inv_t) + fixed40(bf16hi(ws[q]), m, inv_t);
-    return z;
+__device__ __forceinline__ float vec_elem(const uint4& w, int j) {
+    const uint32_t word = j < 2 ? w.x : (j < 4 ? w.y : (j < 6 ? w.z : w.w));
+    return (j & 1) ? bf16hi(word) : bf16lo(word);
+}
+__device__ __forceinline__ double shfl_f64(double v, int src) {
+    return __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(v), src));
 }
 
-// The weight of a logit depends only on its bf16 bit pattern (m and T are fixed per row), so each row first
-// tabulates fixed40 over the patterns it can contain and pass 2 looks weights up instead of evaluating the
-// exponential 150k times.  Table: for each sign, H + 1 entries indexed by t = clamp(magnitude - lo + 1, 0, H):
-//   * t = 0, magnitudes below lo (|x| < tau): every such pattern has the weight of x = 0: with m != 0,
-//     tau = 2^(e_m - 26) is under a quarter ulp of m, so fsub(x, m) == -m exactly; with m == 0, tau = 2^(e_T - 28)
-//     keeps |x / T| < 2^-26, where the polynomial rounds to exactly 1.0, as it does for x = 0;
-//   * t = 1 .. H - 1, magnitudes lo .. hi with hi = the bf16 magnitude at or above 90 T + |m|: fixed40 of the
-//     pattern (positive patterns above m cannot occur: m is the row max);
-//   * t = H, magnitudes beyond hi: (x - m) / T < -88 after rounding for negatives, weight 0 (positives cannot
-//     occur), as for the infinities and NaNs, whose direct weight is 0 too.
-// The clamp runs on both halves of a 32-bit word at once (16-bit SIMD add + min with relu).  Every entry is
-// fixed40 itself, an integer below 2^41, so a thread adds its looked-up weights exactly in double (partial sums stay
-// below 2^53) on the FP64 pipe, and pass 2 sums exactly the values the direct evaluation would.
-constexpr int kTableCap = 12 * 1024;  // entries; rows needing more are evaluated directly
-
-struct RowTable {
-    int lo, H;  // magnitude offset and clamp limit; H < 0: no table
-};
-
-__device__ __forceinline__ int bf16_mag_ceil(float v) {  // smallest bf16 magnitude pattern >= v (v >= 0, finite)
-    uint32_t u = __float_as_uint(v);
-    uint32_t hi = u >> 16;
-    if (u & 0xFFFFu) ++hi;
-    return (int)min(hi, 0x7F80u);
-}
-
-__device__ RowTable plan_table(float m, float inv_t) {
-    RowTable t;
-    t.H = -1;
-    t.lo = 0;
-    if (!isfinite(m) || !(inv_t > 0.f) || !isfinite(inv_t)) return t;
-    const float T = 1.0f / inv_t;
-    float tau;
-    if (m != 0.0f && fabsf(m) >= 1e-30f) {
-        const int e_m = ((__float_as_uint(m) >> 23) & 0xFF) - 127;
-        tau = ldexpf(1.0f, e_m - 26);
-    } else if (m == 0.0f) {
-        const int e_t = ((__float_as_uint(T) >> 23) & 0xFF) - 127;
-        tau = ldexpf(1.0f, max(e_t - 28, -126));
-    } else {
-        return t;  // a tiny nonzero max: evaluate directly
-    }
-    const int lo = (int)(__float_as_uint(tau) >> 16);  // tau is a power of two: exact as bf16 (lo >= 0x80)
-    const int hi = bf16_mag_ceil(90.0f * T + fabsf(m));
-    const int H = max(hi - lo + 2, 1);
-    if (2 * (H + 1) > kTableCap) return t;
-    t.lo = lo;
-    t.H = H;
-    return t;
-}
-
-// stochastic: one 768-thread CTA per row (two resident per SM, so about 300 rows are in flight and the second
-// pass over a row hits L2).  Vector v = r * 768 + t (8 logits) belongs to thread t in round r, so every load is
-// coalesced and the rounds are in row order.  Pass 1: the row max.  Table of weights.  Pass 2: per round, each
-// warp's 256-logit weight sum.  Warp 0 scans the (round, warp) sums in row order to find the one holding
-// floor(u * Z) and searches its 256 logits.  All sums are integers, so no order changes the result.
+// stochastic: one 768-thread CTA per row (two resident per SM).  One pass over the logits: in round r warp w
+// reduces block e = 24 r + w (vector 32 e + lane per lane, so every load is coalesced): the block maximum by
+// warp shuffles, the lane sums of the weights against it, and their butterfly sum; lane 0 keeps (M_b, S_b) in
+// shared memory.  Warp 0 then forms the block weights, the run sums and Z in the rule's order and locates the
+// target run -> block -> lane -> logit (re-reading one block of 256 logits).
 __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
-    extern __shared__ __align__(16) double table[];  // [2][H + 1] (<= kTableCap)
-    __shared__ uint64_t wsum[kMaxRounds * kSampleWarps];
-    __shared__ float wmax[kSampleWarps];
+    __shared__ float blk_m[kMaxRounds * kSampleWarps];
+    __shared__ float blk_s[kMaxRounds * kSampleWarps];
+    __shared__ WalkStage stage;
     __shared__ int flag;
     __shared__ int64_t s_token;
     const int64_t row = blockIdx.x;
@@ -403,71 +382,8 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     const bool aligned = (((uintptr_t)x) & 15u) == 0;
     const int64_t nv = (V + 7) / 8;
     const int rounds = (int)((nv + kSampleThreads - 1) / kSampleThreads);
-    // ---- pass 1: max (bf16 pairs), kUnroll rounds' loads in flight per thread; absent elements read as -inf
-    __nv_bfloat162 mx2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
-    for (int r0 = 0; r0 < rounds; r0 += kUnroll) {
-        uint4 w[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const int64_t v = (int64_t)(r0 + u) * kSampleThreads + threadIdx.x;
-            w[u] = v < nv ? load_vec8(x, v, V, aligned) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) mx2 = __hmax2(mx2, *reinterpret_cast<const __nv_bfloat162*>(&ws[q]));
-        }
-    }
-    float mx = fmaxf(__low2float(mx2), __high2float(mx2));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MFD_FULL_MASK, mx, o));
-    if (lane == 0) wmax[warp] = mx;
-    __syncthreads();
-    float m = wmax[0];
-#pragma unroll 8
-    for (int w = 1; w < kSampleWarps; ++w) m = fmaxf(m, wmax[w]);
     const float inv_t = __frcp_rn(p.temperature);
-    // ---- the row's weight table
-    const RowTable tb = plan_table(m, inv_t);
-    if (tb.H >= 0) {
-        const int half = tb.H + 1;
-        for (int i = threadIdx.x; i < 2 * half; i += kSampleThreads) {
-            const int sg = i >= half ? 1 : 0, t = i - sg * half;
-            uint64_t e;
-            if (t == 0) {
-                e = fixed40(0.0f, m, inv_t);  // every magnitude below tau
-            } else if (t < tb.H) {
-                const uint32_t pat = ((uint32_t)sg << 15) | (uint32_t)(tb.lo + t - 1);
-                const float v = __uint_as_float(pat << 16);
-                e = (sg == 0 && v > m) ? 0ull : fixed40(v, m, inv_t);  // (positives above m cannot occur)
-            } else {
-                e = 0ull;  // beyond the cut, infinities, NaNs
-            }
-            table[i] = (double)e;  // exact: e < 2^41
-        }
-        __syncthreads();
-    }
-    const uint32_t add2 = (uint32_t)(uint16_t)(1 - tb.lo) * 0x10001u;  // both halves: 1 - lo
-    const uint32_t lim2 = (uint32_t)(uint16_t)max(tb.H, 0) * 0x10001u;  // both halves: H
-    const int half_entries = tb.H + 1;
-    // the weight of 8 logits as an exact double (an integer below 2^44)
-    auto vec_weight = [&](uint4 w) -> double {
-        if (tb.H < 0) return (double)vec8_weight(w, m, inv_t);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        double z = 0.0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            // t for both halves at once: clamp(magnitude - lo + 1, 0, H)
-            const uint32_t t2 = __viaddmin_s16x2_relu(ws[q] & 0x7FFF7FFFu, add2, lim2);
-            const int i_lo = (int)(t2 & 0xFFFFu) + (int)((ws[q] >> 15) & 1u) * half_entries;
-            const int i_hi = (int)(t2 >> 16) + (int)(ws[q] >> 31) * half_entries;
-            z += table[i_lo];
-            z += table[i_hi];
-        }
-        return z;
-    };
-    // ---- pass 2: the weight of each (round, warp) block of 256 logits
+    // ---- one pass: block maxima and block sums
     for (int r0 = 0; r0 < rounds; r0 += kUnroll) {
         uint4 w[kUnroll];
 #pragma unroll
@@ -478,76 +394,133 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             if (r0 + u >= rounds) break;
-            // a block of 256 weights sums below 2^52: exact in double; absent elements (-inf) weigh 0
-            double z = vec_weight(w[u]);
+            float mx = -INFINITY;
 #pragma unroll
-            for (int o = 16; o; o >>= 1) z += __shfl_xor_sync(MFD_FULL_MASK, z, o);
-            if (lane == 0) wsum[(r0 + u) * kSampleWarps + warp] = (uint64_t)z;
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, vec_elem(w[u], j));
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MFD_FULL_MASK, mx, o));
+            float sum = 0.0f;
+            if (mx != -INFINITY) {
+                const uint64_t m2 = dup2(mx), c2 = dup2(inv_t);
+                const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {  // logits 2q, 2q + 1: the low and high bf16 of word q
+                    float e0, e1;
+                    exp32_rule_x2(pk2(bf16lo(ws[q]), bf16hi(ws[q])), m2, c2, e0, e1);
+                    sum = __fadd_rn(sum, e0);
+                    sum = __fadd_rn(sum, e1);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(MFD_FULL_MASK, sum, o));
+            if (lane == 0) {
+                blk_m[(r0 + u) * kSampleWarps + warp] = mx;
+                blk_s[(r0 + u) * kSampleWarps + warp] = sum;
+            }
         }
     }
     __syncthreads();
     if (warp == 0) {
-        // exclusive scan over the rounds x warps block sums in row order, a contiguous run of entries per lane
-        const int ne = rounds * kSampleWarps;
-        const int per = (ne + 31) / 32;
-        const int e0 = min(lane * per, ne), e1 = min(e0 + per, ne);
-        uint64_t tot = 0;
-        for (int e = e0; e < e1; ++e) tot += wsum[e];
-        uint64_t incl = tot;
+        const int nb = (int)((V + 255) / 256);
+        float m = -INFINITY;
+        for (int e = lane; e < nb; e += 32) m = fmaxf(m, blk_m[e]);
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t y = shfl_u64(incl, lane >= o ? lane - o : lane);
-            if (lane >= o) incl += y;
-        }
-        const uint64_t Z = shfl_u64(incl, 31);
-        const uint64_t target = (uint64_t)floor(p.uniforms[row] * (double)Z);
-        uint64_t run = incl - tot;
-        int hit = -1;
-        uint64_t before = 0;
-        for (int e = e0; e < e1; ++e) {
-            const uint64_t w = wsum[e];
-            if (hit < 0 && run + w > target) {
-                hit = e;
-                before = run;
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(MFD_FULL_MASK, m, o));
+        auto wblk = [&](int e) -> double {  // the block weight S_b * exp32((M_b - m) / T)
+            const float mb = blk_m[e];
+            if (mb == -INFINITY) return 0.0;
+            return __dmul_rn((double)blk_s[e], (double)exp32_rule(__fmul_rn(__fsub_rn(mb, m), inv_t)));
+        };
+        auto weight = [&](int64_t i, float mb) -> float {  // e_i against its block's maximum
+            return mb == -INFINITY ? 0.0f : exp32_rule(__fmul_rn(__fsub_rn(bf16_at(x + i), mb), inv_t));
+        };
+        // the last logit of positive weight in [lo, hi), or -1
+        auto last_positive = [&](int64_t lo, int64_t hi) -> int64_t {
+            hi = min(hi, V);
+            for (int64_t top = hi; top > lo; top -= 32) {
+                const int64_t i = top - 1 - lane;
+                bool pos = false;
+                if (i >= lo) pos = weight(i, blk_m[i >> 8]) > 0.0f;
+                const uint32_t bal = __ballot_sync(MFD_FULL_MASK, pos);
+                if (bal) return top - 1 - (__ffs(bal) - 1);  // the lowest lane holds the highest index
             }
-            run += w;
+            return -1;
+        };
+        const int per = (nb + 31) / 32;
+        double run = 0.0;
+        for (int e = lane * per; e < (lane + 1) * per && e < nb; ++e) run = __dadd_rn(run, wblk(e));
+        // P_{L+1} = P_L + R_L in lane order (every lane computes the same sums); lane L keeps P_L
+        double P = 0.0, myP = 0.0;
+        for (int L = 0; L < 32; ++L) {
+            const double r = shfl_f64(run, L);
+            if (lane == L) myP = P;
+            P = __dadd_rn(P, r);
         }
-        const uint32_t bal = __ballot_sync(MFD_FULL_MASK, hit >= 0);
-        int64_t tok = V - 1;  // Z == 0 (every logit -inf): no crossing
-        if (bal) {
-            const int src = __ffs(bal) - 1;  // blocks are in lane order: the first lane with a hit holds it
-            const int eh = __shfl_sync(MFD_FULL_MASK, hit, src);
-            const uint64_t base = shfl_u64(before, src);
-            // block eh = (round eh / warps, warp eh % warps): 32 consecutive vectors, one per lane
-            const int64_t v = (int64_t)(eh / kSampleWarps) * kSampleThreads + (eh % kSampleWarps) * 32 + lane;
-            const uint4 w = v < nv ? load_vec8(x, v, V, aligned)
-                                   : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
-            const uint64_t ls = v < nv ? vec8_weight(w, m, inv_t) : 0ull;
-            uint64_t li = ls;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint64_t y = shfl_u64(li, lane >= o ? lane - o : lane);
-                if (lane >= o) li += y;
-            }
-            const uint64_t lex = base + li - ls;
-            const bool in_me = ls > 0 && lex <= target && target < lex + ls;
-            const uint32_t b2 = __ballot_sync(MFD_FULL_MASK, in_me);
-            const int owner = b2 ? __ffs(b2) - 1 : 0;
-            if (b2 && lane == owner) {
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-                uint64_t c = lex;
-                tok = v * 8 + 7;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float xv = (q & 1) ? bf16hi(ws[q >> 1]) : bf16lo(ws[q >> 1]);
-                    c += fixed40(xv, m, inv_t);
-                    if (c > target) {
-                        tok = v * 8 + q;
-                        break;
+        const double Z = P;
+        int64_t tok = V - 1;  // Z == 0: every logit -inf
+        if (Z > 0.0) {
+            const double t = __dmul_rn(p.uniforms[row], Z);
+            const uint32_t cross = __ballot_sync(MFD_FULL_MASK, __dadd_rn(myP, run) > t);
+            if (!cross) {
+                tok = last_positive(0, 256 * (int64_t)nb);
+            } else {
+                const int Ls = __ffs(cross) - 1;
+                const double t1 = __dsub_rn(t, shfl_f64(myP, Ls));
+                // block of run Ls (lane Ls walks its run)
+                int bs = -1;
+                double t2 = 0.0;
+                if (lane == Ls) {
+                    double Q = 0.0;
+                    for (int e = Ls * per; e < (Ls + 1) * per && e < nb; ++e) {
+                        const double Qn = __dadd_rn(Q, wblk(e));
+                        if (Qn > t1) {
+                            bs = e;
+                            t2 = __dsub_rn(t1, Q);
+                            break;
+                        }
+                        Q = Qn;
+                    }
+                }
+                bs = __shfl_sync(MFD_FULL_MASK, bs, Ls);
+                t2 = shfl_f64(t2, Ls);
+                if (bs < 0) {
+                    tok = last_positive(256 * (int64_t)(Ls * per), 256 * (int64_t)((Ls + 1) * per));
+                } else {
+                    const float mb = blk_m[bs];
+                    const double sc = (double)exp32_rule(__fmul_rn(__fsub_rn(mb, m), inv_t));
+                    const int64_t i0 = 256 * (int64_t)bs + 8 * lane;
+                    auto wj = [&](int j) { return i0 + j < V ? __dmul_rn((double)weight(i0 + j, mb), sc) : 0.0; };
+                    double cl = 0.0;
+                    for (int j = 0; j < 8; ++j) cl = __dadd_rn(cl, wj(j));
+                    double B = 0.0, myB = 0.0;
+                    for (int l = 0; l < 32; ++l) {
+                        const double c = shfl_f64(cl, l);
+                        if (lane == l) myB = B;
+                        B = __dadd_rn(B, c);
+                    }
+                    const uint32_t lc = __ballot_sync(MFD_FULL_MASK, __dadd_rn(myB, cl) > t2);
+                    if (!lc) {
+                        tok = last_positive(256 * (int64_t)bs, 256 * (int64_t)bs + 256);
+                    } else {
+                        const int ls = __ffs(lc) - 1;
+                        const double t3 = __dsub_rn(t2, shfl_f64(myB, ls));
+                        int64_t hit = -1, lastpos = -1;
+                        if (lane == ls) {
+                            double a = 0.0;
+                            for (int j = 0; j < 8; ++j) {
+                                const double wv = wj(j);
+                                const double an = __dadd_rn(a, wv);
+                                if (wv > 0.0) lastpos = i0 + j;
+                                if (hit < 0 && an > t3 && wv > 0.0) hit = i0 + j;
+                                a = an;
+                            }
+                            if (hit < 0) hit = lastpos;
+                        }
+                        tok = (int64_t)__shfl_sync(MFD_FULL_MASK, (long long)hit, ls);
                     }
                 }
             }
-            tok = __shfl_sync(MFD_FULL_MASK, (long long)tok, owner);
+            if (tok < 0) tok = V - 1;
         }
         if (lane == 0) s_token = tok;
     }
@@ -562,7 +535,7 @@ __global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
     __syncthreads();
     if (!flag) return;
     __threadfence();
-    if (threadIdx.x < 32) walk_request(p, b, sizeof(WalkStage) <= kTableCap * sizeof(double) ? reinterpret_cast<WalkStage*>(table) : nullptr);
+    if (threadIdx.x < 32) walk_request(p, b, &stage);
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
@@ -615,13 +588,7 @@ static int launch_accept(accept::Params& p, int64_t rows, void* scratch, unsigne
         accept::greedy_kernel<<<(unsigned)(rows * p.parts), accept::kGreedyThreads, 0, stream>>>(p);
     } else {
         p.parts = 1;
-        const int smem = accept::kTableCap * (int)sizeof(uint64_t);
-        cudaError_t e = cudaFuncSetAttribute(accept::sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) {
-            set_error("%s: %s", fn, cudaGetErrorString(e));
-            return MFD_ERR_CUDA;
-        }
-        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, smem, stream>>>(p);
+        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
     }
     MFD_CHECK_LAUNCH(fn);
     return MFD_OK;

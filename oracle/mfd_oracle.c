@@ -22,11 +22,10 @@
  *                             patch lines 1706-1766, which walks at most L-1 edges)
  *   - oracle_sample_rows    : this build's seeded, reproducible sampling rule (the reference
  *                             samples with torch.multinomial, hf/model/utils.py:28-35, which is
- *                             not reproducible, so parity of the sample itself is unpinned):
- *                             e_i = exp32((x_i - m) * (1/T)) with the Cody-Waite + Taylor exp
- *                             below, E_i = trunc(e_i * 2^40) as uint64, Z = sum E_i (exact integer
- *                             sum, so any summation order agrees), token = min{ j : sum_{i<=j} E_i
- *                             > floor(u * Z) }.
+ *                             not reproducible, so parity of the sample itself is unpinned): an
+ *                             inverse-CDF sample of softmax(x / T) whose every sum has a fixed
+ *                             order (see sample_row below), so the CUDA kernel returns the same
+ *                             token bit for bit.
  *   - oracle_argmax_rows    : torch.argmax semantics on bf16 rows (first index of the maximum).
  *
  * Build: gcc -O2 -ffp-contract=off -fPIC -shared (oracle/Makefile).  -ffp-contract=off keeps
@@ -401,29 +400,133 @@ static float mfd_exp32(float y) {
 float oracle_exp32(float y) { return mfd_exp32(y); }
 
 /*
+ * The sampling rule, one row x[0, V) of bf16 logits, c = 1/T (float32), u in [0, 1):
+ *   blocks      b = 0 .. nb-1 of 256 logits (positions past V count as -inf); lane l of a block holds its
+ *               logits 8l .. 8l+7.
+ *   block max   M_b (float32 maximum; -inf for a block of -inf).
+ *   weights     e_i = exp32((x_i - M_b) * c) in float32 (0 when M_b = -inf).
+ *   block sum   s_l = e_{8l} + ... + e_{8l+7} added left to right in float32, then the 32 lane sums by the
+ *               butterfly v_l <- v_l + v_{l xor o} for o = 16, 8, 4, 2, 1; S_b = v_0.
+ *   row max     m = max_b M_b;  block weight w_b = (double)S_b * (double)exp32((M_b - m) * c) (0 for M_b = -inf).
+ *   runs        run L = blocks [L p, L p + p), p = ceil(nb / 32), L = 0 .. 31; R_L = sum of its w_b left to right
+ *               in double from 0.
+ *   total       P_0 = 0, P_{L+1} = P_L + R_L in double; Z = P_32; Z = 0 (every logit -inf): token V - 1.
+ *   target      t = u Z.
+ *   run         L* = first L with P_{L+1} > t; t1 = t - P_{L*}.
+ *   block       Q = 0; for b in run L*: Q' = Q + w_b; first b with Q' > t1 is b*, t2 = t1 - Q.
+ *   lane        in b*, c_l = sum over its 8 logits of (double)e_i * sc (sc = exp32((M_b* - m) * c)) left to right
+ *               from 0; B_0 = 0, B_{l+1} = B_l + c_l; l* = first l with B_{l+1} > t2; t3 = t2 - B_{l*}.
+ *   logit       a = 0; for the 8 logits j of lane l*: a' = a + (double)e_j * sc; first j with a' > t3 and a
+ *               positive weight is the token.
+ *   Where rounding leaves a level without a crossing, the token is the last logit of positive weight in that
+ *   level's range (the run, the block, the lane).
+ * Every block is reduced independently (one pass over the logits on the GPU: block maximum, then weights), and
+ * every later sum has the order written above, so the kernel and this restatement agree bit for bit.
+ */
+static float row_x(const uint16_t* x, int64_t V, int64_t i) { return i < V ? bf16_to_f32(x[i]) : -INFINITY; }
+
+static int64_t last_positive(const uint16_t* x, int64_t V, int64_t lo, int64_t hi, const float* M, float inv_temp) {
+    /* the last logit of positive weight in [lo, hi), or -1 */
+    for (int64_t i = (hi < V ? hi : V) - 1; i >= lo; --i) {
+        const float mb = M[i / 256];
+        if (mb == -INFINITY) continue;
+        if (mfd_exp32((row_x(x, V, i) - mb) * inv_temp) > 0.0f) return i;
+    }
+    return -1;
+}
+
+static int64_t sample_row(const uint16_t* x, int64_t V, float inv_temp, double u, float* M, float* S) {
+    const int64_t nb = (V + 255) / 256;
+    for (int64_t b = 0; b < nb; ++b) {
+        float mb = -INFINITY;
+        for (int64_t i = 256 * b; i < 256 * b + 256; ++i) { const float v = row_x(x, V, i); if (v > mb) mb = v; }
+        float lane[32], tmp[32];
+        for (int l = 0; l < 32; ++l) {
+            float s = 0.0f;
+            for (int j = 0; j < 8; ++j) {
+                const float v = row_x(x, V, 256 * b + 8 * l + j);
+                const float e = mb == -INFINITY ? 0.0f : mfd_exp32((v - mb) * inv_temp);
+                s = s + e;
+            }
+            lane[l] = s;
+        }
+        for (int o = 16; o >= 1; o >>= 1) {
+            for (int l = 0; l < 32; ++l) tmp[l] = lane[l] + lane[l ^ o];
+            memcpy(lane, tmp, sizeof(lane));
+        }
+        M[b] = mb;
+        S[b] = lane[0];
+    }
+    float m = -INFINITY;
+    for (int64_t b = 0; b < nb; ++b) if (M[b] > m) m = M[b];
+    const int64_t per = (nb + 31) / 32;
+#define W_OF(b) (M[b] == -INFINITY ? 0.0 : (double)S[b] * (double)mfd_exp32((M[b] - m) * inv_temp))
+    double R[32], P[33];
+    for (int L = 0; L < 32; ++L) {
+        double acc = 0.0;
+        for (int64_t b = L * per; b < (L + 1) * per && b < nb; ++b) acc = acc + W_OF(b);
+        R[L] = acc;
+    }
+    P[0] = 0.0;
+    for (int L = 0; L < 32; ++L) P[L + 1] = P[L] + R[L];
+    const double Z = P[32];
+    if (!(Z > 0.0)) return V - 1;
+    const double t = u * Z;
+    int Ls = -1;
+    for (int L = 0; L < 32; ++L) if (P[L + 1] > t) { Ls = L; break; }
+    if (Ls < 0) { const int64_t f = last_positive(x, V, 0, 256 * nb, M, inv_temp); return f < 0 ? V - 1 : f; }
+    const double t1 = t - P[Ls];
+    int64_t bs = -1;
+    double t2 = 0.0;
+    {
+        double Q = 0.0;
+        for (int64_t b = Ls * per; b < (Ls + 1) * per && b < nb; ++b) {
+            const double Qn = Q + W_OF(b);
+            if (Qn > t1) { bs = b; t2 = t1 - Q; break; }
+            Q = Qn;
+        }
+    }
+    if (bs < 0) {
+        const int64_t f = last_positive(x, V, 256 * (Ls * per), 256 * ((Ls + 1) * per), M, inv_temp);
+        return f < 0 ? V - 1 : f;
+    }
+    const float mb = M[bs];
+    const double sc = (double)mfd_exp32((mb - m) * inv_temp);
+    double B = 0.0, t3 = 0.0;
+    int ls = -1;
+    for (int l = 0; l < 32; ++l) {
+        double cl = 0.0;
+        for (int j = 0; j < 8; ++j) cl = cl + (double)mfd_exp32((row_x(x, V, 256 * bs + 8 * l + j) - mb) * inv_temp) * sc;
+        const double Bn = B + cl;
+        if (Bn > t2) { ls = l; t3 = t2 - B; break; }
+        B = Bn;
+    }
+    if (ls < 0) { const int64_t f = last_positive(x, V, 256 * bs, 256 * bs + 256, M, inv_temp); return f < 0 ? V - 1 : f; }
+    double a = 0.0;
+    for (int j = 0; j < 8; ++j) {
+        const double w = (double)mfd_exp32((row_x(x, V, 256 * bs + 8 * ls + j) - mb) * inv_temp) * sc;
+        const double an = a + w;
+        if (an > t3 && w > 0.0) return 256 * bs + 8 * ls + j;
+        a = an;
+    }
+    {
+        const int64_t f = last_positive(x, V, 256 * bs + 8 * ls, 256 * bs + 8 * ls + 8, M, inv_temp);
+        return f < 0 ? V - 1 : f;
+    }
+#undef W_OF
+}
+
+/*
  * rows: [R, V] bf16 (as uint16), inv_temp: 1/T as float32, u: [R] float64 uniforms in [0, 1).
- * out: [R] int64 sampled token per row (see the header for the rule).
+ * out: [R] int64 sampled token per row (the rule above).
  */
 void oracle_sample_rows(const uint16_t* rows, int64_t R, int64_t V, float inv_temp, const double* u, int64_t* out) {
-    for (int64_t r = 0; r < R; ++r) {
-        const uint16_t* x = rows + r * V;
-        float m = -INFINITY;
-        for (int64_t i = 0; i < V; ++i) { float v = bf16_to_f32(x[i]); if (v > m) m = v; }
-        uint64_t Z = 0;
-        for (int64_t i = 0; i < V; ++i) {
-            float e = mfd_exp32((bf16_to_f32(x[i]) - m) * inv_temp);
-            Z += (uint64_t)(e * 1099511627776.0f); /* 2^40, exact scaling; trunc toward zero */
-        }
-        uint64_t target = (uint64_t)floor(u[r] * (double)Z);
-        uint64_t c = 0;
-        int64_t tok = V - 1;
-        for (int64_t i = 0; i < V; ++i) {
-            float e = mfd_exp32((bf16_to_f32(x[i]) - m) * inv_temp);
-            c += (uint64_t)(e * 1099511627776.0f);
-            if (c > target) { tok = i; break; }
-        }
-        out[r] = tok;
-    }
+    const int64_t nb = (V + 255) / 256;
+    float* M = (float*)malloc(sizeof(float) * (size_t)nb);
+    float* S = (float*)malloc(sizeof(float) * (size_t)nb);
+    for (int64_t r = 0; r < R; ++r) out[r] = sample_row(rows + r * V, V, inv_temp, u[r], M, S);
+    free(M);
+    free(S);
 }
 
 /* rows [R, V] bf16 -> first index of the row maximum (torch.argmax on finite values). */
