@@ -107,10 +107,11 @@ def test_sample_tokens_edge_rows_bit_exact():
 
 @pytest.mark.parametrize("scale,shift,T", [(1.5, 0.0, 1.0), (0.5, -3.0, 0.1), (3.0, 0.0, 10.0), (0.001, 0.0, 1.0),
                                            (300.0, 20.0, 2.0), (1.0, -50.0, 0.7)])
-def test_sample_tokens_weight_table_regimes(scale, shift, T):
+def test_sample_tokens_value_regimes(scale, shift, T):
     """Rows whose max is positive, negative, zero (all logits <= 0), tiny or large, at small and large
-    temperatures: the per-row weight table (or the direct evaluation it falls back to) reproduces the oracle's
-    integer weights bit for bit."""
+    temperatures (block maxima far apart, weights that underflow to 0 within a block or across blocks): the
+    one-pass kernel's block sums, block weights and fixed-order run sums reproduce the oracle's token bit for
+    bit."""
     from mfd_b200 import ops
     V = 151936
     g = torch.Generator().manual_seed(int(scale * 7 + T * 13))
