@@ -99,9 +99,10 @@ __device__ __forceinline__ void exp32_rule_x2(uint64_t x01, uint64_t m2, uint64_
     upk2(y, y0, y1);
     upk2(t, t0, t1);
     upk2(q, q0, q1);
-    const int n0 = __float_as_int(t0) - 0x4B400000, n1 = __float_as_int(t1) - 0x4B400000;
-    e0 = y0 > -87.0f ? __uint_as_float(__float_as_uint(q0) + ((uint32_t)n0 << 23)) : 0.0f;
-    e1 = y1 > -87.0f ? __uint_as_float(__float_as_uint(q1) + ((uint32_t)n1 << 23)) : 0.0f;
+    // 2^n into the exponent field: (bits(t) - 0x4B400000) << 23 equals bits(t) << 23 modulo 2^32 (0x4B400000's
+    // set bits all shift out), so one shift-add per lane gives exp32_rule's bits
+    e0 = y0 > -87.0f ? __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)) : 0.0f;
+    e1 = y1 > -87.0f ? __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)) : 0.0f;
 }
 
 struct Params {
@@ -337,9 +338,10 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
-constexpr int kSampleThreads = 768;
+constexpr int kSampleThreads = 512;
+constexpr int kSampleCtasPerSm = 3;  // (40 registers a thread)
 constexpr int kSampleWarps = kSampleThreads / 32;
-constexpr int kMaxRounds = 64;  // rows up to 64 rounds x 768 threads x 8 logits = 393216 logits
+constexpr int kMaxRounds = 96;  // rows up to 96 rounds x 512 threads x 8 logits = 393216 logits
 constexpr int kUnroll = 4;      // rounds whose loads are in flight together
 
 // the 8 logits of vector v (elements 8v .. 8v+7 of the row); absent elements read as -inf
@@ -363,12 +365,13 @@ __device__ __forceinline__ double shfl_f64(double v, int src) {
     return __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(v), src));
 }
 
-// stochastic: one 768-thread CTA per row (two resident per SM).  One pass over the logits: in round r warp w
-// reduces block e = 24 r + w (vector 32 e + lane per lane, so every load is coalesced): the block maximum by
+// stochastic: one 512-thread CTA per row (three resident per SM, so a CTA's serial search holds a third of an SM's
+// warps).  One pass over the logits: in round r warp w reduces block e = 16 r + w (vector 32 e + lane per lane,
+// so every load is coalesced): the block maximum by
 // warp shuffles, the lane sums of the weights against it, and their butterfly sum; lane 0 keeps (M_b, S_b) in
 // shared memory.  Warp 0 then forms the block weights, the run sums and Z in the rule's order and locates the
 // target run -> block -> lane -> logit (re-reading one block of 256 logits).
-__global__ void __launch_bounds__(kSampleThreads, 2) sample_kernel(Params p) {
+__global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kernel(Params p) {
     __shared__ float blk_m[kMaxRounds * kSampleWarps];
     __shared__ float blk_s[kMaxRounds * kSampleWarps];
     __shared__ WalkStage stage;
