@@ -262,7 +262,7 @@ def time_steps(step: Step, steps: int, warmup: int, ws: int, dev_index: int):
     return total_ms, per_kernel, clocks.summary()
 
 
-def north_star(dev, steps: int, warmup: int):
+def north_star(dev, steps: int, warmup: int, graph: bool = True):
     """Batch 1, greedy, prefix 4096: BASELINE's headline verify step; L2 flushed between timed steps."""
     prefixes = [4096]
     batch = Batch([0], prefixes, dev, temperature=0.0, target_std=1.0, uniform_prefix=4096)
@@ -282,25 +282,26 @@ def north_star(dev, steps: int, warmup: int):
     # the same four launches captured once in a CUDA graph and replayed (as a serving loop would run them): the
     # replay has no host launch gaps between the kernels, which the eager step above can have
     graph_times = []
-    try:
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step.run()
-        for _ in range(max(warmup, 3)):
-            graph.replay()
-        for _ in range(steps):
-            flush.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda._sleep(2_000_000)
-            s.record()
-            graph.replay()
-            e.record()
+    if graph:  # (single-process runs only: under torchrun the process group's threads share the device)
+        try:
             torch.cuda.synchronize()
-            graph_times.append(s.elapsed_time(e) * 1e3)
-        del graph
-    except RuntimeError as exc:  # capture refused: report the eager step only
-        print(f"north_star: CUDA graph capture failed ({exc}); eager step only", file=sys.stderr)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                step.run()
+            for _ in range(max(warmup, 3)):
+                g.replay()
+            for _ in range(steps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda._sleep(2_000_000)
+                s.record()
+                g.replay()
+                e.record()
+                torch.cuda.synchronize()
+                graph_times.append(s.elapsed_time(e) * 1e3)
+            del g
+        except RuntimeError as exc:  # capture refused: report the eager step only
+            print(f"north_star: CUDA graph capture failed ({exc}); eager step only", file=sys.stderr)
     alg_bytes = batch.input_bytes()
     us_eager = statistics.mean(times)
     us = statistics.mean(graph_times) if graph_times else us_eager
@@ -774,7 +775,7 @@ def main():
     }
     if not args.no_extras:
         if rank == 0:
-            line["north_star"] = north_star(dev, steps=20, warmup=args.warmup)
+            line["north_star"] = north_star(dev, steps=20, warmup=args.warmup, graph=ws == 1)
         barrier(ws)
         line["e2e"] = e2e(dev, reqs, prefixes, steps=3, ws=ws)
         if ws == 1:
