@@ -744,7 +744,7 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
             // (a new group) goes to the lane and slot of group `groups`
             uint32_t ck = kNoKey;
             double cw = 0.0;
-            int cdep = 0;
+            int cdep = 0, ptok = 0, ppar = 0, pd = 0;
             if (lane == owner) {
                 const int sl = k0 == wmin ? 0 : (k1 == wmin ? 1 : 2);
                 const double w = sl == 0 ? w0 : (sl == 1 ? w1 : w2);
@@ -772,12 +772,11 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
                 if (sl == 0) { k0 = nk; w0 = nw; r0 = r + 1; }
                 else if (sl == 1) { k1 = nk; w1 = nw; r1 = r + 1; }
                 else { k2 = nk; w2 = nw; r2 = r + 1; }
-                ekey[i] = wmin;
-                f.etok[m * B + i] = tok;
-                f.epl[m * B + i] = (int16_t)par;
-                f.edep[m * B + i] = (uint8_t)d;
-                f.ehash[m * B + i] = path_hash(par < 0 ? kRootPath : f.ehash[m * B + par], tok);
+                ptok = tok;
+                ppar = par;
+                pd = d;
             }
+            // hand the child over first (the next pop waits on it), then record the popped entry
             cdep = __shfl_sync(MFD_FULL_MASK, cdep, owner);
             if (cdep > 0) {
                 ck = __shfl_sync(MFD_FULL_MASK, ck, owner);
@@ -789,6 +788,14 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
                     else if (sl == 1) { k1 = ck; w1 = cw; r1 = 0; d1 = cdep; q1 = i; }
                     else { k2 = ck; w2 = cw; r2 = 0; d2 = cdep; q2 = i; }
                 }
+            }
+            __syncwarp();  // the parent's path hash (an earlier pop, maybe by another lane) is visible
+            if (lane == owner) {
+                ekey[i] = wmin;
+                f.etok[m * B + i] = ptok;
+                f.epl[m * B + i] = (int16_t)ppar;
+                f.edep[m * B + i] = (uint8_t)pd;
+                f.ehash[m * B + i] = path_hash(ppar < 0 ? kRootPath : f.ehash[m * B + ppar], ptok);
             }
         }
         bad = __any_sync(MFD_FULL_MASK, bad);
@@ -887,9 +894,10 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
             }
             if (lane == 31) sh_wsum[warp] = incl;
             __syncthreads();
-            int base = 0;
-            for (int w = 0; w < warp; ++w) base += sh_wsum[w];
-            int run = base + incl - local;
+            int wv = lane < warp ? sh_wsum[lane] : 0;  // the totals of the warps before this one
+#pragma unroll
+            for (int o = 16; o; o >>= 1) wv += __shfl_xor_sync(MFD_FULL_MASK, wv, o);
+            int run = wv + incl - local;
             for (int x = p0; x < p1; ++x) {
                 const int fl = f.pnid[x];
                 f.pnid[x] = (int16_t)(fl ? run + 1 : 0);
