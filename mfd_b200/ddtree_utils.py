@@ -16,6 +16,8 @@ draft top-k, tree build, verify inputs and walk all stay on the device.
 
 from __future__ import annotations
 
+import json
+import os
 from typing import Optional
 
 import torch
@@ -62,6 +64,31 @@ def row_logsumexp(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.
         ids = torch.empty(rows, 1, dtype=torch.int32, device=x.device)
         ops.topk_logz(x, 1, ids_dtype=torch.int32, out=(top, ids, out))
     return out
+
+
+def ddtree_draft_vocab_path() -> str:
+    """Token-id list of the reduced draft vocabulary ("" = the full vocabulary): the SGLANG_DFLASH_DDTREE_DRAFT_VOCAB
+    setting of the SGLang patch (P:1221-1223), read from the environment."""
+    return str(os.environ.get("SGLANG_DFLASH_DDTREE_DRAFT_VOCAB", "") or "").strip()
+
+
+def load_draft_vocab(path: str, *, vocab_size: int) -> torch.Tensor:
+    """The draft vocabulary at ``path`` (P:1226-1244) as sorted unique int64 token ids on the CPU: a JSON list, a
+    JSON object with "token_ids", or whitespace-separated ids.  Sorting keeps the full vocabulary's relative order
+    in the subset.  Ids outside [0, vocab_size), or none at all, raise ValueError."""
+    with open(path) as f:
+        text = f.read()
+    try:
+        spec = json.loads(text)
+        ids = spec["token_ids"] if isinstance(spec, dict) else spec
+    except ValueError:
+        ids = text.split()
+    ids = sorted({int(i) for i in ids})
+    if not ids or ids[0] < 0 or ids[-1] >= vocab_size:
+        raise ValueError(
+            f"SGLANG_DFLASH_DDTREE_DRAFT_VOCAB={path!r}: token ids must lie in [0, {vocab_size}), "
+            f"got {len(ids)} ids in [{ids[0] if ids else None}, {ids[-1] if ids else None}].")
+    return torch.tensor(ids, dtype=torch.int64)
 
 
 class DDTreeDraftTopK:

@@ -49,3 +49,28 @@ def test_tree_context_conv_windows_match_reference():
     assert ctx.conv_index_cpu == z["conv_index"].tolist()
     cp, cv = qwen35_tree.chain_tree(6)
     assert cp == z["chain_parents"].tolist() and torch.equal(cv, torch.from_numpy(z["chain_vis"]))
+
+
+def test_load_draft_vocab_formats(tmp_path, monkeypatch):
+    """The reduced draft vocabulary loader (P:1226-1244): JSON list, JSON object with "token_ids", whitespace
+    separated ids; sorted unique int64; out-of-range or empty lists raise ValueError."""
+    a = tmp_path / "a.json"
+    a.write_text("[5, 3, 3, 9]")
+    b = tmp_path / "b.json"
+    b.write_text('{"token_ids": [7, 1]}')
+    c = tmp_path / "c.txt"
+    c.write_text("4 2\n8")
+    assert ddtree_utils.load_draft_vocab(str(a), vocab_size=10).tolist() == [3, 5, 9]
+    assert ddtree_utils.load_draft_vocab(str(b), vocab_size=10).tolist() == [1, 7]
+    t = ddtree_utils.load_draft_vocab(str(c), vocab_size=10)
+    assert t.tolist() == [2, 4, 8] and t.dtype == torch.int64
+    with pytest.raises(ValueError):
+        ddtree_utils.load_draft_vocab(str(a), vocab_size=9)
+    d = tmp_path / "d.json"
+    d.write_text("[]")
+    with pytest.raises(ValueError):
+        ddtree_utils.load_draft_vocab(str(d), vocab_size=9)
+    monkeypatch.setenv("SGLANG_DFLASH_DDTREE_DRAFT_VOCAB", f" {a} ")
+    assert ddtree_utils.ddtree_draft_vocab_path() == str(a)
+    monkeypatch.delenv("SGLANG_DFLASH_DDTREE_DRAFT_VOCAB")
+    assert ddtree_utils.ddtree_draft_vocab_path() == ""
