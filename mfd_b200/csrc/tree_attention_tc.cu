@@ -9,25 +9,27 @@
 // split are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.  With per-request prefix
 // lengths (up to 64 requests) the CTAs of the longest requests are launched first, so the short ones fill the tail.
 //
-// Warp roles (576 threads):
-//   warp 0       producer: Q once by TMA, then 128-key K and V tiles into a 3-stage ring (128-byte swizzle, the
-//                canonical UMMA K-major / MN-major layouts; no multicast) -- by TMA from dense [bs, Hkv, S, 128]
-//                caches, or, in paged mode (SGLang's paged mode attention), gathered row by row with 16-byte
-//                cp.async through the request's req_to_token row into the same swizzled layout
-//   warp 1       MMA issuer: S[i%2] = Q K_i^T (M=128, N=128, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
-//                (M=128, N=128, K=16 x 8, A = P read from TMEM, V MN-major), so the scores of tile i are computed
-//                while the softmax works on tile i-1
-//   warps 2..17  softmax: the four warps of TMEM lane quarter q each take 32 of a tile's 128 key columns (row max
-//                and, at the end, row sum exchanged through shared memory): tcgen05.ld of S, mask (only tiles
-//                reaching the tree keys or the split end), exp2, bf16 P written back over S in TMEM; lazy O rescale
-//                in TMEM only when a row's running max grows by more than 2^8.  A quarter whose 32 rows are all
-//                padding (the last M-tile holds 4 of 128 rows for 65 x 4) keeps only the barrier protocol.
-//                Epilogue through a shared-memory stage so every store is coalesced.
+// The kernel is a template over its tile configuration (Cfg below); the launched one has 128-key tiles, a 3-stage
+// ring, 16 softmax warps and one CTA per SM.  Warp roles (576 threads):
+//   warp 0       producer: Q once by TMA, then K and V tiles into the ring (128-byte swizzle, the canonical UMMA
+//                K-major / MN-major layouts; no multicast) -- by TMA from dense [bs, Hkv, S, 128] caches, or, in
+//                paged mode (SGLang's paged mode attention), gathered row by row with 16-byte cp.async through the
+//                request's req_to_token row into the same swizzled layout
+//   warp 1       MMA issuer: S[i%2] = Q K_i^T (M=128, N=tile keys, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
+//                (M=128, N=128, A = P read from TMEM, V MN-major), so the scores of tile i are computed while the
+//                softmax works on tile i-1
+//   warps 2..    softmax: the PARTS warps of TMEM lane quarter q each take 32 of a tile's key columns and 128 /
+//                PARTS of O's columns (row max and, at the end, row sum exchanged through shared memory):
+//                tcgen05.ld of S, mask (only tiles reaching the tree keys or the split end), exp2, bf16 P written
+//                back over S in TMEM; lazy O rescale in TMEM only when a row's running max grows by more than 2^8.
+//                A quarter whose 32 rows are all padding (the last M-tile holds 4 of 128 rows for 65 x 4) keeps
+//                only the barrier protocol.  Epilogue through a shared-memory stage so every store is coalesced.
 // Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
 // merges all splits and writes bf16 out.  With one split the CTA writes out directly.
 //
-// TMEM: O at columns [0, 128), S[0] at [128, 256), S[1] at [256, 384).  Every mbarrier wait is bounded; when one
-// gives up the CTA records a nonzero status, finishes without waiting further, and still releases its TMEM.
+// TMEM: O at columns [0, 128), S[0] and S[1] after it (one column per tile key each): 512 columns allocated.
+// Every mbarrier wait is bounded; when one gives up the CTA records a nonzero status, finishes without waiting
+// further, and still releases its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,28 +40,54 @@ namespace mfd {
 namespace tca {
 
 constexpr int D = 128;
-constexpr int kKt = 128;       // keys per tile
-constexpr int kStages = 3;     // K/V ring depth
-constexpr int kParts = 4;      // softmax warps per TMEM lane quarter, each taking 32 of a tile's 128 key columns
-constexpr int kSoftmaxThreads = 128 * kParts;
-constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, warps 2..17 softmax
-constexpr int kTmemCols = 512;
-constexpr int kSCol = 128;     // S[b] at column kSCol + 128 b; P[b] (bf16 pairs) over its first 64 columns
+constexpr int kSmemMax = 227 * 1024;  // the per-block opt-in maximum
+constexpr int kSmemPerSm = 228 * 1024;  // per SM, of which 1 KB per resident block is reserved
 
-constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
-constexpr int kKVBytes = kKt * D * 2;  // 32 KB: [2 d-halves][128 keys][128 B]
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kQBytes;
-constexpr int kOffV = kOffK + kStages * kKVBytes;
-constexpr int kOffX = kOffV + kStages * kKVBytes;  // row maxima / sums exchanged by the column parts of a row
-constexpr int kOffBar = kOffX + kParts * kM * 4;
-constexpr int kSmemUsed = kOffBar + 128;            // + barriers, TMEM address, flags
-constexpr int kSmemMax = 227 * 1024;                // the per-block opt-in maximum
-// the 128-byte-swizzled TMA destinations need a 1024-byte aligned base: the slack that fits is reserved and the
-// kernel checks at entry that the base's misalignment is within it
-constexpr int kSmemSlack = kSmemMax - kSmemUsed < 1024 ? kSmemMax - kSmemUsed : 1024;
-constexpr int kSmemBytes = kSmemUsed + kSmemSlack;
-static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemMax, "shared memory");
+// A kernel configuration: keys per tile, K/V ring depth, softmax warps per TMEM lane quarter (each takes 32 of a
+// tile's key columns and D / PARTS of O's columns), and resident CTAs per SM.  The launched one, CfgWide =
+// Cfg<128, 3, 4, 1>: one CTA per SM, 227 KB of shared memory, 512 TMEM columns.  (Cfg<64, 2, 2, 2>, two CTAs per
+// SM with 99 KB and 256 TMEM columns each, passes the same tests but ran the 32-request verify step's attention in
+// 348 us against 280 us.)
+template <int KT, int STAGES, int PARTS, int MINB>
+struct Cfg {
+    static constexpr int kKt = KT;
+    static constexpr int kStages = STAGES;
+    static constexpr int kParts = PARTS;
+    static constexpr int kCtasPerSm = MINB;
+    static constexpr int kOCols = D / PARTS;  // O columns each part rescales and stores
+    static constexpr int kSoftmaxThreads = 128 * PARTS;
+    static constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, then the softmax warps
+    static constexpr int kSCol = 128;  // S[b] at column kSCol + KT b; P[b] (bf16 pairs) over its first KT / 2 columns
+    static constexpr int kTmemCols = kSCol + 2 * KT <= 256 ? 256 : 512;
+    static constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
+    static constexpr int kKVBytes = KT * D * 2;   // [2 d-halves][KT keys][128 B]
+    static constexpr int kOffQ = 0;
+    static constexpr int kOffK = kOffQ + kQBytes;
+    static constexpr int kOffV = kOffK + STAGES * kKVBytes;
+    static constexpr int kOffX = kOffV + STAGES * kKVBytes;  // row maxima / sums exchanged by the parts of a row
+    static constexpr int kOffBar = kOffX + PARTS * kM * 4;
+    static constexpr int kSmemUsed = kOffBar + 128;  // + barriers, TMEM address, flags
+    static constexpr int kSmemCap = MINB == 1 ? kSmemMax : kSmemPerSm / MINB - 1024;
+    // the 128-byte-swizzled TMA destinations need a 1024-byte aligned base: the slack that fits is reserved and
+    // the kernel checks at entry that the base's misalignment is within it
+    static constexpr int kSmemSlack = kSmemCap - kSmemUsed < 1024 ? kSmemCap - kSmemUsed : 1024;
+    static constexpr int kSmemBytes = kSmemUsed + kSmemSlack;
+    // barrier slots
+    static constexpr int kBarQ = 0;
+    static constexpr int kBarKVFull = 1;                      // + stage
+    static constexpr int kBarKVEmpty = kBarKVFull + STAGES;   // + stage
+    static constexpr int kBarSFull = kBarKVEmpty + STAGES;    // + buffer
+    static constexpr int kBarPFull = kBarSFull + 2;  // + buffer (P written into S[b]; also frees S[b] for tile + 2)
+    static constexpr int kBarPV = kBarPFull + 2;     // + buffer: P V of tile j completes kBarPV + j % 2
+    static constexpr int kNumBars = kBarPV + 2;
+    static_assert(KT / PARTS == 32, "each softmax warp takes 32 key columns");
+    static_assert(kOCols % 32 == 0, "O columns per part");
+    static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemCap, "shared memory");
+    static_assert(STAGES * kKVBytes >= kM * 256, "the epilogue stages 128 bf16 rows in the K ring");
+    static_assert(8 * kNumBars + 8 <= 128, "barrier area");
+    static_assert(MINB * kThreads <= 2048, "threads per SM");
+};
+using CfgWide = Cfg<128, 3, 4, 1>;
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -157,34 +185,27 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
 }
-// named barriers: 1 = the softmax threads, 2 + q = the kParts warps of TMEM lane quarter q
-__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory"); }
+// named barriers: 1 = the softmax threads, 2 + q = the PARTS warps of TMEM lane quarter q
+template <int PARTS>
+__device__ __forceinline__ void softmax_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(128 * PARTS) : "memory");
+}
+template <int PARTS>
 __device__ __forceinline__ void quarter_sync(int quarter) {
-    asm volatile("bar.sync %0, %1;" ::"r"(2 + quarter), "n"(32 * kParts) : "memory");
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + quarter), "n"(32 * PARTS) : "memory");
 }
 // the same barrier, returning the AND of v over the quarter's threads (so its warps leave a loop together)
+template <int PARTS>
 __device__ __forceinline__ bool quarter_sync_and(int quarter, bool v) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred pi, po;\n\tsetp.ne.b32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
         "selp.u32 %0, 1, 0, po;\n\t}"
         : "=r"(r)
-        : "r"((uint32_t)v), "r"(2 + quarter), "n"(32 * kParts)
+        : "r"((uint32_t)v), "r"(2 + quarter), "n"(32 * PARTS)
         : "memory");
     return r != 0u;
 }
-
-
-// barrier slots
-enum {
-    kBarQ = 0,
-    kBarKVFull = 1,                      // + stage
-    kBarKVEmpty = kBarKVFull + kStages,  // + stage
-    kBarSFull = kBarKVEmpty + kStages,   // + buffer
-    kBarPFull = kBarSFull + 2,           // + buffer (P written into S[b]; also frees S[b] for tile + 2)
-    kBarPV = kBarPFull + 2,              // + buffer: P V of tile j completes kBarPV + j % 2
-    kNumBars = kBarPV + 2
-};
 
 // The request whose prefix is the z-th longest (ties by request index), so that the longest requests' CTAs are
 // launched first and the shortest fill the tail.  Every warp computes it (lane j ranks requests j, j + 32, ...);
@@ -210,9 +231,18 @@ __device__ __forceinline__ int request_by_length_rank(const int32_t* prefix, int
     return found;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const Params p) {
+    constexpr int kKt = C::kKt, kStages = C::kStages, kParts = C::kParts, kOCols = C::kOCols;
+    constexpr int kSoftmaxThreads = C::kSoftmaxThreads, kTmemCols = C::kTmemCols, kSCol = C::kSCol;
+    constexpr int kQBytes = C::kQBytes, kKVBytes = C::kKVBytes;
+    constexpr int kOffQ = C::kOffQ, kOffK = C::kOffK, kOffV = C::kOffV, kOffX = C::kOffX, kOffBar = C::kOffBar;
+    constexpr int kSmemSlack = C::kSmemSlack, kNumBars = C::kNumBars;
+    constexpr int kBarQ = C::kBarQ, kBarKVFull = C::kBarKVFull, kBarKVEmpty = C::kBarKVEmpty;
+    constexpr int kBarSFull = C::kBarSFull, kBarPFull = C::kBarPFull, kBarPV = C::kBarPV;
+    constexpr int kKeyGroups = kKt / 32;  // the paged gather's 32-key groups per tile
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
     if (pad > (uint32_t)kSmemSlack) {  // (uniform: before any barrier, copy or TMEM use)
@@ -278,11 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // takes key 32 t + 4 j + (l >> 3), granule l & 7.
     // slot ids of the next tile's keys key0 + lane + 32 t (context keys only), loaded one tile ahead so that the
     // req_to_token read is off the chain of the tile being issued
-    int32_t next_slot[4];
+    int32_t next_slot[kKeyGroups];
     auto fetch_slots = [&](int i) {
         const int key0 = k_lo + i * kKt;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kKeyGroups; ++t) {
             const int r = key0 + lane + 32 * t;
             next_slot[t] = (i < ntiles && r < prefix) ? __ldg(r2t_row + r) : 0;
         }
@@ -290,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto load_kv_paged = [&](int i) {
         const int st = i % kStages;
         const int key0 = k_lo + i * kKt;
-        int64_t roff[4];  // element offsets of keys key0 + lane + 32 t (row start of this KV head)
-        bool rcache[4];
+        int64_t roff[kKeyGroups];  // element offsets of keys key0 + lane + 32 t (row start of this KV head)
+        bool rcache[kKeyGroups];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kKeyGroups; ++t) {
             const int r = key0 + lane + 32 * t;
             rcache[t] = r < prefix;
             roff[t] = rcache[t] ? (int64_t)min(max(next_slot[t], 0), (int)(p.slots - 1)) * p.skc_t + hk * D
@@ -302,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fetch_slots(i + 1);
         const int c = lane & 7;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kKeyGroups; ++t) {
 #pragma unroll 2
             for (int j = 0; j < 8; ++j) {
                 const int src = 4 * j + (lane >> 3);  // the lane holding this instruction's key
@@ -357,19 +387,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------------------------------------------------------- TMA producer
         if (p.paged) {
             // tile i's copies are issued, then tile i - 1 is published (two tiles' copies in flight); a stage is
-            // refilled only after the MMA released it
+            // refilled only after the MMA released it.  The release of stage i % kStages (the P V of tile
+            // i - kStages) follows the scores of tile i - kStages + 1, so that tile must be published before the
+            // wait: with a 2-stage ring that is tile i - 1, published as soon as its copies land.
             fetch_slots(0);
+            int pub = 0;  // tiles published
             for (int i = 0; i < ntiles; ++i) {
                 if (i >= kStages) {
+                    if (pub < i - kStages + 2) {
+                        publish_paged(i - 1, true);
+                        pub = i;
+                    }
                     bool w = true;
                     if (lane == 0) w = mbar_wait(&bars[kBarKVEmpty + i % kStages], ((i / kStages) - 1) & 1, kTries);
                     ok &= __shfl_sync(MFD_FULL_MASK, (int)w, 0) != 0;
                     if (!ok) break;
                 }
                 load_kv_paged(i);
-                if (i >= 1) publish_paged(i - 1, false);
+                if (i >= 1 && pub < i) {
+                    publish_paged(i - 1, false);
+                    pub = i;
+                }
             }
-            if (ok && ntiles > 0) publish_paged(ntiles - 1, true);
+            if (ok && pub < ntiles) publish_paged(ntiles - 1, true);
             asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing in flight when the warp leaves
         } else if (lane == 0) {
             for (int i = kStages; i < ntiles && ok; ++i) {
@@ -428,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t* anc_row = p.anc + ((size_t)(p.paged ? 0 : b) * p.n + node) * p.words;  // paged: shared
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [kParts][128 rows]
-        const int c_lo = part * 32;  // this warp's 32 of the tile's 128 key columns
+        const int c_lo = part * 32;      // this warp's 32 of the tile's kKt key columns
+        const int o_lo = part * kOCols;  // and its kOCols of O's 128 columns
         const float sc = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
         // a quarter whose 32 rows are all padding keeps only the barrier protocol: it leaves its TMEM rows as they
@@ -491,7 +532,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the row's max over the parts (every part has finished reading S[bi] after this barrier, so P may
             // overwrite it)
             xmax[part * kM + rt] = mx;
-            quarter_sync(quarter);
+            quarter_sync<kParts>(quarter);
 #pragma unroll
             for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[q * kM + rt]);
             float alpha = 1.f;
@@ -517,18 +558,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
             if (__any_sync(MFD_FULL_MASK, rescale)) {  // O must hold the P V of tile i-1; this part rescales O
-                                                       // columns [32 part, +32)
+                                                       // columns [o_lo, o_lo + kOCols)
                 if (i >= 1) {
                     ok &= mbar_wait(&bars[kBarPV + (bi ^ 1)], ((i - 1) >> 1) & 1, kTries);
                     tc_fence_after();
                 }
-                float o[32];
-                tmem_ld32(tmem + lane_off + c_lo, o);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] *= alpha;
-                tmem_st32(tmem + lane_off + c_lo, o);
+                for (int oc = 0; oc < kOCols; oc += 32) {
+                    float o[32];
+                    tmem_ld32(tmem + lane_off + o_lo + oc, o);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] *= alpha;
+                    tmem_st32(tmem + lane_off + o_lo + oc, o);
+                }
             }
-            // P(i) as bf16 pairs over the first 64 columns of S[bi]: this part's 32 keys = 16 columns
+            // P(i) as bf16 pairs over the first kKt / 2 columns of S[bi]: this part's 32 keys = 16 columns
             tmem_st16u(s_tm + part * 16, pk);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
@@ -536,29 +580,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
             // the next tile's maxima may be written only after every part has read these; a failed wait anywhere
             // in the quarter ends the loop for all its warps
-            ok = quarter_sync_and(quarter, ok);
+            ok = quarter_sync_and<kParts>(quarter, ok);
             if (!ok) break;
         }
         if (ntiles > 0 && ok) {  // the last P V (every earlier one completed before it)
             ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
             tc_fence_after();
         }
-        // ---- epilogue: the row sum over the parts, then this part's 32 columns of O / l
-        quarter_sync(quarter);  // every part is past its last use of xmax
+        // ---- epilogue: the row sum over the parts, then this part's kOCols columns of O / l
+        quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
         xmax[part * kM + rt] = l_run;
-        quarter_sync(quarter);
+        quarter_sync<kParts>(quarter);
         float l_row = 0.f;
 #pragma unroll
         for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
         const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
         const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
-        // staging of bf16 rows for coalesced stores: K stage 0 is free once the last P V completed
+        // staging of bf16 rows for coalesced stores: the K ring is free once the last P V completed
         unsigned char* stage = smem + kOffK;  // [128 rows][256 B]
-        {
+#pragma unroll
+        for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {
             float o[32];
             if (ntiles > 0 && quarter_live) {
-                tmem_ld32(tmem + lane_off + c_lo, o);
+                tmem_ld32(tmem + lane_off + oc, o);
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) o[j] = 0.f;
@@ -566,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.splits == 1) {
 #pragma unroll
                 for (int j = 0; j < 32; j += 8)
-                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c_lo + j) * 2) =
+                    *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + j) * 2) =
                         make_uint4(pack_bf16(o[j] * inv, o[j + 1] * inv), pack_bf16(o[j + 2] * inv, o[j + 3] * inv),
                                    pack_bf16(o[j + 4] * inv, o[j + 5] * inv), pack_bf16(o[j + 6] * inv, o[j + 7] * inv));
             } else {
@@ -574,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4* dst = reinterpret_cast<float4*>(p.o_part) + ((size_t)split * units + unit) * (32 * kM);
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
-                    dst[((c_lo + j) >> 2) * kM + rt] =
+                    dst[((oc + j) >> 2) * kM + rt] =
                         make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
             }
         }
@@ -583,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 p.lse_part[((size_t)split * units + unit) * kM + rt] = l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
             // the last split of this (request, KV head, M-tile) merges all of them
             __threadfence();
-            softmax_sync();
+            softmax_sync<kParts>();
             if (threadIdx.x == 64) {
                 unsigned int* tk = p.tickets + unit;
                 const unsigned int t = atomicAdd(tk, 1u);
@@ -591,56 +636,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (last) *tk = 0u;  // ready for the next launch
                 *shared_flag = last;
             }
-            softmax_sync();
+            softmax_sync<kParts>();
             if (*shared_flag) {
                 __threadfence();
                 const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
                 float m = -INFINITY;
                 for (int sp = 0; sp < p.splits; ++sp) m = fmaxf(m, __ldcg(lse + (size_t)sp * units * kM));
-                float acc[8][4];
+#pragma unroll 1
+                for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {  // 32 columns (8 float4 chunks) at a time
+                    float acc[8][4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-                float wsum = 0.f;
-                if (m != -INFINITY) {
-                    // two splits' loads in flight at a time
-                    for (int sp = 0; sp < p.splits; sp += 2) {
-                        float4 v[2][8];
-                        float w[2];
+                    for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+                    float wsum = 0.f;
+                    if (m != -INFINITY) {
+                        // two splits' loads in flight at a time
+                        for (int sp = 0; sp < p.splits; sp += 2) {
+                            float4 v[2][8];
+                            float w[2];
 #pragma unroll
-                        for (int t = 0; t < 2; ++t) {
-                            const int sq = sp + t < p.splits ? sp + t : sp;
-                            const float l = __ldcg(lse + (size_t)sq * units * kM);
-                            w[t] = (sp + t < p.splits && l != -INFINITY) ? fast_exp2(l - m) : 0.f;
-                            const float4* src =
-                                reinterpret_cast<const float4*>(p.o_part) + ((size_t)sq * units + unit) * (32 * kM);
+                            for (int t = 0; t < 2; ++t) {
+                                const int sq = sp + t < p.splits ? sp + t : sp;
+                                const float l = __ldcg(lse + (size_t)sq * units * kM);
+                                w[t] = (sp + t < p.splits && l != -INFINITY) ? fast_exp2(l - m) : 0.f;
+                                const float4* src = reinterpret_cast<const float4*>(p.o_part) +
+                                                    ((size_t)sq * units + unit) * (32 * kM);
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) v[t][c] = __ldcg(src + (part * 8 + c) * kM + rt);
-                        }
+                                for (int c = 0; c < 8; ++c) v[t][c] = __ldcg(src + ((oc >> 2) + c) * kM + rt);
+                            }
 #pragma unroll
-                        for (int t = 0; t < 2; ++t) {
-                            if (w[t] == 0.f) continue;  // (a split without visible keys holds zeros)
-                            wsum += w[t];
+                            for (int t = 0; t < 2; ++t) {
+                                if (w[t] == 0.f) continue;  // (a split without visible keys holds zeros)
+                                wsum += w[t];
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) {
-                                acc[c][0] += w[t] * v[t][c].x;
-                                acc[c][1] += w[t] * v[t][c].y;
-                                acc[c][2] += w[t] * v[t][c].z;
-                                acc[c][3] += w[t] * v[t][c].w;
+                                for (int c = 0; c < 8; ++c) {
+                                    acc[c][0] += w[t] * v[t][c].x;
+                                    acc[c][1] += w[t] * v[t][c].y;
+                                    acc[c][2] += w[t] * v[t][c].z;
+                                    acc[c][3] += w[t] * v[t][c].w;
+                                }
                             }
                         }
                     }
-                }
-                const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
+                    const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-                for (int c = 0; c < 8; c += 2)
-                    *reinterpret_cast<uint4*>(stage + rt * 256 + (c_lo + c * 4) * 2) =
-                        make_uint4(pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
-                                   pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
-                                   pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+                    for (int c = 0; c < 8; c += 2)
+                        *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + c * 4) * 2) = make_uint4(
+                            pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
+                            pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
+                            pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+                }
             }
         }
         // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
-        softmax_sync();
+        softmax_sync<kParts>();
         if (p.splits == 1 || *shared_flag) {
             const int ts = threadIdx.x - 64;
             for (int e = ts; e < kM * 16; e += kSoftmaxThreads) {
@@ -690,7 +738,9 @@ static bool make_map(CUtensorMap* m, const void* base, uint64_t d1, uint64_t d2,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int launch(const Shape& sh, const Params& p, cudaStream_t stream) {
+template <class C>
+static int launch_cfg(const Shape& sh, const Params& p, cudaStream_t stream) {
+    const char* who = p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention";
     CUtensorMap tq, tk, tv;
     const uint32_t nodes_per_tile = (uint32_t)(kM / p.G);
     bool okm = make_map(&tq, sh.q, (uint64_t)p.H, (uint64_t)p.n, (uint64_t)p.bs, sh.sq_h, sh.sq_n, sh.sq_b,
@@ -701,24 +751,27 @@ int launch(const Shape& sh, const Params& p, cudaStream_t stream) {
     } else {
         okm = okm &&
               make_map(&tk, sh.k, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sk_s, sh.sk_h, sh.sk_b,
-                       kKt, 1) &&
+                       C::kKt, 1) &&
               make_map(&tv, sh.v, (uint64_t)sh.max_keys, (uint64_t)p.Hkv, (uint64_t)p.bs, sh.sv_s, sh.sv_h, sh.sv_b,
-                       kKt, 1);
+                       C::kKt, 1);
     }
     if (!okm) {
-        set_error("%s: could not encode the TMA tensor maps", p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention");
+        set_error("%s: could not encode the TMA tensor maps", who);
         return MFD_ERR_CUDA;
     }
-    cudaError_t e = cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e =
+        cudaFuncSetAttribute(tree_attn_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (e != cudaSuccess) {
-        set_error("%s: %s", p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention", cudaGetErrorString(e));
+        set_error("%s: %s", who, cudaGetErrorString(e));
         return MFD_ERR_CUDA;
     }
     dim3 grid((unsigned)(p.splits * p.mtiles), (unsigned)p.Hkv, (unsigned)p.bs);
-    tree_attn_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, p);
-    MFD_CHECK_LAUNCH(p.paged ? "mfd_paged_mode_attention" : "mfd_tree_attention");
+    tree_attn_tc_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, p);
+    MFD_CHECK_LAUNCH(who);
     return MFD_OK;
 }
+
+int launch(const Shape& sh, const Params& p, cudaStream_t stream) { return launch_cfg<CfgWide>(sh, p, stream); }
 
 }  // namespace tca
 }  // namespace mfd
