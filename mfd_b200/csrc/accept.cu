@@ -80,9 +80,11 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 }
 __device__ __forceinline__ uint64_t dup2(float a) { return pk2(a, a); }
 // exp32_rule((x0 - m) * c) and exp32_rule((x1 - m) * c), the operations of exp32_rule on both lanes at once (a lane
-// whose argument is not above -87 is computed on and then replaced by 0, as exp32_rule returns)
+// whose argument is not above -87 is computed on and then replaced by 0, as exp32_rule returns).  UNIT: c is 1, so
+// the product is the difference itself (multiplying by 1 is exact) and is not computed.
+template <bool UNIT>
 __device__ __forceinline__ void exp32_rule_x2(uint64_t x01, uint64_t m2, uint64_t c2, float& e0, float& e1) {
-    const uint64_t y = mul2(sub2(x01, m2), c2);
+    const uint64_t y = UNIT ? sub2(x01, m2) : mul2(sub2(x01, m2), c2);
     const uint64_t t = add2(mul2(y, dup2(1.44269504088896341f)), dup2(12582912.0f));
     const uint64_t n = sub2(t, dup2(12582912.0f));
     uint64_t r = fma2(n, dup2(-0.693359375f), y);
@@ -371,6 +373,7 @@ __device__ __forceinline__ double shfl_f64(double v, int src) {
 // warp shuffles, the lane sums of the weights against it, and their butterfly sum; lane 0 keeps (M_b, S_b) in
 // shared memory.  Warp 0 then forms the block weights, the run sums and Z in the rule's order and locates the
 // target run -> block -> lane -> logit (re-reading one block of 256 logits).
+template <bool UNIT_T>  // temperature exactly 1 (then 1 / T is exactly 1)
 __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kernel(Params p) {
     __shared__ float blk_m[kMaxRounds * kSampleWarps];
     __shared__ float blk_s[kMaxRounds * kSampleWarps];
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {  // logits 2q, 2q + 1: the low and high bf16 of word q
                     float e0, e1;
-                    exp32_rule_x2(pk2(bf16lo(ws[q]), bf16hi(ws[q])), m2, c2, e0, e1);
+                    exp32_rule_x2<UNIT_T>(pk2(bf16lo(ws[q]), bf16hi(ws[q])), m2, c2, e0, e1);
                     sum = __fadd_rn(sum, e0);
                     sum = __fadd_rn(sum, e1);
                 }
@@ -591,7 +594,10 @@ static int launch_accept(accept::Params& p, int64_t rows, void* scratch, unsigne
         accept::greedy_kernel<<<(unsigned)(rows * p.parts), accept::kGreedyThreads, 0, stream>>>(p);
     } else {
         p.parts = 1;
-        accept::sample_kernel<<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
+        if (p.temperature == 1.0f)
+            accept::sample_kernel<true><<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
+        else
+            accept::sample_kernel<false><<<(unsigned)rows, accept::kSampleThreads, 0, stream>>>(p);
     }
     MFD_CHECK_LAUNCH(fn);
     return MFD_OK;
