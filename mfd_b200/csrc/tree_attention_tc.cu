@@ -641,7 +641,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 __threadfence();
                 const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
                 float m = -INFINITY;
-                for (int sp = 0; sp < p.splits; ++sp) m = fmaxf(m, __ldcg(lse + (size_t)sp * units * kM));
+                for (int sp0 = 0; sp0 < p.splits; sp0 += 8) {  // eight splits' values per L2 round trip
+                    float l[8];
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        l[t] = sp0 + t < p.splits ? __ldcg(lse + (size_t)(sp0 + t) * units * kM) : -INFINITY;
+#pragma unroll
+                    for (int t = 0; t < 8; ++t) m = fmaxf(m, l[t]);
+                }
 #pragma unroll 1
                 for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {  // 32 columns (8 float4 chunks) at a time
                     float acc[8][4];
