@@ -289,8 +289,10 @@ constexpr int kGreedyThreads = 256;
 
 // greedy: CTA (row, part) reduces its part; the last part of a row reduces the parts; the last row of a
 // request walks the tree
+constexpr int kGreedyFlatKeys = 1024;  // part keys of one request staged by the one-ticket path
 __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     __shared__ uint64_t red[kGreedyThreads / 32];
+    __shared__ uint64_t flat_keys[kGreedyFlatKeys];
     __shared__ int flag;
     __shared__ WalkStage stage;
     const int64_t row = blockIdx.x / p.parts;
@@ -302,6 +304,35 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     chunk = (chunk + 7) / 8 * 8;
     const int64_t c0 = min(V, (int64_t)part * chunk), c1 = min(V, c0 + chunk);
     const uint64_t best = block_reduce_max_u64<kGreedyThreads>(argmax_share<kGreedyThreads>(x, c0, c1), red);
+    if (p.walk && p.parts > 1 && p.width * p.parts <= kGreedyFlatKeys) {
+        // one ticket per request over all its rows' parts: the last CTA takes every row's maximum over its parts
+        // (all keys staged in shared memory in one round of loads), writes the posterior and walks
+        if (threadIdx.x == 0) {
+            p.part_keys[row * p.parts + part] = best;
+            __threadfence();
+            const unsigned int t = atomicAdd(p.tickets + b, 1u);
+            flag = (t == (unsigned int)(p.width * p.parts - 1));
+        }
+        __syncthreads();
+        if (!flag) return;
+        __threadfence();
+        const int nkeys = (int)(p.width * p.parts);
+        const uint64_t* keys = p.part_keys + b * p.width * p.parts;
+        for (int e = threadIdx.x; e < nkeys; e += kGreedyThreads) flat_keys[e] = __ldcg(keys + e);
+        __syncthreads();
+        for (int r = threadIdx.x; r < (int)p.width; r += kGreedyThreads) {
+            uint64_t k = 0;
+            for (int i = 0; i < p.parts; ++i) {
+                const uint64_t v = flat_keys[r * p.parts + i];
+                k = v > k ? v : k;
+            }
+            p.posterior[b * p.width + r] = (int64_t)key_index(k);
+        }
+        __syncthreads();  // the posterior rows are visible to the walking warp
+        if (threadIdx.x < 32) walk_request(p, b, &stage);
+        if (threadIdx.x == 0) p.tickets[b] = 0u;
+        return;
+    }
     if (p.parts > 1) {
         if (threadIdx.x == 0) {
             p.part_keys[row * p.parts + part] = best;
