@@ -1,6 +1,6 @@
 """Verify-step benchmark (tree build + tree verify attention + acceptance), B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests-per-gpu R]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests R]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
     python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
     python bench.py --kernel K                             (one kernel alone, L2 flushed between launches: a kernel
@@ -9,20 +9,22 @@
                                                             or the paged drafter attention, paged_mode_attn)
 
 Workload (synthetic, seeded per global request id so any partition computes the same
-requests): 32 requests per GPU per step (32/64/128/256 requests at 1/2/4/8 GPUs), each with drafter logits
-float32 [K=8, L=16, V=151936] (N(0,1), 4 ids per (mode, position) boosted by U(4,10)), an exact mixture tree of
-B=64 nodes, tree-masked GQA verify attention (32/8 heads, head_dim 128, prefix U(1024, 8192)), and stochastic
-acceptance at T=1 over target logits bf16 [65, V] N(0, 1.5) with seeded uniforms.  Requests are partitioned
-across ranks (sorted by prefix, dealt round-robin); there is no collective on the data path (only the timing
-max-reduce), so scaling is weak: the work per GPU is fixed.  Inputs (~3.8 GB per GPU) are far larger than L2.
+requests): 256 requests per step, partitioned 256/128/64/32 per GPU at 1/2/4/8 GPUs (strong scaling: the job is
+fixed, the GPUs share it).  Each request has drafter logits float32 [K=8, L=16, V=151936] (N(0,1), 4 ids per
+(mode, position) boosted by U(4,10)), an exact mixture tree of B=64 nodes, tree-masked GQA verify attention (32/8
+heads, head_dim 128, prefix U(1024, 8192)), and stochastic acceptance at T=1 over target logits bf16 [65, V]
+N(0, 1.5) with seeded uniforms.  Requests are partitioned across ranks (sorted by prefix, dealt round-robin); there
+is no collective on the data path (only the timing max-reduce).  Inputs (~117 MB per request, 30 GB per step at
+one GPU) are far larger than L2.
 
 Printed by rank 0: one JSON line (metric trees/s, whole job), with
-  north_star: BASELINE's headline verify step -- batch 1, greedy, prefix 4096, configs 0 + 1 + acceptance --
-              in microseconds per step (L2 flushed between steps), rank 0 only;
-  roofline:   the dominant kernel (the fused logits step) against the measured HBM copy bandwidth;
-  e2e:        the same metric through the public API with inputs copied from pinned host memory each step;
-  cpu_baseline: the reference's CPU path (its compiled C++ builder, torch's CPU top-k / logsumexp / SDPA /
-              softmax sampling, its walk) on a bounded sample, rank 0 at N=1.
+  north_star:    BASELINE's headline verify step -- batch 1, greedy, prefix 4096, configs 0 + 1 + acceptance --
+                 in microseconds per step (L2 flushed between steps), rank 0 only;
+  roofline:      the dominant kernel (the fused logits step) against the measured HBM copy bandwidth;
+  step_roofline: the whole step's algorithmic bytes against the same peak;
+  e2e:           the same metric through the public API with inputs copied from pinned host memory each step;
+  cpu_baseline:  the reference's CPU path (its compiled C++ builder, torch's CPU top-k / logsumexp / SDPA /
+                 softmax sampling, its walk) on a bounded sample, compute only, rank 0 at N=1.
 """
 
 from __future__ import annotations
@@ -43,7 +45,8 @@ sys.path.insert(0, ROOT)
 K_MODES, L_BLOCK, VOCAB, BUDGET = 8, 16, 151936, 64
 W = BUDGET + 1
 H, HKV, D = 32, 8, 128
-REQUESTS_PER_GPU = 32
+TOTAL_REQUESTS = 256     # 256 requests, partitioned 256/128/64/32 per GPU at 1/2/4/8 GPUs
+REQUESTS_PER_GPU = 32    # the --kernel / --config profiling cases
 # Logits-step DRAM traffic per row (read + write) from an ncu capture of 1024 rows x 151936 fp32, k = 64
 # (bench.py --kernel logits_step --requests-per-gpu 8): 626.81 MB read + 10.39 MB written.  Traffic grows with the
 # rows, so a launch of R rows moves R times this.
@@ -94,6 +97,15 @@ def max_over_ranks(ws, value: float) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(ws, value: float) -> float:
+    if ws == 1:
+        return value
+    dev = "cuda" if torch.distributed.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+    return float(t.item())
+
+
 def prefix_lengths(total: int, seed: int = 4321):
     """Prefix length of every request id: U(1024, 8192), the same for a request whatever the job size."""
     g = torch.Generator().manual_seed(seed)
@@ -113,6 +125,51 @@ def gen_draft_logits(req: int, dev, out: torch.Tensor):
     ids = torch.randint(0, VOCAB, (K_MODES, L_BLOCK, 4), generator=g, device=dev)
     boost = torch.rand(K_MODES, L_BLOCK, 4, generator=g, device=dev) * 6 + 4
     out.scatter_add_(2, ids, boost)
+
+
+def sharp_draft_logits(seed: int, dev, out: torch.Tensor, share: float = 0.75):
+    """configs[3]'s drafter logits [K, L, V] float32: N(0,1) plus, per (mode, position), one token boosted by
+    U(12, 16) -- the position's consensus token for a mode with probability `share`, else a token of the mode's
+    own.  The modes then share a deep chain and branch off it, so a B=64 mixture tree reaches depth 9 and more
+    (the config-0 generator's trees are about 3 deep)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out.normal_(generator=g)
+    consensus = torch.randint(0, VOCAB, (1, L_BLOCK, 1), generator=g, device=dev).expand(K_MODES, L_BLOCK, 1)
+    own = torch.randint(0, VOCAB, (K_MODES, L_BLOCK, 1), generator=g, device=dev)
+    pick = torch.rand(K_MODES, L_BLOCK, 1, generator=g, device=dev) < share
+    ids = torch.where(pick, consensus, own)
+    out.scatter_add_(2, ids, torch.rand(K_MODES, L_BLOCK, 1, generator=g, device=dev) * 4 + 12)
+
+
+def forced_path(tokens, parents, depths, depth: int, seed: int):
+    """A seeded random root-to-node path of `depth` edges in one tree (tokens/parents/depths: host sequences of the
+    W verify rows, node 0 the root; depths[0] = 0).  Picks uniformly among the nodes at that depth, preferring
+    leaves; returns the node ids root..end, or the deepest available path when the tree is shallower."""
+    n = len(parents)
+    has_child = [False] * n
+    for i in range(1, n):
+        if parents[i] >= 0:
+            has_child[parents[i]] = True
+    real = [i for i in range(n) if i == 0 or parents[i] >= 0]
+    depth = min(depth, max(depths[i] for i in real))
+    at = [i for i in real if depths[i] == depth]
+    leaves = [i for i in at if not has_child[i]]
+    pool = leaves or at
+    g = torch.Generator().manual_seed(seed)
+    end = pool[int(torch.randint(0, len(pool), (1,), generator=g))]
+    path = [end]
+    while path[-1] != 0:
+        path.append(parents[path[-1]])
+    return path[::-1]
+
+
+def force_argmax(target: torch.Tensor, tokens, path):
+    """target [W, V] logits: along the path, each node's row gets its argmax forced onto the next path node's token
+    (value = the row's maximum + 1), so the greedy walk accepts exactly the path (the last node's row keeps its own
+    argmax, the bonus token)."""
+    for a, b in zip(path[:-1], path[1:]):
+        row = target[a]
+        row[int(tokens[b])] = row.float().max() + 1.0
 
 
 class Batch:
@@ -135,8 +192,11 @@ class Batch:
             gen_draft_logits(r, dev, self.draft[i])
             g = torch.Generator(device=dev).manual_seed(7_000_001 * (r + 1))
             self.q[i].copy_(torch.randn(W, H, D, generator=g, device=dev))
-            self.k[i].copy_(torch.randn(HKV, smax, D, generator=g, device=dev) * 0.5)
-            self.v[i].copy_(torch.randn(HKV, smax, D, generator=g, device=dev) * 0.5)
+            # each request's keys are drawn at its own length (prefix + tree), so its values do not depend on the
+            # other requests of the batch (the padding beyond prefix + W is never read)
+            p = self.prefix[i]
+            self.k[i, :, :p + W].copy_(torch.randn(HKV, p + W, D, generator=g, device=dev) * 0.5)
+            self.v[i, :, :p + W].copy_(torch.randn(HKV, p + W, D, generator=g, device=dev) * 0.5)
             self.target[i].copy_(torch.randn(W, VOCAB, generator=g, device=dev) * target_std)
             self.u[i].copy_(torch.rand(W, generator=g, device=dev, dtype=torch.float64))
         self.prefix_t = torch.tensor(self.prefix, dtype=torch.int32, device=dev)
@@ -152,6 +212,13 @@ class Batch:
     def input_bytes(self):
         kv = sum(2 * HKV * (p + W) * D * 2 for p in self.prefix)
         return self.draft.numel() * 4 + self.q.numel() * 2 + kv + self.target.numel() * 2 + self.u.numel() * 8
+
+    def step_bytes(self):
+        """Algorithmic bytes of one step: the inputs read once, the logits-step results (top log-probs, ids, log Z)
+        written once and read back by the tree build, the trees, the attention output and the accept outputs."""
+        cand = self.top.numel() * 4 + self.ids.numel() * 4 + self.logz.numel() * 4
+        return (self.input_bytes() + 2 * cand + self.tree.numel() * 8 + self.attn_out.numel() * 2
+                + self.bs * (W * 8 + 3 * L_BLOCK * 8 + 32))
 
 
 # ------------------------------------------------------------------------------------------------ the step
@@ -318,38 +385,86 @@ def north_star(dev, steps: int, warmup: int, graph: bool = True):
     }
 
 
-def e2e(dev, reqs, prefixes, steps: int, ws: int, chunk: int = 8):
-    """The public API end to end on every rank: each step copies its requests' inputs from pinned host memory to
-    the device, runs the verify step, and reads the accepted lengths / tokens and the trees back.  Timed on the
-    device (CUDA events), max over ranks; value = requests of all ranks per second."""
-    sample = reqs[:chunk]
-    batch = Batch(sample, prefixes, dev)
-    host = {name: getattr(batch, name).cpu().pin_memory() for name in ("draft", "q", "k", "v", "target", "u")}
-    host["prefix_t"] = batch.prefix_t.cpu().pin_memory()
-    step = Step(batch)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    out_bytes = 0
+def h2d_link_gbs(dev, nbytes: int = 1 << 30, reps: int = 5) -> float:
+    """Pinned host -> device copy bandwidth of this GPU's link (best of `reps` copies of 1 GiB, CUDA events)."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dst.copy_(src, non_blocking=True)
+    best = float("inf")
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        dst.copy_(src, non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del src, dst
+    return nbytes / (best * 1e-3) / 1e9
+
+
+E2E_FIELDS = ("draft", "q", "k", "v", "target", "u", "prefix_t")
+
+
+def e2e(dev, reqs, prefixes, steps: int, ws: int, sample: int = 16, chunk: int = 4):
+    """The public API end to end on every rank, over a sample of its requests: each step copies those requests'
+    inputs from pinned host memory to the device (a copy stream, `chunk` requests at a time, so the copy of one
+    chunk overlaps the verify step of the previous one), runs the verify step per chunk, and reads the accepted
+    lengths, accepted tokens and trees back into pinned host memory.  Timed on the device (CUDA events), max over
+    ranks; value = requests of all ranks per second.  The copies dominate: the drafter logits alone are 77.8 MB
+    per request, so the line also reports the H2D rate against this link's measured pinned-copy bandwidth."""
+    sample_reqs = reqs[:sample]
+    groups = [sample_reqs[i:i + chunk] for i in range(0, len(sample_reqs), chunk)]
+    batches = [Batch(g, prefixes, dev) for g in groups]
+    hosts = [{name: getattr(b, name).cpu().pin_memory() for name in E2E_FIELDS} for b in batches]
+    steps_ = [Step(b) for b in batches]
+    outs = [(torch.empty(b.bs, dtype=torch.int32).pin_memory(), torch.empty(b.bs, L_BLOCK, dtype=torch.int64).pin_memory(),
+             torch.empty_like(b.tree, device="cpu").pin_memory()) for b in batches]
+    h2d = sum(t.numel() * t.element_size() for h in hosts for t in h.values())
+    d2h = sum(t.numel() * t.element_size() for o in outs for t in o)
+    cur = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    done = [torch.cuda.Event() for _ in batches]
+    ready = [torch.cuda.Event() for _ in batches]
+    for ev in done:
+        ev.record(cur)
 
     def one():
-        nonlocal out_bytes
-        for name, t in host.items():
-            getattr(batch, name).copy_(t, non_blocking=True)
-        o = step.run()
-        res = (o["accept_len"].cpu(), o["out_tokens"].cpu(), batch.tree.cpu())
-        out_bytes = sum(r.numel() * r.element_size() for r in res)
-        return res
+        for j, (b, h, st, o) in enumerate(zip(batches, hosts, steps_, outs)):
+            with torch.cuda.stream(copy):
+                copy.wait_event(done[j])  # this chunk's buffers are free once its previous step has read them
+                for name, t in h.items():
+                    getattr(b, name).copy_(t, non_blocking=True)
+                ready[j].record(copy)
+            cur.wait_event(ready[j])
+            r = st.run()
+            o[0].copy_(r["accept_len"], non_blocking=True)
+            o[1].copy_(r["out_tokens"], non_blocking=True)
+            o[2].copy_(b.tree, non_blocking=True)
+            done[j].record(cur)
 
     one()
+    torch.cuda.synchronize()
     barrier(ws)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
+    s.record(cur)
+    copy.wait_event(s)
     for _ in range(steps):
         one()
-    e.record()
+    e.record(cur)
     torch.cuda.synchronize()
     ms = max_over_ranks(ws, s.elapsed_time(e) / steps)
-    return {"value": round(len(sample) * ws / (ms / 1e3), 3), "unit": "trees/s", "h2d_bytes_per_step": h2d * ws,
-            "d2h_bytes_per_step": out_bytes * ws, "requests_per_step": len(sample) * ws, "ms_per_step": round(ms, 3)}
+    assert all(int(o[0].min()) >= 0 for o in outs)  # the results were read back
+    link = h2d_link_gbs(dev)
+    rate = h2d / (ms * 1e-3) / 1e9
+    del batches, steps_, hosts
+    return {"value": round(len(sample_reqs) * ws / (ms / 1e3), 3), "unit": "trees/s",
+            "h2d_bytes_per_step": h2d * ws, "d2h_bytes_per_step": d2h * ws,
+            "requests_per_step": len(sample_reqs) * ws, "ms_per_step": round(ms, 3),
+            "h2d_gbs_per_gpu": round(rate, 1), "h2d_link_gbs_measured": round(link, 1),
+            "h2d_frac_of_link": round(rate / link, 4),
+            "bound": "host-to-device copies (PCIe): the step's inputs cross the link once per step",
+            "how": f"{len(sample_reqs)} requests per GPU from pinned host memory in chunks of {chunk}, copy stream "
+                   "overlapped with the previous chunk's verify step; results read back to pinned memory"}
 
 
 def commit_line(name: str, steps: int, warmup: int, requests: int):
@@ -377,7 +492,8 @@ def commit_line(name: str, steps: int, warmup: int, requests: int):
                 src[b, i], tgt[b, i] = base + 10 + 2 * i + 1, base + 10 + i  # node slot -> position slot
         src, tgt = src.to(dev), tgt.to(dev)
         ptrs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device=dev)
-        us = timed_us(lambda: ops.commit_kv_moves(ptrs, slot, src, tgt), steps, warmup, flush)
+        us = timed_us(lambda: ops.commit_kv_moves(ptrs, slot, src, tgt, base_align=16, pool_slots=slots), steps, warmup,
+                     flush)
         alg = requests * moves * nbuf * slot * 2
         work = f"{requests} requests x {moves} moves x {nbuf} buffers x {slot} B slots"
     else:
@@ -487,17 +603,24 @@ def paged_line(steps: int, warmup: int, requests: int):
 
 # ------------------------------------------------------------------------------------------------ CPU reference
 
-def cpu_reference_request(req: int, prefix: int, temperature: float, ext):
-    """The reference's CPU path for one request: float32 top-k + logsumexp (hf/ddtree.py:240-245), its C++ mixture
-    builder (tree_build_ext.build_mixture), the compile_ddtree_tree mask + float32 SDPA with GQA repeat, the
-    `sample` rule (argmax / softmax + multinomial, hf/model/utils.py:28-35) and its C++ walk."""
+def cpu_reference_inputs(req: int, prefix: int):
+    """One request's host inputs for the reference's CPU path (generated outside any timed region)."""
     g = torch.Generator().manual_seed(1_000_003 * (req + 1))
     x = torch.randn(K_MODES, L_BLOCK, VOCAB, generator=g)
     ids = torch.randint(0, VOCAB, (K_MODES, L_BLOCK, 4), generator=g)
     x.scatter_add_(2, ids, torch.rand(K_MODES, L_BLOCK, 4, generator=g) * 6 + 4)
-    q = torch.randn(1, H, W, D).to(torch.bfloat16)
-    kv = (torch.randn(2, 1, HKV, prefix + W, D) * 0.5).to(torch.bfloat16)
-    target = (torch.randn(1, W, VOCAB) * 1.5).to(torch.bfloat16)
+    q = torch.randn(1, H, W, D, generator=g).to(torch.bfloat16)
+    kv = (torch.randn(2, 1, HKV, prefix + W, D, generator=g) * 0.5).to(torch.bfloat16)
+    target = (torch.randn(1, W, VOCAB, generator=g) * 1.5).to(torch.bfloat16)
+    return x, q, kv, target, prefix
+
+
+def cpu_reference_request(inputs, temperature: float, ext) -> float:
+    """The reference's CPU path for one request: float32 top-k + logsumexp (hf/ddtree.py:240-245), its C++ mixture
+    builder (tree_build_ext.build_mixture), the compile_ddtree_tree mask + float32 SDPA with GQA repeat, the
+    `sample` rule (argmax / softmax + multinomial, hf/model/utils.py:28-35) and its C++ walk.  Returns the seconds
+    of that compute alone (inputs come from cpu_reference_inputs)."""
+    x, q, kv, target, prefix = inputs
     t0 = time.perf_counter()
     top, tid = torch.topk(x, k=BUDGET, dim=-1)
     lz = torch.logsumexp(x, dim=-1, keepdim=True)
@@ -542,16 +665,29 @@ def reference_ext():
     return None, "port"
 
 
+def cpu_reference_run(reqs, prefixes, temperature: float, ext, warmup: int = 1):
+    """Compute seconds of the reference's CPU path per request over `reqs` (after `warmup` untimed requests); each
+    request's inputs are generated before its timer starts."""
+    for i in range(warmup):
+        cpu_reference_request(cpu_reference_inputs(reqs[i % len(reqs)], prefixes[reqs[i % len(reqs)]]),
+                              temperature, ext)
+    secs = []
+    for r in reqs:
+        inputs = cpu_reference_inputs(r, prefixes[r])
+        secs.append(cpu_reference_request(inputs, temperature, ext))
+    return secs
+
+
 def cpu_baseline(sample_requests: int = 3, temperature: float = 1.0):
     torch.set_num_threads(os.cpu_count() or 1)
     ext, kind = reference_ext()
-    prefixes = prefix_lengths(REQUESTS_PER_GPU)
-    cpu_reference_request(0, 1024, temperature, ext)  # warm-up
-    secs = [cpu_reference_request(r, prefixes[r], temperature, ext) for r in range(sample_requests)]
+    prefixes = prefix_lengths(TOTAL_REQUESTS)
+    secs = cpu_reference_run(list(range(sample_requests)), prefixes, temperature, ext)
     per = statistics.mean(secs)
     return {"value": round(1.0 / per, 4), "unit": "trees/s", "cores": torch.get_num_threads(), "kind": kind,
             "sample": f"{sample_requests} requests of the benchmark workload (prefixes {prefixes[:sample_requests]}), "
-                      f"mean {per * 1e3:.1f} ms per request, host {os.cpu_count()} cpus"}
+                      f"compute only (inputs generated before each timer), mean {per * 1e3:.1f} ms per request, "
+                      f"host {os.cpu_count()} cpus"}
 
 
 # ------------------------------------------------------------------------------------------------ main
@@ -645,22 +781,36 @@ def config_line(config: int, steps: int, warmup: int):
         q = torch.randn(1, H, T, D, generator=g, device=dev).bfloat16()
         k = (torch.randn(1, HKV, ctx + T, D, generator=g, device=dev) * 0.5).bfloat16()
         v = (torch.randn(1, HKV, ctx + T, D, generator=g, device=dev) * 0.5).bfloat16()
-        batch = Batch([0], [4096], dev, temperature=0.0, target_std=1.0, uniform_prefix=64)
-        step = Step(batch)
-        step.run()
         attn_us = timed_us(lambda: mode_block_attention(q, k, v, Km, bsz, D ** -0.5), steps, warmup, flush)
         attn_flops = 4 * T * H * (ctx + bsz) * D
         attn_bytes = 2 * (H * T * D * 2) + 2 * HKV * (ctx + T) * D * 2
         line["mode_attention_us"] = round(attn_us, 2)
         line["mode_attention_tensor_roofline_us"] = round(attn_flops / (pk["bf16_tflops"] * 1e12) * 1e6, 2)
         line["mode_attention_hbm_roofline_us"] = round(attn_bytes / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
+        # the mixture tree of sharp drafter logits, then greedy acceptance over target logits N(0,1) whose argmax
+        # is forced along a seeded root-to-leaf path of depth 9
+        batch = Batch([0], [64], dev, temperature=0.0, target_std=1.0, uniform_prefix=64)
+        sharp_draft_logits(3, dev, batch.draft[0])
+        step = Step(batch)
+        step.run()
+        t = batch.tree[0].cpu().tolist()
+        path = forced_path(t[0], t[2], t[1], 9, seed=3)
+        force_argmax(batch.target[0], t[0], path)
+        o = ops.accept(batch.target, batch.tree[:, 0], batch.tree[:, 2], temperature=0.0, max_steps=L_BLOCK - 1,
+                       out_len=L_BLOCK)
+        line["tree_depth"] = max(t[1][: int(batch.counts[0]) + 1])
+        line["forced_path_depth"] = len(path) - 1
+        line["accept_len"] = int(o["accept_len"][0])
+        line["accepted_tokens_match_path"] = o["accepted"][0, : len(path)].tolist() == path
 
         def fn():
             ops.accept(batch.target, batch.tree[:, 0], batch.tree[:, 2], temperature=0.0, max_steps=L_BLOCK - 1,
                        out_len=L_BLOCK)
         nbytes, flops = W * VOCAB * 2, 0
-        line["workload"] = ("configs[3]: mode attention (128 queries x 32 heads over 4096 context + own 16-key block) "
-                            "then greedy acceptance over target logits bf16 [65, 151936]; 'us' is the acceptance")
+        line["workload"] = ("configs[3]: mode attention (128 queries x 32 heads over 4096 context + own 16-key block), "
+                            "then a B=64 mixture tree of sharp drafter logits and greedy acceptance over target "
+                            "logits bf16 [65, 151936] N(0,1) with the argmax forced along a depth-9 path; 'us' is "
+                            "the acceptance")
     else:
         raise SystemExit(f"--config {config}: not available")
     us = timed_us(fn, steps, warmup, flush)
@@ -682,7 +832,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mfd", choices=["mfd", "reference"])
-    ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU)
+    ap.add_argument("--requests", type=int, default=TOTAL_REQUESTS,
+                    help="requests of the whole job (split over the GPUs: strong scaling)")
+    ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU, help="--kernel lines only")
     ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
     ap.add_argument("--kernel", default=None,
@@ -698,22 +850,24 @@ def main():
             return
         torch.set_num_threads(os.cpu_count() or 1)
         ext, kind = reference_ext()
-        prefixes = prefix_lengths(REQUESTS_PER_GPU)
-        for i in range(args.warmup):
-            cpu_reference_request(i, prefixes[i], 1.0, ext)
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            cpu_reference_request(i % REQUESTS_PER_GPU, prefixes[i % REQUESTS_PER_GPU], 1.0, ext)
-        secs = (time.perf_counter() - t0) / args.steps
+        prefixes = prefix_lengths(args.requests)
+        # one request of the workload per step, in request-id order; each request's inputs are generated before
+        # its timer starts, so the sum below is the reference's compute alone
+        reqs = [i % args.requests for i in range(args.steps)]
+        secs = sum(cpu_reference_run(reqs, prefixes, 1.0, ext, warmup=args.warmup)) / args.steps
         value = 1.0 / secs
         line = {"impl": "reference", "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
                 "value": round(value, 4), "unit": "trees/s", "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "configs[4] batched verify step, one request per step on the host CPU",
-                           "budget": BUDGET, "modes": K_MODES, "block": L_BLOCK, "vocab": VOCAB},
+                "scaling": "none: one host process with all its cores, whatever the GPU count",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"configs[4] batched verify step ({args.requests} requests), one request per "
+                                       "step on the host CPU, compute only",
+                           "requests": args.requests, "budget": BUDGET, "modes": K_MODES, "block": L_BLOCK,
+                           "vocab": VOCAB},
                 "cpu_baseline": {"value": round(value, 4), "unit": "trees/s", "cores": torch.get_num_threads(),
-                                 "kind": kind, "sample": "one request of the workload per step"},
+                                 "kind": kind, "sample": f"{args.steps} requests of the workload (ids 0..), one per "
+                                                         "step, inputs generated outside the timed compute"},
                 "e2e": {"value": round(value, 4), "unit": "trees/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -737,7 +891,7 @@ def main():
     from mfd_b200 import _lib
 
     _lib.load()
-    total = args.requests_per_gpu * ws
+    total = args.requests
     prefixes = prefix_lengths(total)
     reqs = partition(total, ws, rank, prefixes)
     batch = Batch(reqs, prefixes, dev)
@@ -753,23 +907,35 @@ def main():
     rows = len(reqs) * K_MODES * L_BLOCK
     logits_bytes = rows * VOCAB * 4
     achieved = logits_bytes / (per_kernel["logits_step"] * 1e-6) / 1e9
+    # roofline of the whole step: every input read once and every output written once, on the slowest rank
+    step_bytes = batch.step_bytes()
+    roof_ms = max_over_ranks(ws, step_bytes / (pk["hbm_gbs"] * 1e9) * 1e3)
+    job_bytes = sum_over_ranks(ws, step_bytes)
     line = {
         "metric": "verify-step trees/s (tree build + tree verify attention + accept)",
         "value": round(value, 3), "unit": "trees/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[4]: batched verify step, 32 requests per GPU, T=1",
+        "config": {"workload": f"configs[4]: batched verify step, {total} requests partitioned over {ws} GPU(s), T=1",
                    "requests": total, "requests_per_gpu": len(reqs), "budget": BUDGET, "modes": K_MODES,
                    "block": L_BLOCK, "vocab": VOCAB, "heads": H, "kv_heads": HKV, "head_dim": D,
                    "prefix": "U(1024, 8192)", "l2": "inputs (~117 MB per request) far larger than L2",
                    "dtypes": "fp32 drafter logits, bf16 q/k/v and target logits, fp32 accumulation",
-                   "parallelism": f"requests partitioned over {ws} GPU(s), no collective"},
+                   "parallelism": f"requests partitioned over {ws} GPU(s) (sorted by prefix, dealt round-robin), "
+                                  "no collective"},
         "kernels_us_per_step": {k: round(v, 2) for k, v in per_kernel.items()},
         "roofline": {"kernel": "mfd_topk_logz (logits step)", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                      "peak_source": pk["source"], "traffic": round(TOPK_TRAFFIC_PER_ROW * rows),
                      "traffic_source": "ncu capture of 1024 rows, scaled by rows",
                      "algorithmic_bytes_per_launch": logits_bytes},
+        "step_roofline": {"bound": "hbm", "algorithmic_bytes_per_step": job_bytes,
+                          "algorithmic_bytes_per_gpu": step_bytes, "roofline_ms": round(roof_ms, 4),
+                          "achieved_gbs_per_gpu": round(step_bytes / (ms_per_step * 1e-3) / 1e9, 1),
+                          "peak": pk["hbm_gbs"], "frac": round(roof_ms / ms_per_step, 4),
+                          "what": "every input of the step read once (drafter logits, q, prefix + tree K/V, target "
+                                  "logits, uniforms) and every output written once, on the slowest GPU"},
         "clocks": clocks,
         "gpu_launches": Step.LAUNCHES * args.steps,
     }

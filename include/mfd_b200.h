@@ -57,7 +57,8 @@ int mfd_topk_logz(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64
  * workspace and tickets: the scratch is one static device array in the library (4 MiB of partial records plus
  * tickets for 16384 rows; every GPU that loads the library holds it until the process exits).  Calls needing
  * more (mfd_topk_logz_workspace(rows, vocab, k) > 4 MiB, or rows > 16384) fail with MFD_ERR_UNSUPPORTED.
- * The first call on each device resolves the array's device address (make it before any stream capture).
+ * The first call on each device resolves the array's device address (make it before any stream capture; a
+ * cudaDeviceReset after that first call is not supported, since the cached address would go stale).
  * All calls share the array: calls that may run at the same time on the GPU (other streams, other threads)
  * race; stream-ordered calls do not.  Allocates nothing.
  * Replaces: nothing in the reference (no counterpart; an allocation-free form of the entry point above).
@@ -220,28 +221,35 @@ int mfd_tree_prep(const void* x, const void* conv_state, const int32_t* conv_ind
 
 /*
  * Commit step, KV moves in a token-major pool (SGLang).  buffers: a device array of num_buffers base addresses
- * (every layer's K and V buffer), each holding slots of slot_bytes (a multiple of 8; the bases 16-byte aligned when
- * slot_bytes is a multiple of 16).  For request b and i < width, slot move_src[b, i] moves to move_tgt[b, i] in
- * every buffer when the two differ; every source is read before any store (a path slot can be another move's
- * target).  move_src, move_tgt [bs, width] int64 on the device (width <= 1024).  One launch for all buffers.
+ * (every layer's K and V buffer), each holding slots of slot_bytes (a multiple of 8).  base_align: an alignment in
+ * bytes (a multiple of 8) that every buffer base has; the kernel moves 16-byte units only when slot_bytes and
+ * base_align are multiples of 16, else 8-byte units, so a base must be at least 8-byte aligned.  For request b and
+ * i < width, slot move_src[b, i] moves to move_tgt[b, i] in every buffer when the two differ; every source is read
+ * before any store (a path slot can be another move's target).  move_src, move_tgt [bs, width] int64 on the device
+ * (width <= 1024); negative ids are no-ops.  pool_slots > 0 bounds the slot ids: a move whose source or target is
+ * >= pool_slots is skipped and status (optional device int) receives MFD_ERR_INVALID; 0 leaves them unchecked.
+ * One launch for all buffers.
  * Replaces: patch:1769-1841 (DDTreeKVCompactor / _ddtree_compact_kv_kernel).
  */
-int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes, const int64_t* move_src,
-                        const int64_t* move_tgt, int64_t bs, int64_t width, void* stream);
+int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes, int64_t base_align,
+                        const int64_t* move_src, const int64_t* move_tgt, int64_t bs, int64_t width,
+                        int64_t pool_slots, int* status, void* stream);
 
 /*
  * Commit step, HF cache compaction.  buffers: a device array of num_buffers base addresses of cache tensors viewed
- * as [outer, rows, row_bytes] (outer_stride and row_stride in bytes, multiples of 8).  Row past_length + keep[i]
- * moves to past_length + i for i < keep_count in every buffer and outer index; nothing happens when the appended
- * window rows - past_length is empty, or keep_count is 0 or the whole window (as the reference returns early).
- * keep [keep_count] int64 on the device (keep_count <= 1024); status (optional device int) receives
- * MFD_ERR_INVALID for a keep index outside the window (that move is skipped).
+ * as [outer, rows, row_bytes] (outer_stride and row_stride in bytes, multiples of 8).  base_align: an alignment in
+ * bytes (a multiple of 8) that every buffer base has; 16-byte units are used only when it, row_bytes and both
+ * strides are multiples of 16.  Row past_length + keep[i] moves to past_length + i for i < keep_count in every
+ * buffer and outer index; nothing happens when the appended window rows - past_length is empty, or keep_count is
+ * 0 or the whole window (as the reference returns early).  keep [keep_count] int64 on the device
+ * (keep_count <= 1024); status (optional device int) receives MFD_ERR_INVALID for a keep index outside the window
+ * (that move is skipped).
  * Replaces: inference/hf/ddtree.py:33-61 (compact_tail_inplace), 385-403 (_compact_appended_window), applied by
  *           406-436 (compact_dynamic_cache) to every layer's keys and values.
  */
 int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, int64_t outer, int64_t outer_stride, int64_t rows,
-                     int64_t row_stride, int64_t row_bytes, int64_t past_length, const int64_t* keep,
-                     int64_t keep_count, int* status, void* stream);
+                     int64_t row_stride, int64_t row_bytes, int64_t base_align, int64_t past_length,
+                     const int64_t* keep, int64_t keep_count, int* status, void* stream);
 
 /*
  * Commit step of the Gated-DeltaNet layers: every layer's recurrent state (in place) becomes the state at the

@@ -58,8 +58,9 @@ _SIGS = {
                              c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mfd_tree_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp,
                               c_vp, c_vp]),
-    "mfd_commit_kv_moves": (c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp]),
-    "mfd_compact_tail": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp]),
+    "mfd_commit_kv_moves": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "mfd_compact_tail": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,
+                                 c_vp]),
     "mfd_gdn_commit": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                c_vp]),
     "mfd_conv_commit": (c_int, [c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),

@@ -33,11 +33,11 @@ struct Params {
     const int64_t* tgt;
     const int64_t* keep;     // HF: rows past + keep[i] -> past + i
     int64_t past;
-    int64_t rows;            // HF: rows per group (bounds check); 0: unchecked (pool slots)
+    int64_t rows;            // rows per group (HF) or slots of the pool (SGLang): bounds check; 0: unchecked
     int64_t list_stride;
     int L;
     int tile_units;          // units per CTA tile
-    int* status;             // optional: MFD_ERR_INVALID when an HF row index is out of range
+    int* status;             // optional: MFD_ERR_INVALID when a row index / slot id is out of range
 };
 
 template <typename U>
@@ -66,7 +66,9 @@ __global__ void __launch_bounds__(kThreads) moves_kernel(Params p) {
         } else {
             s = p.src[g * p.list_stride + i];
             t = p.tgt[g * p.list_stride + i];
-            ok = true;
+            // a slot id beyond the pool is skipped and flagged, never dereferenced
+            ok = !(p.rows > 0 && s != t && (s >= p.rows || t >= p.rows));
+            if (!ok && p.status) atomicExch(p.status, (int)MFD_ERR_INVALID);
         }
         if (ok && s != t && s >= 0 && t >= 0) {
             const int slot = atomicAdd(&n_moves, 1);  // order within the list does not matter: sources are staged
@@ -129,12 +131,14 @@ static int launch(Params p, int64_t groups, int64_t nbufs, int64_t slot_bytes, b
 using namespace mfd;
 
 extern "C" int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers, int64_t slot_bytes,
-                                   const int64_t* move_src, const int64_t* move_tgt, int64_t bs, int64_t width,
-                                   void* stream) {
-    if (bs < 0 || width < 0 || num_buffers < 0 || slot_bytes <= 0 || slot_bytes % 8 || width > ckv::kMaxMoves) {
-        set_error("mfd_commit_kv_moves: invalid sizes bs=%lld width=%lld buffers=%lld slot_bytes=%lld (a multiple "
-                  "of 8, width <= 1024)",
-                  (long long)bs, (long long)width, (long long)num_buffers, (long long)slot_bytes);
+                                   int64_t base_align, const int64_t* move_src, const int64_t* move_tgt, int64_t bs,
+                                   int64_t width, int64_t pool_slots, int* status, void* stream) {
+    if (bs < 0 || width < 0 || num_buffers < 0 || slot_bytes <= 0 || slot_bytes % 8 || width > ckv::kMaxMoves ||
+        base_align <= 0 || base_align % 8 || pool_slots < 0) {
+        set_error("mfd_commit_kv_moves: invalid sizes bs=%lld width=%lld buffers=%lld slot_bytes=%lld base_align=%lld "
+                  "pool_slots=%lld (slot_bytes and base_align multiples of 8, width <= 1024)",
+                  (long long)bs, (long long)width, (long long)num_buffers, (long long)slot_bytes,
+                  (long long)base_align, (long long)pool_slots);
         return MFD_ERR_INVALID;
     }
     if (bs == 0 || width == 0 || num_buffers == 0) return MFD_OK;
@@ -150,16 +154,20 @@ extern "C" int mfd_commit_kv_moves(const uint64_t* buffers, int64_t num_buffers,
     p.tgt = move_tgt;
     p.list_stride = width;
     p.L = (int)width;
-    // 16-byte units need 16-byte slots (the pool bases are allocator-aligned)
-    return ckv::launch(p, bs, num_buffers, slot_bytes, slot_bytes % 16 == 0, (cudaStream_t)stream,
-                       "mfd_commit_kv_moves");
+    p.rows = pool_slots;
+    p.status = status;
+    // 16-byte units need 16-byte slots and 16-byte aligned buffer bases
+    return ckv::launch(p, bs, num_buffers, slot_bytes, slot_bytes % 16 == 0 && base_align % 16 == 0,
+                       (cudaStream_t)stream, "mfd_commit_kv_moves");
 }
 
 extern "C" int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, int64_t outer, int64_t outer_stride,
-                                int64_t rows, int64_t row_stride, int64_t row_bytes, int64_t past_length,
-                                const int64_t* keep, int64_t keep_count, int* status, void* stream) {
+                                int64_t rows, int64_t row_stride, int64_t row_bytes, int64_t base_align,
+                                int64_t past_length, const int64_t* keep, int64_t keep_count, int* status,
+                                void* stream) {
     if (num_buffers < 0 || outer < 0 || rows < 0 || past_length < 0 || past_length > rows || keep_count < 0 ||
-        row_bytes <= 0 || row_bytes % 8 || row_stride % 8 || outer_stride % 8 || keep_count > ckv::kMaxMoves) {
+        row_bytes <= 0 || row_bytes % 8 || row_stride % 8 || outer_stride % 8 || keep_count > ckv::kMaxMoves ||
+        base_align <= 0 || base_align % 8) {
         set_error("mfd_compact_tail: invalid sizes (buffers %lld, outer %lld, rows %lld, past %lld, keep %lld, row "
                   "bytes %lld)",
                   (long long)num_buffers, (long long)outer, (long long)rows, (long long)past_length,
@@ -187,6 +195,6 @@ extern "C" int mfd_compact_tail(const uint64_t* buffers, int64_t num_buffers, in
     p.rows = rows;
     p.L = (int)keep_count;
     p.status = status;
-    const bool a16 = row_bytes % 16 == 0 && row_stride % 16 == 0 && outer_stride % 16 == 0;
+    const bool a16 = row_bytes % 16 == 0 && row_stride % 16 == 0 && outer_stride % 16 == 0 && base_align % 16 == 0;
     return ckv::launch(p, outer, num_buffers, row_bytes, a16, (cudaStream_t)stream, "mfd_compact_tail");
 }

@@ -701,6 +701,7 @@ static int sm_count() {
 }
 
 static int kp_for(int64_t k) {
+    if (k > 256) return 256;  // (callers reject k > 256; this only keeps the doubling from overflowing)
     int kp = 32;
     while (kp < k) kp <<= 1;
     return kp;
@@ -749,7 +750,7 @@ static Plan plan(int64_t rows, int64_t vocab, int64_t k) {
 using namespace mfd;
 
 extern "C" size_t mfd_topk_logz_workspace(int64_t rows, int64_t vocab, int64_t k) {
-    if (rows <= 0 || vocab <= 0 || k <= 0) return 0;
+    if (rows <= 0 || vocab <= 0 || k <= 0 || k > vocab || k > 256 || vocab >= (int64_t)0x7fffffff) return 0;
     topk::Plan pl = topk::plan(rows, vocab, k);
     const size_t ms = (size_t)rows * pl.max_pieces * sizeof(float2);
     const size_t keys = (size_t)rows * pl.max_pieces * pl.kp * sizeof(uint64_t);

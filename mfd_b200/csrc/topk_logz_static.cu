@@ -10,7 +10,9 @@
 // The array's name in host code is only a host-side stand-in for the device symbol, not a device address: a
 // kernel given it would fault or, where the GPU can reach host memory, silently use the wrong memory.  So on the
 // first call on each device, with that device current, cudaGetSymbolAddress() resolves the device address once
-// and caches it per device; later calls reuse it.  Make that first call before capturing any stream.
+// and caches it per device; later calls reuse it.  Make that first call before capturing any stream.  The cached
+// address belongs to the device context that was current then: after a cudaDeviceReset the module may load at
+// another address, so resetting a device after its first call here is not supported.
 //
 // Every call shares the array and it keeps the previous call's contents: the ticket words, which must start at
 // zero, are cleared on the call's stream before the kernel runs (cudaMemsetAsync, no allocation).  Calls whose
@@ -71,9 +73,22 @@ int scratch_for_current_device(unsigned char** out) {
 extern "C" int mfd_topk_logz_static(const void* x, int x_dtype, int64_t rows, int64_t vocab, int64_t row_stride,
                                     int64_t k, float* top_logp, void* top_ids, int ids_dtype, float* logz,
                                     void* stream) {
-    if (rows < 0 || vocab <= 0 || k <= 0) {
-        mfd::set_error("mfd_topk_logz_static: invalid sizes rows=%lld vocab=%lld k=%lld", (long long)rows,
-                       (long long)vocab, (long long)k);
+    // the argument checks of mfd_topk_logz, before any capacity check, so invalid calls report MFD_ERR_INVALID
+    if (rows < 0 || vocab <= 0 || k <= 0 || k > vocab || k > 256 || row_stride < vocab) {
+        mfd::set_error("mfd_topk_logz_static: invalid sizes rows=%lld vocab=%lld k=%lld stride=%lld (need "
+                       "0<k<=min(vocab,256))", (long long)rows, (long long)vocab, (long long)k, (long long)row_stride);
+        return MFD_ERR_INVALID;
+    }
+    if (x_dtype != MFD_F32 && x_dtype != MFD_BF16) {
+        mfd::set_error("mfd_topk_logz_static: x_dtype must be MFD_F32 or MFD_BF16");
+        return MFD_ERR_INVALID;
+    }
+    if (ids_dtype != MFD_I32 && ids_dtype != MFD_I64) {
+        mfd::set_error("mfd_topk_logz_static: ids_dtype must be MFD_I32 or MFD_I64");
+        return MFD_ERR_INVALID;
+    }
+    if (vocab >= (int64_t)0x7fffffff) {
+        mfd::set_error("mfd_topk_logz_static: vocab must be < 2^31");
         return MFD_ERR_INVALID;
     }
     if (rows == 0) return MFD_OK;

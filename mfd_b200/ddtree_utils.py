@@ -190,6 +190,14 @@ class DDTreeKVCompactor:
             raise ValueError(f"DDTree KV compaction needs one slot stride (multiple of 8 bytes), got {strides}")
         self.data_ptrs = kv_pool.data_ptrs
         self.slot_bytes = next(iter(strides))
+        # the alignment every buffer base has (read once here, so the call itself does no host read) and the
+        # pool's slot count when the pool exposes its buffers (slot ids beyond it are skipped, not dereferenced)
+        bases = [int(b) for b in kv_pool.data_ptrs.tolist()]
+        if any(b % 8 for b in bases):
+            raise ValueError("DDTree KV compaction needs buffer bases aligned to 8 bytes")
+        self.base_align = 16 if all(b % 16 == 0 for b in bases) else 8
+        bufs = getattr(kv_pool, "k_buffer", None)
+        self.pool_slots = int(bufs[0].shape[0]) if bufs else 0
 
     @staticmethod
     def supports(kv_pool) -> bool:
@@ -207,4 +215,5 @@ class DDTreeKVCompactor:
     def __call__(self, *, move_src: torch.Tensor, move_tgt: torch.Tensor) -> None:
         if move_src.shape[0] == 0:
             return
-        ops.commit_kv_moves(self.data_ptrs, self.slot_bytes, move_src, move_tgt)
+        ops.commit_kv_moves(self.data_ptrs, self.slot_bytes, move_src, move_tgt, base_align=self.base_align,
+                            pool_slots=self.pool_slots)

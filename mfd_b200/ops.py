@@ -384,34 +384,44 @@ def _pointer_array(tensors, dev, extra=()) -> torch.Tensor:
     return arr
 
 
-def commit_kv_moves(buffers, slot_bytes: int, move_src: torch.Tensor, move_tgt: torch.Tensor) -> None:
+def _base_align(addr: int) -> int:
+    return 16 if addr % 16 == 0 else 8
+
+
+def commit_kv_moves(buffers, slot_bytes: int, move_src: torch.Tensor, move_tgt: torch.Tensor,
+                    base_align: int | None = None, pool_slots: int = 0, status: torch.Tensor | None = None) -> None:
     """The commit step's KV moves in a token-major pool: for request b and i < width, slot move_src[b, i] moves to
     move_tgt[b, i] in every buffer when they differ, every source read before any store.  buffers: a list of
     CUDA tensors (one per layer K / V buffer, slot_bytes per slot) or a device int64 tensor of base addresses
-    (the pool's data_ptrs).  move_src, move_tgt [bs, width] int64 on the device.  One launch."""
-    dev = require_cuda(move_src, move_tgt)
+    (the pool's data_ptrs, with `base_align` the alignment all of them have; 8 when not given).  move_src,
+    move_tgt [bs, width] int64 on the device.  pool_slots > 0: moves with a slot id >= pool_slots are skipped and
+    flagged in `status` (device int32).  One launch."""
+    dev = require_cuda(move_src, move_tgt, status)
     if isinstance(buffers, torch.Tensor) and buffers.dtype == torch.int64 and buffers.dim() == 1:
         ptrs = buffers.to(dev)
+        align = 8 if base_align is None else int(base_align)
     else:
         buffers = list(buffers)
-        align = 16 if slot_bytes % 16 == 0 else 8
         for t in buffers:
-            if not t.is_cuda or t.data_ptr() % align:
-                raise RuntimeError(f"commit_kv_moves: buffers must be CUDA tensors aligned to {align} bytes")
+            if not t.is_cuda or t.data_ptr() % 8:
+                raise RuntimeError("commit_kv_moves: buffers must be CUDA tensors aligned to 8 bytes")
+        align = min([_base_align(t.data_ptr()) for t in buffers] or [16])
         ptrs = _pointer_array(buffers, dev)
     src = move_src.to(torch.int64).contiguous()
     tgt = move_tgt.to(torch.int64).contiguous()
     if src.shape != tgt.shape or src.dim() != 2:
         raise RuntimeError("commit_kv_moves: move_src and move_tgt must both be [bs, width]")
-    rc = _lib.lib().mfd_commit_kv_moves(ptrs.data_ptr(), ptrs.numel(), int(slot_bytes), src.data_ptr(),
-                                        tgt.data_ptr(), src.shape[0], src.shape[1], stream_ptr(dev))
+    rc = _lib.lib().mfd_commit_kv_moves(ptrs.data_ptr(), ptrs.numel(), int(slot_bytes), align, src.data_ptr(),
+                                        tgt.data_ptr(), src.shape[0], src.shape[1], int(pool_slots), ptr(status),
+                                        stream_ptr(dev))
     check(rc, "mfd_commit_kv_moves")
 
 
 def compact_tail(tensors, past_length: int, keep, status: torch.Tensor | None = None) -> None:
     """Row past_length + keep[i] -> past_length + i along dim -2 of every tensor (HF caches [..., S, D]), in place,
-    all tensors of one layout in one launch; no-op when the appended window is empty or keep is empty or keeps the
-    whole window (the reference's early returns).  keep: a list of ints or a device int64 tensor."""
+    all tensors of one layout and base alignment in one launch; no-op when the appended window is empty or keep is
+    empty or keeps the whole window (the reference's early returns).  keep: a list of ints or a device int64
+    tensor.  A tensor whose base is only 8-byte aligned goes to the 8-byte path."""
     tensors = [t for t in tensors if t is not None and t.numel() > 0]
     if not tensors:
         return
@@ -428,20 +438,37 @@ def compact_tail(tensors, past_length: int, keep, status: torch.Tensor | None = 
     for t in tensors:
         if t.dim() < 2 or t.stride(-1) != 1:
             raise RuntimeError("compact_tail: tensors need a contiguous last dim")
+        if t.data_ptr() % 8:
+            raise RuntimeError("compact_tail: tensors must start on an 8-byte boundary")
         outer = t.numel() // (t.shape[-2] * t.shape[-1])
         try:
             v = t.view(outer, t.shape[-2], t.shape[-1]) if t.dim() != 3 or outer != t.shape[0] else t
         except RuntimeError as e:
             raise RuntimeError("compact_tail: the dims before the last two must collapse into one stride") from e
         es = t.element_size()
-        key = (tuple(v.shape), v.stride(0) * es, v.stride(1) * es, v.shape[2] * es)
+        key = (tuple(v.shape), v.stride(0) * es, v.stride(1) * es, v.shape[2] * es, _base_align(v.data_ptr()))
         groups.setdefault(key, []).append(v)
     L = _lib.lib()
-    for (shape, outer_stride, row_stride, row_bytes), views in groups.items():
+    for (shape, outer_stride, row_stride, row_bytes, align), views in groups.items():
         ptrs = _pointer_array(views, dev)
         rc = L.mfd_compact_tail(ptrs.data_ptr(), ptrs.numel(), shape[0], outer_stride, shape[1], row_stride, row_bytes,
-                                int(past_length), keep_t.data_ptr(), keep_t.numel(), ptr(status), stream_ptr(dev))
+                                align, int(past_length), keep_t.data_ptr(), keep_t.numel(), ptr(status),
+                                stream_ptr(dev))
         check(rc, "mfd_compact_tail")
+
+
+def compact_tail_groups(tensors) -> list:
+    """The launch groups compact_tail forms for these tensors: (shape, outer stride, row stride, row bytes, base
+    alignment) per group, in first-seen order.  Host logic only (no launch)."""
+    keys = []
+    for t in tensors:
+        outer = t.numel() // (t.shape[-2] * t.shape[-1])
+        es = t.element_size()
+        v = t.view(outer, t.shape[-2], t.shape[-1]) if t.dim() != 3 or outer != t.shape[0] else t
+        key = (tuple(v.shape), v.stride(0) * es, v.stride(1) * es, v.shape[2] * es, _base_align(v.data_ptr()))
+        if key not in keys:
+            keys.append(key)
+    return keys
 
 
 def gdn_commit(states, us, ks, gs, path) -> None:

@@ -215,3 +215,37 @@ def test_qwen35_commit_end_to_end():
         torch.testing.assert_close(cache.layers[li].recurrent_states[0].cpu(), s_ref, rtol=0,
                                    atol=1e-5 * float(s_ref.abs().max()))
         assert torch.equal(cache.layers[li].conv_states[0].cpu(), c_ref)
+
+
+def test_commit_kv_moves_skips_slot_ids_beyond_the_pool():
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(5)
+    nslots, width = 64, 8
+    bufs = [torch.randint(-2**62, 2**62, (nslots, 256), generator=g, dtype=torch.int64).to(DEV) for _ in range(3)]
+    before = [b.clone() for b in bufs]
+    src = torch.zeros(2, width, dtype=torch.int64)
+    tgt = torch.zeros(2, width, dtype=torch.int64)
+    src[0, 0], tgt[0, 0] = 10, 3          # a valid move
+    src[1, 0], tgt[1, 0] = nslots + 5, 4  # source beyond the pool
+    src[1, 1], tgt[1, 1] = 6, 1 << 40     # target beyond the pool
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.commit_kv_moves(bufs, 2048, src.to(DEV), tgt.to(DEV), pool_slots=nslots, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 1  # MFD_ERR_INVALID
+    for b, o in zip(bufs, before):
+        want = o.clone()
+        want[3] = o[10]
+        assert torch.equal(b, want)  # only the valid move happened
+
+
+def test_compact_tail_on_an_8_byte_aligned_view():
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(6)
+    flat = torch.randint(-2**62, 2**62, (2 * 30 * 16 + 1,), generator=g, dtype=torch.int64)
+    view_cpu = flat[1:].view(2, 30, 16)
+    ref = oracle.compact_tail(view_cpu.numpy(), 20, [3, 5, 9])
+    dflat = flat.to(DEV)
+    view = dflat[1:].view(2, 30, 16)
+    assert view.data_ptr() % 16 == 8
+    ops.compact_tail([view], 20, [3, 5, 9])
+    assert np.array_equal(view.cpu().numpy(), ref)

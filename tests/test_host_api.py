@@ -74,3 +74,14 @@ def test_load_draft_vocab_formats(tmp_path, monkeypatch):
     assert ddtree_utils.ddtree_draft_vocab_path() == str(a)
     monkeypatch.delenv("SGLANG_DFLASH_DDTREE_DRAFT_VOCAB")
     assert ddtree_utils.ddtree_draft_vocab_path() == ""
+
+
+def test_compact_tail_routes_8_byte_aligned_bases_to_the_8_byte_path():
+    from mfd_b200 import ops
+    buf = torch.zeros(2 * 40 * 16 + 1, dtype=torch.int64)
+    base = buf[: 2 * 40 * 16].view(2, 40, 16)        # 16-byte rows, base aligned as allocated
+    shifted = buf[1:].view(2, 40, 16)                  # same layout, base 8 bytes further on
+    assert base.data_ptr() % 16 == 0 and shifted.data_ptr() % 16 == 8
+    keys = ops.compact_tail_groups([base, shifted])
+    assert len(keys) == 2 and keys[0][-1] == 16 and keys[1][-1] == 8
+    assert keys[0][:-1] == keys[1][:-1]  # only the alignment separates the two launches

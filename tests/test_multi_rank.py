@@ -23,7 +23,7 @@ def _worker(rank, ws, port, queue):
     try:
         import bench
 
-        total = bench.REQUESTS_PER_GPU * ws
+        total = bench.TOTAL_REQUESTS
         prefixes = bench.prefix_lengths(total)
         reqs = bench.partition(total, ws, rank, prefixes)
         mx = bench.max_over_ranks(ws, float(10 + rank))

@@ -60,3 +60,9 @@ def test_static_scratch_rejects_oversize_requests():
         rc = lib.mfd_topk_logz_static(None, MFD_F32, R, V, V, k, None, None, MFD_I64, None, None)
         assert rc == 2
         assert b"static scratch" in lib.mfd_last_error()
+    # invalid arguments report MFD_ERR_INVALID before any capacity check (k = 2^31 would overflow a doubling loop)
+    for R, V, k in [(8192, 151936, 1 << 31), (4, 100, 257), (4, 100, 101)]:
+        rc = lib.mfd_topk_logz_static(None, MFD_F32, R, V, V, k, None, None, MFD_I64, None, None)
+        assert rc == 1
+        assert b"invalid sizes" in lib.mfd_last_error()
+    assert lib.mfd_topk_logz_workspace(8192, 151936, 1 << 31) == 0
