@@ -481,6 +481,20 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
             const uint32_t s_tm = tmem + lane_off + kSCol + bi * kKt;
             ok &= mbar_wait(&bars[kBarSFull + bi], (i >> 1) & 1, kTries);
             tc_fence_after();
+            if (key0 + kKt > k_hi) {
+                // the tile runs past this split's keys: its rows from k_hi on hold whatever the caller's buffer
+                // has beyond the request's keys (any bits, NaN included).  Their P is 0, but 0 * NaN is NaN in the
+                // P V product, so those V rows are cleared before P is published (the tile landed before S(i) was
+                // computed, and P V (i) is issued only after every softmax warp has arrived below).  Each key row
+                // is 128 contiguous bytes per d-half, whatever the swizzle order of its 16-byte granules.
+                const int r0 = k_hi > key0 ? k_hi - key0 : 0;
+                unsigned char* vt = smem + kOffV + (i % kStages) * kKVBytes;
+                for (int g = threadIdx.x - 64; g < (kKt - r0) * 16; g += kSoftmaxThreads) {
+                    const int rr = r0 + (g >> 4), h = (g >> 3) & 1, c = g & 7;
+                    *reinterpret_cast<uint4*>(vt + h * (kKVBytes / 2) + rr * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores' reads
+            }
             if (!quarter_live) {
                 tc_fence_before();
                 __syncwarp();

@@ -135,3 +135,37 @@ def test_tree_attention_workspace_reused_across_sizes():
                                         D ** -0.5)
             assert np.abs(out[b] - ref).max() <= TOL, (bs, splits, b)
     assert ops.tree_attention_status() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3])
+def test_tree_attention_ignores_nan_beyond_each_requests_keys(splits):
+    """A KV buffer holds whatever the caller left beyond a request's keys (here NaN, in K and V alike, and under
+    a shorter constant prefix too): masked keys of a tile that runs past the request's last key must contribute
+    nothing, as keys the reference's mask + SDPA never sees."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(90 + splits)
+    bs, n, H, Hkv, D, S = 3, 65, 32, 8, 128, 1500
+    prefixes = [1413, 700, 1000]
+    parents = [[-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)] for _ in range(bs)]
+    q = torch.randn(bs, n, H, D, generator=g).to(torch.bfloat16)
+    k = torch.full((bs, Hkv, S, D), float("nan")).to(torch.bfloat16)
+    v = torch.full((bs, Hkv, S, D), float("nan")).to(torch.bfloat16)
+    for b, p in enumerate(prefixes):
+        k[b, :, :p + n] = (torch.randn(Hkv, p + n, D, generator=g) * 0.5).to(torch.bfloat16)
+        v[b, :, :p + n] = (torch.randn(Hkv, p + n, D, generator=g) * 0.5).to(torch.bfloat16)
+    anc = torch.stack([anc_bits(par, 2) for par in parents]).to(DEV)
+    pl = torch.tensor(prefixes, dtype=torch.int32, device=DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, pl, D ** -0.5, splits=splits).float().cpu()
+    assert torch.isfinite(out).all()
+    for b, p in enumerate(prefixes):
+        kk = k[b, :, :p + n].transpose(0, 1).float().numpy()
+        vv = v[b, :, :p + n].transpose(0, 1).float().numpy()
+        ref = oracle.tree_attention(q[b].float().numpy(), kk[:p], vv[:p], kk[p:], vv[p:], parents[b], D ** -0.5)
+        assert np.abs(out[b].numpy() - ref).max() <= TOL
+    # one constant prefix shorter than the buffer: the keys after prefix + n are NaN as well
+    p = 700
+    kc, vc = k[1:2].clone(), v[1:2].clone()
+    out1 = ops.tree_attention(q[1:2].to(DEV), kc.to(DEV), vc.to(DEV), anc[1:2], p, D ** -0.5, splits=splits)
+    assert torch.isfinite(out1.float()).all()
+    assert torch.equal(out1.cpu(), out[1:2].to(torch.bfloat16)) or \
+        (out1.float().cpu() - out[1:2]).abs().max() <= TOL
