@@ -13,6 +13,7 @@
 
 #include <stddef.h>
 #include <stdint.h>
+#include <stdbool.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -137,6 +138,22 @@ int mfd_verify_inputs(const int64_t* root_tokens, const int64_t* prefix_lens, co
                       int8_t* mask_out, void* stream);
 
 /*
+ * HF verify inputs of one tree, in the caller's buffers: ids[0] = *root_token, ids[i] = tokens[i]; positions[i] =
+ * start + depths[i] (i < n, node 0 the root); the tree block of the additive mask, mask[i, past_length + j] = 0
+ * where vis[i, j] != 0 else the bits min_bits (i, j < n); the previous round's block mask[i, prev_start + j]
+ * (i, j < prev_length) reset to 0 outside the new block; vis_out[i, j] = vis[i, j] (bool).  root_token, tokens,
+ * depths (int64), vis ([n, vis_stride] uint8) on the device.  mask: [mask_rows, mask_cols] elements of
+ * mask_elem_bytes (2: bf16 / fp16, 4: fp32) with row stride mask_row_stride elements; both blocks must lie inside.
+ * Replaces: inference/hf/ddtree.py:317-357 (compile_ddtree_tree: its host-to-device copies of ids, depths and
+ * visibility and the fill / masked_fill of the mask block).
+ */
+int mfd_compile_tree(const int64_t* root_token, const int64_t* tokens, const int64_t* depths, int64_t n,
+                     const uint8_t* vis, int64_t vis_stride, int64_t start, int64_t past_length, int64_t prev_start,
+                     int64_t prev_length, int64_t* ids_out, int64_t* positions_out, void* mask,
+                     int64_t mask_elem_bytes, int64_t mask_row_stride, int64_t mask_rows, int64_t mask_cols,
+                     uint32_t min_bits, bool* vis_out, int64_t vis_out_stride, void* stream);
+
+/*
  * Tree-masked GQA verify attention on the tcgen05 tensor cores.  q, out [bs, n, H, 128] bf16 (strides in elements,
  * multiples of 8, last dim contiguous); k, v [bs, Hkv, max_keys, 128] bf16 holding each request's prefix keys
  * followed by its n tree keys (keys at or past max_keys are never read); prefix_lens [bs] int32 on the device (or
@@ -206,6 +223,19 @@ int mfd_tree_gdn(const void* q, int64_t sq, const void* k, int64_t sk, const voi
                  const float* g_cum, int64_t sg, const float* beta, int64_t sb, const float* s0, const int8_t* anc,
                  int64_t sa, int64_t n, int64_t num_heads, int64_t num_k_heads, int64_t dk, int64_t dv, float* u,
                  float* o, float* states, int* status, void* stream);
+
+/*
+ * Gates of a Gated-DeltaNet layer over a tree, per node i and value head h: beta = sigmoid(b[i, h]),
+ * g = -exp(A_log[h]) * softplus(a[i, h] + dt_bias[h]), and G[i, h] = the sum of g over the root path of i (i
+ * included).  a, b [n, H] (row strides sa, sb in elements; ab_dtype MFD_BF16 or MFD_F32), A_log and dt_bias [H]
+ * float32, parents [n] int64 (parents[i] < i, -1 for a root) on the device; outputs beta, G [n, H] float32.
+ * n <= 2048.  status (optional device int) receives MFD_ERR_INVALID for a parent that is not an earlier node
+ * (that node is treated as a root).
+ * Replaces: inference/hf/qwen35_tree.py:77-79 (sigmoid, softplus decay, G = anc_f @ g).
+ */
+int mfd_tree_gates(const void* a, int64_t sa, const void* b, int64_t sb, int ab_dtype, const float* a_log,
+                   const float* dt_bias, const int64_t* parents, int64_t n, int64_t num_heads, float* beta, float* G,
+                   int* status, void* stream);
 
 /*
  * Inputs of mfd_tree_gdn from the pre-convolution projections: per node i and channel c,

@@ -45,6 +45,8 @@ _SIGS = {
                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mfd_verify_inputs": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
                                   c_vp]),
+    "mfd_compile_tree": (c_int, [c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp,
+                                 c_i64, c_i64, c_i64, c_i64, ctypes.c_uint32, c_vp, c_i64, c_vp]),
     "mfd_tree_attention_workspace": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64]),
     "mfd_tree_attention_tickets": (c_i64, [c_i64, c_i64, c_i64, c_i64]),
     "mfd_tree_attention": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_i64,
@@ -56,6 +58,8 @@ _SIGS = {
                                          c_i64, c_i64, c_vp, c_size, c_vp, c_i64, c_vp]),
     "mfd_tree_gdn": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64,
                              c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "mfd_tree_gates": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp,
+                               c_vp]),
     "mfd_tree_prep": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_f32, c_vp, c_vp,
                               c_vp, c_vp]),
     "mfd_commit_kv_moves": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),

@@ -89,10 +89,9 @@ class Tree:
 
 
 def _trivial(build_subtimes):
-    visibility = torch.zeros((1, 1), dtype=torch.bool)
-    visibility[0, 0] = True
+    """The root-only tree the reference returns for budget <= 0 or no drafted positions."""
     return (torch.empty(0, dtype=torch.long), torch.empty(0, dtype=torch.long), [-1],
-            _EmptyTree(), visibility, build_subtimes)
+            _EmptyTree(), torch.ones((1, 1), dtype=torch.bool), build_subtimes)
 
 
 class _EmptyTree(list):
@@ -123,6 +122,10 @@ def _build(draft_logits: torch.Tensor, prior: torch.Tensor | None, budget: int, 
     node_depths = tree_cpu[1, 1 : n + 1].clone()
     parents = tree_cpu[2, : n + 1].tolist()
     child_maps = Tree(tree[0, 0], tree[0, 2], n + 1, tree_cpu[0], tree_cpu[2])
+    # the device copies travel with the host tensors the reference's callers receive, so compile_ddtree_tree and
+    # qwen35_tree.tree_verify read the tree where it was built instead of copying it back to the device
+    node_token_ids._mfd_tree = tree[0]
+    vis_cpu._mfd_vis = vis[0]
     return node_token_ids, node_depths, parents, child_maps, vis_cpu, build_subtimes
 
 
@@ -146,51 +149,59 @@ def build_mixture_tree(draft_logits: torch.Tensor, mode_log_prior: torch.Tensor,
 def compile_ddtree_tree(root_token_id, start, node_token_ids, node_depths, visibility_cpu, past_length, dtype,
                         device, verify_input_ids_buffer, verify_position_ids_buffer, attention_mask_buffer,
                         tree_visibility_buffer, previous_tree_start, previous_tree_length):
-    """Verify inputs and the additive tree mask in the caller's buffers (inference/hf/ddtree.py:317-357)."""
-    current_length = 1 + int(node_token_ids.numel())
-    if previous_tree_length > 0:
-        attention_mask_buffer[0, 0, :previous_tree_length,
-                              previous_tree_start: previous_tree_start + previous_tree_length] = 0
-    verify_input_ids = verify_input_ids_buffer[:, :current_length]
-    verify_input_ids[0, 0] = root_token_id
-    if current_length > 1:
-        verify_input_ids[0, 1:current_length].copy_(node_token_ids, non_blocking=False)
-    verify_position_ids = verify_position_ids_buffer[:, :current_length]
-    verify_position_ids[0, 0] = start
-    if current_length > 1:
-        verify_position_ids[0, 1:current_length].copy_(node_depths, non_blocking=False)
-        verify_position_ids[0, 1:current_length].add_(start)
-    visibility = tree_visibility_buffer[:current_length, :current_length]
-    visibility.copy_(visibility_cpu, non_blocking=False)
-    tree_block = attention_mask_buffer[0, 0, :current_length, past_length: past_length + current_length]
-    tree_block.fill_(torch.finfo(dtype).min)
-    tree_block.masked_fill_(visibility, 0)
-    attention_mask = attention_mask_buffer[:, :, :current_length, : past_length + current_length]
-    return verify_input_ids, verify_position_ids, attention_mask, past_length, current_length
+    """Verify inputs and the additive tree mask in the caller's buffers (inference/hf/ddtree.py:317-357): one
+    mfd_compile_tree launch writes the ids, the positions, the visibility and the tree's block of the mask, and
+    resets the previous round's block.  A tree from this package's builders is read on the device where it was
+    built (nothing crosses the bus, nothing waits for the host); a tree built elsewhere is copied over once."""
+    n = 1 + int(node_token_ids.numel())
+    dev = attention_mask_buffer.device
+    tree = getattr(node_token_ids, "_mfd_tree", None)
+    vis = getattr(visibility_cpu, "_mfd_vis", None)
+    if tree is None or vis is None or tree.device != dev or vis.device != dev:
+        host = torch.zeros(2, n, dtype=torch.long)
+        host[0, 1:] = node_token_ids.reshape(-1)
+        host[1, 1:] = node_depths.reshape(-1)
+        tree = host.to(dev)
+        vis = visibility_cpu.to(device=dev, dtype=torch.uint8)
+    if isinstance(root_token_id, torch.Tensor) and root_token_id.device == dev:
+        root = root_token_id.reshape(1).to(torch.long)
+    else:
+        root = torch.tensor([int(root_token_id)], dtype=torch.long, device=dev)
+    mask2d = attention_mask_buffer[0, 0]
+    ops.compile_tree(root, tree[0], tree[1], vis, n, start, past_length, previous_tree_start, previous_tree_length,
+                     verify_input_ids_buffer[0], verify_position_ids_buffer[0], mask2d, torch.finfo(dtype).min,
+                     tree_visibility_buffer)
+    return (verify_input_ids_buffer[:, :n], verify_position_ids_buffer[:, :n],
+            attention_mask_buffer[:, :, :n, : past_length + n], past_length, n)
 
 
 def multi_mode_draft_mask(context_length: int, num_modes: int, block_size: int, dtype: torch.dtype,
                           device: torch.device) -> torch.Tensor:
-    """Additive [1, 1, K*bs, context + K*bs] mask of a multi-mode draft step (inference/hf/ddtree.py:360-365)."""
-    query_block = torch.arange(num_modes * block_size, device=device) // block_size
-    mask = torch.zeros((num_modes * block_size, context_length + num_modes * block_size), dtype=dtype, device=device)
-    mask[:, context_length:].masked_fill_(query_block.unsqueeze(1) != query_block.unsqueeze(0), torch.finfo(dtype).min)
-    return mask.view(1, 1, *mask.shape)
+    """Additive [1, 1, K*bs, context + K*bs] mask of a multi-mode draft step (inference/hf/ddtree.py:360-365): the
+    context is open to every query; the block part is closed except on the K diagonal blocks, where a mode's
+    queries see their own block's keys (not causal inside a block)."""
+    rows = num_modes * block_size
+    mask = torch.full((rows, context_length + rows), torch.finfo(dtype).min, dtype=dtype, device=device)
+    mask[:, :context_length] = 0
+    # [K, bs, K, bs] view of the block part; its diagonal over the two mode axes is the K own-mode blocks
+    mask[:, context_length:].unflatten(0, (num_modes, block_size)).unflatten(2, (num_modes, block_size)) \
+        .diagonal(dim1=0, dim2=2).zero_()
+    return mask[None, None]
 
 
 def follow_verified_tree(child_maps, posterior: torch.Tensor):
-    """(accepted node indices, next token): follow the target's token at each node from the root."""
+    """(accepted node indices, next token): from the root, step to the child whose token the target produced at the
+    current node, while there is one.  A Tree (this package's builders) walks on the device (mfd_follow); a list of
+    {token: child} dicts (the reference's Python child maps, or the root-only tree) walks here."""
     if isinstance(child_maps, Tree):
         return child_maps.follow(posterior[0])
-    posterior_tokens = posterior[0].tolist()
-    accepted_indices = [0]
-    current_index = 0
-    next_token = int(posterior_tokens[current_index])
-    while next_token in child_maps[current_index]:
-        current_index = child_maps[current_index][next_token]
-        accepted_indices.append(current_index)
-        next_token = int(posterior_tokens[current_index])
-    return accepted_indices, next_token
+    target = [int(t) for t in posterior[0].tolist()]
+    path = [0]
+    while True:
+        child = child_maps[path[-1]].get(target[path[-1]])
+        if child is None:
+            return path, target[path[-1]]
+        path.append(child)
 
 
 # ----------------------------------------------------------------------------------------------- commit step

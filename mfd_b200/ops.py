@@ -202,6 +202,29 @@ def verify_inputs(root_tokens, prefix_lens, tokens, depths, parents, mask_offset
     check(rc, "mfd_verify_inputs")
 
 
+def compile_tree(root: torch.Tensor, tokens: torch.Tensor, depths: torch.Tensor, vis: torch.Tensor, n: int, start: int,
+                 past_length: int, prev_start: int, prev_length: int, ids_out: torch.Tensor, positions_out: torch.Tensor,
+                 mask: torch.Tensor, min_value: float, vis_out: torch.Tensor) -> None:
+    """One tree's HF verify inputs (mfd_compile_tree): root int64 [1] / 0-dim, tokens and depths int64 [>= n] (slot 0
+    the root), vis uint8 [>= n, >= n] (row-contiguous), all on the device; ids_out / positions_out int64 [>= n];
+    mask [rows, cols] (bf16 / fp16 / fp32, last dim contiguous); vis_out bool [>= n, >= n].  min_value is written
+    where a tree key is not visible, in mask's dtype."""
+    dev = require_cuda(root, tokens, depths, vis, ids_out, positions_out, mask, vis_out)
+    if mask.dim() != 2 or mask.stride(1) != 1 or mask.element_size() not in (2, 4):
+        raise RuntimeError("compile_tree: mask must be 2-D with a contiguous last dim, 2- or 4-byte elements")
+    if vis.stride(1) != 1 or vis_out.stride(1) != 1 or ids_out.stride(-1) != 1 or positions_out.stride(-1) != 1:
+        raise RuntimeError("compile_tree: vis, vis_out, ids and positions need a contiguous last dim")
+    bits_t = torch.int16 if mask.element_size() == 2 else torch.int32
+    min_bits = int(torch.tensor(min_value, dtype=mask.dtype).view(bits_t).item()) & (0xFFFF if bits_t == torch.int16
+                                                                                      else 0xFFFFFFFF)
+    rc = _lib.lib().mfd_compile_tree(root.data_ptr(), tokens.data_ptr(), depths.data_ptr(), int(n), vis.data_ptr(),
+                                     vis.stride(0), int(start), int(past_length), int(prev_start), int(prev_length),
+                                     ids_out.data_ptr(), positions_out.data_ptr(), mask.data_ptr(), mask.element_size(),
+                                     mask.stride(0), mask.shape[0], mask.shape[1], min_bits, vis_out.data_ptr(),
+                                     vis_out.stride(0), stream_ptr(dev))
+    check(rc, "mfd_compile_tree")
+
+
 # ----------------------------------------------------------------------------------------------- attention
 
 def default_splits(bs: int, n: int, num_heads: int, num_kv_heads: int, keys: int) -> int:
@@ -341,6 +364,30 @@ def tree_gdn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g_cum: torch.Ten
                                  ptr(st), ptr(status), stream_ptr(dev))
     check(rc, "mfd_tree_gdn")
     return (u, o, st) if emit_states else (u, o)
+
+
+def tree_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor, parents: torch.Tensor,
+               status: torch.Tensor | None = None):
+    """a, b [n, H] (the layer's in_proj_a / in_proj_b outputs, bf16 or float32), a_log, dt_bias [H], parents [n]
+    int64 on the device -> (beta, G) float32 [n, H]: sigmoid(b) and the per-token log decay
+    -exp(A_log) softplus(a + dt_bias) summed along each node's root path."""
+    dev = require_cuda(a, b, a_log, dt_bias, parents, status)
+    n, H = a.shape
+    if b.shape != a.shape or b.dtype != a.dtype or a.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("tree_gates: a and b must be [n, H] of one dtype, bf16 or float32")
+    a = a if a.stride(1) == 1 else a.contiguous()
+    b = b if b.stride(1) == 1 else b.contiguous()
+    a_log = a_log.float().contiguous()
+    dt_bias = dt_bias.float().contiguous()
+    parents = parents.to(torch.int64).contiguous()
+    beta = torch.empty(n, H, dtype=torch.float32, device=dev)
+    G = torch.empty(n, H, dtype=torch.float32, device=dev)
+    rc = _lib.lib().mfd_tree_gates(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                                   MFD_BF16 if a.dtype == torch.bfloat16 else MFD_F32, a_log.data_ptr(),
+                                   dt_bias.data_ptr(), parents.data_ptr(), n, H, beta.data_ptr(), G.data_ptr(),
+                                   ptr(status), stream_ptr(dev))
+    check(rc, "mfd_tree_gates")
+    return beta, G
 
 
 def tree_prep(x: torch.Tensor, conv_state: torch.Tensor, conv_index: torch.Tensor, conv_w: torch.Tensor,

@@ -14,6 +14,8 @@ restatement oracle/mfd_oracle.c through ctypes.  Floating-point paths are restat
   tree_gdn           tests/test_gdn_tree_math.py:29-60 (chunk form with ancestor mask, one
                      triangular solve) with the GQA key-head map of hf/tree_gdn_kernel.py:71, 101,
                      per-node states by the commit formula hf/qwen35_tree.py:134-137
+  compile_tree       hf/ddtree.py:317-357 (compile_ddtree_tree: verify ids, positions, additive tree mask)
+  tree_gates         hf/qwen35_tree.py:77-79 (beta, softplus decay, G = anc_f @ g)
   tree_prep          hf/tree_gdn_kernel.py:27-56 (_tree_prep: windowed conv through parent pointers,
                      SiLU rounded to bf16, l2norm + q scale); pinned against torch's causal conv1d on chains
 
@@ -290,6 +292,24 @@ def tree_gdn(q, k, v, g_cum, beta, s0, parents, emit_states=False):
     return u, o, states
 
 
+def commit_state(s0, u, k, G, path):
+    """The state at the deepest accepted node a = path[-1] (inference/hf/qwen35_tree.py:134-137) in float64:
+    S_a = e^{G_a} S0 + sum_{j on path} e^{G_a - G_j} k_j u_j^T, value head h reading key head h // (H / HK).
+    s0 [H, Dk, Dv], u [n, H, Dv], k [n, HK, Dk], G [n, H] -> [H, Dk, Dv]."""
+    s0 = np.asarray(s0, np.float64)
+    u = np.asarray(u, np.float64)
+    k = np.asarray(k, np.float64)
+    G = np.asarray(G, np.float64)
+    H, HK = u.shape[1], k.shape[1]
+    a = path[-1]
+    out = np.exp(G[a])[:, None, None] * s0
+    for j in path:
+        w = np.exp(G[a] - G[j])  # [H]
+        kk = k[j][np.arange(H) // (H // HK)]  # [H, Dk]
+        out += w[:, None, None] * kk[:, :, None] * u[j][:, None, :]
+    return out
+
+
 def gdn_recurrence(q, k, v, g, beta, s0, parents):
     """Node-by-node gated delta rule (tests/test_gdn_tree_math.py:38-44, fla layout S [Dk, Dv]):
     S_i = exp(g_i) S_p (I - beta_i k_i k_i^T)... written as S_i = e^{g_i}(S_p - beta_i k_i (k_i^T S_p)) +
@@ -314,6 +334,18 @@ def gdn_recurrence(q, k, v, g, beta, s0, parents):
             states[i, h] = s
             o[i, h] = s.T @ q[i, hk]
     return o, states
+
+
+def tree_gates(a, b, a_log, dt_bias, parents):
+    """inference/hf/qwen35_tree.py:77-79 in float64: beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)
+    (torch's softplus: x above 20), G = anc @ g with anc the ancestor-or-self matrix of the parents."""
+    a = np.asarray(a, np.float64)
+    x = a + np.asarray(dt_bias, np.float64)[None]
+    sp = np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20))))
+    g = -np.exp(np.asarray(a_log, np.float64))[None] * sp
+    beta = 1.0 / (1.0 + np.exp(-np.asarray(b, np.float64)))
+    G = visibility(list(parents)).astype(np.float64) @ g
+    return beta, G
 
 
 def bf16_round(x) -> np.ndarray:
@@ -347,6 +379,25 @@ def tree_prep(x, conv_state, conv_index, conv_w, num_k_heads, num_v_heads, head_
         return a / np.sqrt((a * a).sum(-1, keepdims=True, dtype=np.float32) + np.float32(1e-6), dtype=np.float32)
 
     return bf16_round(l2n(q) * np.float32(scale)), bf16_round(l2n(k)), bf16_round(v)
+
+
+def compile_tree(root, start, tokens, depths, vis, past, prev_start, prev_len, ids_buf, pos_buf, mask_buf,
+                 vis_buf, min_value):
+    """The HF verify inputs of one round (inference/hf/ddtree.py:317-357) written into numpy buffers in place:
+    the previous round's block of the additive mask reset to 0, ids = [root, tokens], positions = start +
+    [0, depths], the visibility copied, and the new block set to min_value except where visible (0).  ids_buf and
+    pos_buf [max_nodes], mask_buf [max_nodes, max_cols], vis_buf [max_nodes, max_nodes]."""
+    n = 1 + len(tokens)
+    if prev_len > 0:
+        mask_buf[:prev_len, prev_start:prev_start + prev_len] = 0
+    ids_buf[0] = root
+    ids_buf[1:n] = tokens
+    pos_buf[0] = start
+    pos_buf[1:n] = np.asarray(depths) + start
+    vis = np.asarray(vis, bool)
+    vis_buf[:n, :n] = vis
+    mask_buf[:n, past:past + n] = np.where(vis, 0, min_value)
+    return n
 
 
 def compact_tail(cache, past_length, keep):

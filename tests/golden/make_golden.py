@@ -10,7 +10,8 @@ Sources of truth, all the reference's own code (imported read-only, never copied
   - inference/hf/tree_build_ext.py's C++ builders (build_single / build_mixture / Tree.follow) and the
     SGLang patch's C++ build_trees, compiled from the reference sources by oracle/build_ref.py;
   - inference/hf/mode_attention.py `reference` (float32 masked SDPA);
-  - inference/hf/ddtree.py compile_ddtree_tree (the additive verify mask) + torch SDPA in float64;
+  - inference/hf/ddtree.py compile_ddtree_tree (the additive verify mask) + torch SDPA in float64, and the
+    verify inputs it writes over consecutive rounds (compile_tree.npz);
   - tests/test_gdn_tree_math.py's tree_case inputs and its node-by-node recurrence.
   - inference/hf/ddtree.py _compact_appended_window / compact_dynamic_cache (the commit step's cache
     compaction, its index_select path) on CPU tensors and a transformers DynamicCache.
@@ -219,6 +220,47 @@ def verify_attention_case():
          mask=mask.numpy(), out=out.float().numpy())
 
 
+def compile_tree_case():
+    """compile_ddtree_tree over consecutive rounds into the same buffers: each round's tree block overlaps the
+    previous one (the prefix advances by less than the previous tree), bf16 and float32 masks."""
+    gen = torch.Generator().manual_seed(31)
+    flat = {}
+    max_nodes, max_len = 24, 100
+    for d, dtype in enumerate((torch.bfloat16, torch.float32)):
+        ids_buf = torch.zeros(1, max_nodes, dtype=torch.long)
+        pos_buf = torch.zeros(1, max_nodes, dtype=torch.long)
+        mask_buf = torch.zeros(1, 1, max_nodes, max_len + max_nodes, dtype=dtype)
+        vis_buf = torch.zeros(max_nodes, max_nodes, dtype=torch.bool)
+        prev_start, prev_len, start = 0, 0, 40
+        for r, n in enumerate((17, 13, 21)):
+            parents = [-1] + [int(torch.randint(0, i, (1,), generator=gen)) for i in range(1, n)]
+            vis = torch.zeros(n, n, dtype=torch.bool)
+            depths = [0] * n
+            for i in range(n):
+                j = i
+                while j >= 0:
+                    vis[i, j] = True
+                    j = parents[j]
+                if i:
+                    depths[i] = depths[parents[i]] + 1
+            tokens = torch.randint(0, 1000, (n - 1,), generator=gen)
+            root = int(torch.randint(0, 1000, (1,), generator=gen))
+            pre = f"d{d}r{r}_"
+            flat.update({pre + "parents": np.array(parents, np.int64), pre + "tokens": tokens.numpy(),
+                         pre + "depths": np.array(depths[1:], np.int64), pre + "vis": vis.numpy(),
+                         pre + "root": np.int64(root), pre + "start": np.int64(start),
+                         pre + "prev": np.array([prev_start, prev_len], np.int64)})
+            _, _, _, prev_start, prev_len = ddtree.compile_ddtree_tree(
+                torch.tensor(root), start, tokens, torch.tensor(depths[1:], dtype=torch.long), vis, start, dtype,
+                torch.device("cpu"), ids_buf, pos_buf, mask_buf, vis_buf, prev_start, prev_len)
+            flat.update({pre + "ids": ids_buf.numpy().copy(), pre + "pos": pos_buf.numpy().copy(),
+                         pre + "mask_bits": mask_buf.view(torch.int16 if dtype == torch.bfloat16 else torch.int32)
+                         .numpy().copy(), pre + "vis_buf": vis_buf.numpy().copy()})
+            start += 1 + int(torch.randint(0, 4, (1,), generator=gen))
+    flat["dims"] = np.array([max_nodes, max_len], np.int64)
+    save("compile_tree.npz", **flat)
+
+
 def gdn_case():
     """tests/test_gdn_tree_math.py tree_case (seeds 0..2) and its node-by-node recurrence, float64."""
     flat = {}
@@ -295,6 +337,7 @@ if __name__ == "__main__":
     topk_rows()
     mode_attention_case()
     verify_attention_case()
+    compile_tree_case()
     gdn_case()
     tree_context_case()
     compact_case()

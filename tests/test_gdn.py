@@ -115,8 +115,10 @@ def test_tree_gdn_rejects_a_mask_that_is_not_a_tree():
 
 
 @pytest.mark.gpu
-def test_commit_state_matches_emitted_node_state():
-    from mfd_b200 import ops, qwen35_tree
+def test_commit_of_a_path_matches_emitted_node_state():
+    """mfd_gdn_commit at the end of a root path equals the state mfd_tree_gdn emits for that node, and both equal
+    the commit formula (oracle.commit_state, float64)."""
+    from mfd_b200 import ops
     n = 65
     parents = random_parents(n, 11)
     q, k, v, G, beta, s0 = gdn_inputs(n, 8, 4, 128, parents, 11)
@@ -127,8 +129,11 @@ def test_commit_state_matches_emitted_node_state():
     while parents[path[-1]] >= 0:
         path.append(int(parents[path[-1]]))
     path = path[::-1]
-    S = qwen35_tree.commit_state(s0.to(DEV), u, k.to(DEV), G.to(DEV), path)
+    S = s0.float().clone().to(DEV)
+    ops.gdn_commit([S], [u], [k.to(DEV)], [G.float().to(DEV)], path)
     torch.testing.assert_close(S, st[leaf], rtol=0, atol=1e-5)
+    ref = oracle.commit_state(s0.numpy(), u.cpu().numpy(), k.float().numpy(), G.float().numpy(), path)
+    np.testing.assert_allclose(S.cpu().numpy(), ref, rtol=0, atol=1e-4 * float(np.abs(ref).max()))
 
 
 # ------------------------------------------------------------------------------------------------ tree_prep
@@ -176,3 +181,24 @@ def test_tree_prep_vs_oracle(n, HK, H, D, seed):
     np.testing.assert_allclose(q.float().cpu().numpy(), rq, rtol=8e-3, atol=1e-6)
     np.testing.assert_allclose(k.float().cpu().numpy(), rk, rtol=8e-3, atol=1e-6)
     np.testing.assert_allclose(v.float().cpu().numpy(), rv, rtol=8e-3, atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n,H,dtype", [(65, 32, torch.bfloat16), (257, 16, torch.float32), (1, 4, torch.bfloat16)])
+def test_tree_gates_vs_oracle(n, H, dtype):
+    """beta, the softplus log decay and its sum along each root path (mfd_tree_gates) against the reference's
+    formulas in float64 (oracle.tree_gates: sigmoid, -exp(A_log) softplus(a + dt_bias), G = anc @ g); inputs reach
+    softplus's linear branch (a + dt_bias > 20)."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(n + H)
+    parents = random_parents(n, n)
+    a = (torch.randn(n, H, generator=g) * 3).to(dtype)
+    a[0, 0] = 30.0
+    b = torch.randn(n, H, generator=g).to(dtype)
+    a_log = torch.randn(H, generator=g) * 0.5
+    dt_bias = torch.randn(H, generator=g)
+    beta, G = ops.tree_gates(a.to(DEV), b.to(DEV), a_log.to(DEV), dt_bias.to(DEV),
+                             torch.from_numpy(np.asarray(parents)).to(DEV))
+    rb, rG = oracle.tree_gates(a.float().numpy(), b.float().numpy(), a_log.numpy(), dt_bias.numpy(), parents)
+    np.testing.assert_allclose(beta.cpu().numpy(), rb, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(G.cpu().numpy(), rG, rtol=1e-4, atol=1e-4)

@@ -172,8 +172,8 @@ def test_conv_commit_matches_window_gather():
 
 
 def test_qwen35_commit_end_to_end():
-    """qwen35_tree.commit on a cache of two GDN layers: states and conv windows as the reference's commit computes
-    them (its torch formula, here qwen35_tree.commit_state and a gather), then compact_attention is called."""
+    """qwen35_tree.commit on a cache of two GDN layers: states as the reference's commit formula gives them
+    (oracle.commit_state, float64) and conv windows as its gather, then compact_attention is called."""
     from mfd_b200 import qwen35_tree
     from tests.test_gdn import gdn_inputs, random_parents
     n, H, HK, D, kernel = 33, 4, 2, 128, 4
@@ -203,14 +203,16 @@ def test_qwen35_commit_end_to_end():
         layer.recurrent_states = s0[None].clone().to(DEV)
         layer.conv_states = torch.randn(1, conv_dim, kernel, generator=g).bfloat16().to(DEV)
         cache.layers[li] = layer
-        ctx.stash[li] = (u.to(DEV), k.bfloat16().to(DEV), G.float().to(DEV), x.to(DEV))
+        ctx.records[li] = qwen35_tree._LayerRecord(u=u.to(DEV), k=k.bfloat16().to(DEV), G=G.float().to(DEV),
+                                                   x=x.to(DEV))
         win = ctx.conv_index_cpu[accepted[-1]]
         conv_old = layer.conv_states[0].cpu()
-        expect[li] = (qwen35_tree.commit_state(s0.to(DEV), u.to(DEV), k.bfloat16().to(DEV), G.to(DEV), accepted).cpu(),
+        s_ref = oracle.commit_state(s0.numpy(), u.numpy(), k.bfloat16().float().numpy(), G.float().numpy(), accepted)
+        expect[li] = (torch.from_numpy(s_ref).float(),
                       torch.stack([conv_old[:, i] if i < kernel else x[i - kernel] for i in win], dim=-1))
     called = []
     qwen35_tree.commit(cache, ctx, accepted, 100, lambda c, past, acc: called.append((past, list(acc))))
-    assert called == [(100, accepted)] and ctx.stash == {}
+    assert called == [(100, accepted)] and ctx.records == {}
     for li, (s_ref, c_ref) in expect.items():
         torch.testing.assert_close(cache.layers[li].recurrent_states[0].cpu(), s_ref, rtol=0,
                                    atol=1e-5 * float(s_ref.abs().max()))
