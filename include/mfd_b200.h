@@ -213,9 +213,13 @@ int mfd_paged_mode_attention(const void* q, int64_t sq_t, int64_t sq_h, const vo
  * bf16 (node stride sv); g_cum, beta [n, H] float32 (node strides sg, sb; g_cum = log decay summed along the root
  * path); s0 [H, Dk, Dv] float32; anc [n, n] int8 (row stride sa), row i = ancestors of i and i, nodes in
  * topological order.  Value head h reads key head h / (H / HK).  Outputs u, o [n, H, Dv] float32 and, if
- * states != null, states [n, H, Dk, Dv] float32.  status (optional, device int): 0, or 1 when anc is not the
- * ancestor matrix of a topologically ordered tree (outputs then unspecified).
- * Limits: n <= 128, Dk, Dv <= 128 and multiples of 4.
+ * states != null, states [n, H, Dk, Dv] float32.  status (optional, device int): 0; 1 when anc is not the
+ * ancestor matrix of a topologically ordered tree; MFD_ERR_CAPACITY when the tree's ancestor pairs (the sum over
+ * nodes of depth + 1) exceed what the kernel holds at this n (any tree of up to 128 nodes fits; 257 nodes: 6.7
+ * thousand pairs); 3 if a bounded wait gave up.  Outputs are unspecified unless the status is 0.
+ * Limits: n <= 384, Dk <= 128 and a multiple of 8, Dv a multiple of 4 (<= 128 when states are written).
+ * The contractions run on the tcgen05 tensor cores (S0^T k, S0^T q and the Gram products per 128-node tile; one
+ * path contraction per node and head for the states).
  * Replaces: inference/hf/tree_gdn_kernel.py:153-171 (tree_gdn: _tree_kkt, fla solve_tril, _tree_u), and the
  *           state formula of inference/hf/qwen35_tree.py:134-137 evaluated for every node.
  */

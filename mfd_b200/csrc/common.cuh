@@ -131,6 +131,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// SMs of the current device (host).
+inline int current_sm_count() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
 // online (max, sum of exp(x - max)) pair merge; -inf maxima carry a zero sum
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
     float mn = fmaxf(m, m2);

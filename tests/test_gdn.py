@@ -61,8 +61,11 @@ def check_against_oracle(q, k, v, G, beta, s0, parents, emit_states):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("n,H,HK,D,seed", [(65, 32, 16, 128, 0), (64, 32, 16, 128, 1), (37, 4, 4, 64, 2),
-                                          (128, 8, 2, 128, 3), (1, 2, 1, 128, 4)])
+                                          (128, 8, 2, 128, 3), (1, 2, 1, 128, 4), (200, 8, 4, 128, 6),
+                                          (257, 32, 16, 128, 9), (257, 8, 4, 128, 10), (384, 4, 2, 128, 11)])
 def test_tree_gdn_vs_oracle(n, H, HK, D, seed):
+    """Odd seeds check u and o, even seeds the per-node states too; 200, 257 and 384 nodes span two and three
+    128-node tiles (257 = a budget-256 tree with its root, the size the reference's guide times)."""
     parents = random_parents(n, seed)
     check_against_oracle(*gdn_inputs(n, H, HK, D, parents, seed), parents, emit_states=(seed % 2 == 0))
 
@@ -74,6 +77,20 @@ def test_tree_gdn_chain_and_star():
     check_against_oracle(*gdn_inputs(n, 4, 2, 128, chain, 7), chain, emit_states=True)
     star = np.array([-1] + [0] * (n - 1), np.int64)
     check_against_oracle(*gdn_inputs(n, 4, 2, 128, star, 8), star, emit_states=True)
+
+
+@pytest.mark.gpu
+def test_tree_gdn_reports_ancestor_pairs_beyond_capacity():
+    """A 257-node chain has 33153 ancestor pairs, more than the u/o kernel holds at that size: the status word says
+    MFD_ERR_CAPACITY (4) instead of computing from a truncated path table."""
+    from mfd_b200 import ops
+    n = 257
+    chain = np.arange(-1, n - 1, dtype=np.int64)
+    q, k, v, G, beta, s0 = gdn_inputs(n, 2, 1, 128, chain, 12)
+    status = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    ops.tree_gdn(q.to(DEV), k.to(DEV), v.to(DEV), G.to(DEV), beta.to(DEV), s0.to(DEV), anc8_of(chain).to(DEV),
+                 status=status)
+    assert int(status.item()) == 4
 
 
 @pytest.mark.gpu
