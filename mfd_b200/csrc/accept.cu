@@ -47,38 +47,9 @@ __device__ __forceinline__ float exp32_rule(float y) {
     q = __fmaf_rn(q, r, 1.0f);
     return ok ? __uint_as_float(__float_as_uint(q) + ((uint32_t)ni << 23)) : 0.0f;
 }
-// Packed float32 pairs (Blackwell f32x2 arithmetic): every lane of add / sub / mul / fma .rn.f32x2 is the IEEE
-// round-to-nearest result of the scalar operation, so exp32_rule_x2 returns, per lane, exactly exp32_rule's bits
-// with half the floating-point instructions.
-__device__ __forceinline__ uint64_t pk2(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t dup2(float a) { return pk2(a, a); }
+// The packed float32 pair operations (pk2, add2, sub2, mul2, fma2, dup2; common.cuh) round every lane like the
+// scalar operation, so exp32_rule_x2 below returns, per lane, exactly exp32_rule's bits with half the
+// floating-point instructions.
 // exp32_rule((x0 - m) * c) and exp32_rule((x1 - m) * c), the operations of exp32_rule on both lanes at once (a lane
 // whose argument is not above -87 is computed on and then replaced by 0, as exp32_rule returns).  UNIT: c is 1, so
 // the product is the difference itself (multiplying by 1 is exact) and is not computed.

@@ -82,6 +82,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&r)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) r[i] = __uint_as_float(u[i]);
 }
+// tmem_ld32 without the wait: several loads are issued back to back and tmem_ld_wait(...) ends them together
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&u)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]),
+          "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]),
+          "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+        : "r"(taddr));
+}
+// wait for the issued TMEM loads; every register of u then passes through an empty volatile asm after the wait, so
+// no use of a loaded value is scheduled before it (volatile asm statements keep their order)
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&u)[N][32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int c = 0; c < N; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(u[c][i]));
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"

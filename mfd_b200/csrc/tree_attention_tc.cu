@@ -5,25 +5,27 @@
 // custom mask of sglang-v0.5.22-mfd.patch:1625-1703).  The mask is read from the builder's ancestor bitsets.
 //
 // Rows: the G query heads sharing a KV head are packed as r = node * G + g (260 rows for 65 nodes x 4 heads), so
-// a key tile feeds G x n rows.  One CTA per (request, KV head, key split, 128-row M-tile); the M-tiles of one
-// split are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.  With per-request prefix
-// lengths (up to 64 requests) the CTAs of the longest requests are launched first, so the short ones fill the tail.
+// a key tile feeds G x n rows.  One CTA per (request, KV head, key split, 128-row M-tile); the M-tiles of one split
+// are adjacent CTAs, so their shared K/V tiles come from L2 after the first read.  With per-request prefix lengths
+// (up to 64 requests) the CTAs of the longest requests are launched first, so the short ones fill the tail.
 //
-// The kernel is a template over its tile configuration (Cfg below); the launched one has 128-key tiles, a 3-stage
-// ring, 16 softmax warps and one CTA per SM.  Warp roles (576 threads):
-//   warp 0       producer: Q once by TMA, then K and V tiles into the ring (128-byte swizzle, the canonical UMMA
-//                K-major / MN-major layouts; no multicast) -- by TMA from dense [bs, Hkv, S, 128] caches, or, in
-//                paged mode (SGLang's paged mode attention), gathered row by row with 16-byte cp.async through the
-//                request's req_to_token row into the same swizzled layout
+// The kernel is a template over its tile configuration (Cfg below); the launched one has 128-key tiles, 3-stage K
+// and V ring, 8 softmax warps and one CTA per SM.  Warp roles (320 threads):
+//   warp 0       producer: Q once by TMA, then K and V tiles into their rings (128-byte swizzle, the canonical UMMA
+//                K-major / MN-major layouts; no multicast) -- by TMA from dense [bs, Hkv, S, 128] caches (with an
+//                L2 prefetch of the tiles kPrefetchAhead ahead), or, in paged mode (SGLang's paged mode attention),
+//                gathered row by row with 16-byte cp.async through the request's req_to_token row into the same
+//                swizzled layout
 //   warp 1       MMA issuer: S[i%2] = Q K_i^T (M=128, N=tile keys, K=16 x 8) into TMEM, then O += P_{i-1} V_{i-1}
 //                (M=128, N=128, A = P read from TMEM, V MN-major), so the scores of tile i are computed while the
 //                softmax works on tile i-1
-//   warps 2..    softmax: the PARTS warps of TMEM lane quarter q each take 32 of a tile's key columns and 128 /
-//                PARTS of O's columns (row max and, at the end, row sum exchanged through shared memory):
-//                tcgen05.ld of S, mask (only tiles reaching the tree keys or the split end), exp2, bf16 P written
-//                back over S in TMEM; lazy O rescale in TMEM only when a row's running max grows by more than 2^8.
-//                A quarter whose 32 rows are all padding (the last M-tile holds 4 of 128 rows for 65 x 4) keeps
-//                only the barrier protocol.  Epilogue through a shared-memory stage so every store is coalesced.
+//   warps 2..    softmax: the PARTS warps of TMEM lane quarter q each take 128 / PARTS of a tile's key columns and
+//                of O's columns (row max and, at the end, row sum exchanged through shared memory): tcgen05.ld of
+//                S, mask (only tiles reaching the tree keys or the split end), exp2 (a third of them by a cubic on
+//                the FMA pipe, the rest on the MUFU unit), bf16 P written back over S in TMEM; lazy O rescale in
+//                TMEM only when a row's running max grows by more than 2^8.  A quarter whose 32 rows are all padding
+//                (the last M-tile holds 4 of 128 rows for 65 x 4) keeps only the barrier protocol.  Epilogue
+//                through a shared-memory stage so every store is coalesced.
 // Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
 // merges all splits and writes bf16 out.  With one split the CTA writes out directly.
 //
@@ -44,11 +46,16 @@ constexpr int D = 128;
 constexpr int kSmemMax = 227 * 1024;  // the per-block opt-in maximum
 constexpr int kSmemPerSm = 228 * 1024;  // per SM, of which 1 KB per resident block is reserved
 
-// A kernel configuration: keys per tile, K/V ring depth, softmax warps per TMEM lane quarter (each takes 32 of a
-// tile's key columns and D / PARTS of O's columns), and resident CTAs per SM.  The launched one, CfgWide =
-// Cfg<128, 3, 4, 1>: one CTA per SM, 227 KB of shared memory, 512 TMEM columns.  (Cfg<64, 2, 2, 2>, two CTAs per
-// SM with 99 KB and 256 TMEM columns each, passes the same tests but ran the 32-request verify step's attention in
-// 348 us against 280 us.)
+// A kernel configuration: keys per tile, K/V ring depth, softmax warps per TMEM lane quarter (each takes
+// KT / PARTS of a tile's key columns and D / PARTS of O's columns), resident CTAs per SM.  TMEM: O at columns
+// [0, 128) and two S buffers after it (S of key tile i in buffer i % 2), so the scores of tile i are computed while
+// the softmax works on tile i - 1.
+// Launched: CfgRow = Cfg<128, 3, 2, 1>, one CTA per SM, 512 TMEM columns.  Measured alternatives (attention of the
+// 256-request verify step, L2 flushed): four warps per row quarter (Cfg<128, 3, 4, 1>) 2127 us against 2030 us for
+// two; one warp per row quarter (each thread a whole 128-key row) 2056 us; two M-tiles per CTA sharing each K / V
+// tile with the MMA warp alternating between them (2 stages) 2221 to 2561 us; separate K and V rings (a K stage
+// refilled as soon as its scores complete) 2146 us; Cfg<64, 2, 2, 2> (two CTAs per SM)
+// was slower still at 32 requests (348 against 280 us).
 template <int KT, int STAGES, int PARTS, int MINB>
 struct Cfg {
     static constexpr int kKt = KT;
@@ -58,7 +65,8 @@ struct Cfg {
     static constexpr int kOCols = D / PARTS;  // O columns each part rescales and stores
     static constexpr int kSoftmaxThreads = 128 * PARTS;
     static constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, then the softmax warps
-    static constexpr int kSCol = 128;  // S[b] at column kSCol + KT b; P[b] (bf16 pairs) over its first KT / 2 columns
+    // S buffer b at column kSCol + KT b; P (bf16 pairs) over its first KT / 2 columns
+    static constexpr int kSCol = 128;
     static constexpr int kTmemCols = kSCol + 2 * KT <= 256 ? 256 : 512;
     static constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
     static constexpr int kKVBytes = KT * D * 2;   // [2 d-halves][KT keys][128 B]
@@ -67,7 +75,8 @@ struct Cfg {
     static constexpr int kOffV = kOffK + STAGES * kKVBytes;
     static constexpr int kOffX = kOffV + STAGES * kKVBytes;  // row maxima / sums exchanged by the parts of a row
     static constexpr int kOffBar = kOffX + PARTS * kM * 4;
-    static constexpr int kSmemUsed = kOffBar + 128;  // + barriers, TMEM address, flags
+    static constexpr int kBarArea = 256;
+    static constexpr int kSmemUsed = kOffBar + kBarArea;  // + barriers, TMEM address, flags
     static constexpr int kSmemCap = MINB == 1 ? kSmemMax : kSmemPerSm / MINB - 1024;
     // the 128-byte-swizzled TMA destinations need a 1024-byte aligned base: the slack that fits is reserved and
     // the kernel checks at entry that the base's misalignment is within it
@@ -75,21 +84,24 @@ struct Cfg {
     static constexpr int kSmemBytes = kSmemUsed + kSmemSlack;
     // barrier slots
     static constexpr int kBarQ = 0;
-    static constexpr int kBarKVFull = 1;                      // + stage
-    static constexpr int kBarKVEmpty = kBarKVFull + STAGES;   // + stage
-    static constexpr int kBarSFull = kBarKVEmpty + STAGES;    // + buffer
-    static constexpr int kBarPFull = kBarSFull + 2;  // + buffer (P written into S[b]; also frees S[b] for tile + 2)
-    static constexpr int kBarPV = kBarPFull + 2;     // + buffer: P V of tile j completes kBarPV + j % 2
+    static constexpr int kBarKVFull = 1;                     // + stage
+    static constexpr int kBarKVEmpty = kBarKVFull + STAGES;  // + stage
+    static constexpr int kBarSFull = kBarKVEmpty + STAGES;   // + S buffer
+    static constexpr int kBarPFull = kBarSFull + 2;  // + S buffer (P written into it; frees it for the next scores)
+    static constexpr int kBarPV = kBarPFull + 2;     // + S buffer: the P V that read it completes
     static constexpr int kNumBars = kBarPV + 2;
-    static_assert(KT / PARTS == 32, "each softmax warp takes 32 key columns");
+    static_assert(KT % (32 * PARTS) == 0, "each softmax warp takes a multiple of 32 key columns");
     static_assert(kOCols % 32 == 0, "O columns per part");
     static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemCap, "shared memory");
     static_assert(STAGES * kKVBytes >= kM * 256, "the epilogue stages 128 bf16 rows in the K ring");
-    static_assert(8 * kNumBars + 8 <= 128, "barrier area");
+    static_assert(8 * kNumBars + 8 <= kBarArea, "barrier area");
     static_assert(MINB * kThreads <= 2048, "threads per SM");
 };
-using CfgWide = Cfg<128, 3, 4, 1>;
+using CfgRow = Cfg<128, 3, 2, 1>;
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
+// K / V tiles are prefetched into L2 this many tiles before their load into the ring, so the ring's loads see L2
+// latency instead of DRAM latency (a stage is refilled less than one tile period before its scores are needed)
+constexpr int kPrefetchAhead = 4;
 
 // ------------------------------------------------------------------ TMA (the tcgen05 wrappers are in tcgen05.cuh)
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
@@ -100,18 +112,51 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
         : "memory");
 }
-// named barriers: 1 = the softmax threads, 2 + q = the PARTS warps of TMEM lane quarter q
+// L2 prefetch of one tile of a tensor map (no shared-memory destination, no completion to wait for)
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(c0),
+                 "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+// 2^x on the FMA pipe, both lanes of a packed pair, for a share of the softmax's exponentials (the MUFU unit's
+// ex2 alone would bound the softmax).  x = n + f with n = round(x) (adding 1.5 * 2^23 rounds to an integer) and
+// f in [-1/2, 1/2]; 2^f by the cubic p(f) = 1 + f (c1 + f (c2 + f c3)), coefficients fitted to 2^f on [-1/2, 1/2]
+// for the least maximum relative error (iteratively reweighted least squares, Lawson's method, on 20001 points;
+// the constant term fixed at 1): 1.02e-4, far below the bf16 rounding (2^-9) P gets next.  2^n enters as n << 23
+// added to p's bits (the bits of the rounded sum are 0x4B400000 + n, and 0x4B400000 << 23 vanishes modulo 2^32).
+// x is first clamped to -127: there f = 0 and p = 1 exactly, so the bits are those of +0 -- masked scores (-inf)
+// and NaN give 0 as ex2.approx.ftz gives for -inf.
+constexpr float kExpC1 = 0.6932827234268188f, kExpC2 = 0.24220797419548035f, kExpC3 = 0.055007610470056534f;
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+    float x0, x1;
+    upk2(x, x0, x1);
+    const uint64_t xc = pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f));
+    const uint64_t t = add2(xc, dup2(12582912.f));
+    const uint64_t f = sub2(xc, sub2(t, dup2(12582912.f)));
+    const uint64_t q = fma2(fma2(fma2(dup2(kExpC3), f, dup2(kExpC2)), f, dup2(kExpC1)), f, dup2(1.f));
+    float q0, q1, t0, t1;
+    upk2(q, q0, q1);
+    upk2(t, t0, t1);
+    return pk2(__uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23)),
+               __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23)));
+}
+// every kPolyEvery-th exponential pair of a row's keys goes to exp2_poly2, the rest to ex2.approx
+constexpr int kPolyEvery = 3;
+
+// named barriers: 1 = the softmax threads, 2 + q = the PARTS warps of TMEM lane quarter q (one warp: a warp sync)
 template <int PARTS>
 __device__ __forceinline__ void softmax_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(128 * PARTS) : "memory");
 }
 template <int PARTS>
 __device__ __forceinline__ void quarter_sync(int quarter) {
-    asm volatile("bar.sync %0, %1;" ::"r"(2 + quarter), "n"(32 * PARTS) : "memory");
+    if (PARTS == 1) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(2 + quarter), "n"(32 * PARTS) : "memory");
 }
 // the same barrier, returning the AND of v over the quarter's threads (so its warps leave a loop together)
 template <int PARTS>
 __device__ __forceinline__ bool quarter_sync_and(int quarter, bool v) {
+    if (PARTS == 1) return __all_sync(MFD_FULL_MASK, v);
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred pi, po;\n\tsetp.ne.b32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
@@ -205,6 +250,14 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         *shared_flag = 0;
         mbar_fence_init();
     }
+    auto prefetch_kv = [&](int i) {
+        if (i >= ntiles) return;
+        const int key0 = k_lo + i * kKt;
+        for (int h = 0; h < 2; ++h) {
+            tma_prefetch_4d(&tmk, h * 64, key0, hk, b);
+            tma_prefetch_4d(&tmv, h * 64, key0, hk, b);
+        }
+    };
     auto load_kv = [&](int i) {
         const int st = i % kStages;
         const int key0 = k_lo + i * kKt;
@@ -282,10 +335,12 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         const int nodes_per_tile = kM / p.G;
         mbar_expect_tx(&bars[kBarQ], kQBytes);
         for (int h = 0; h < 2; ++h)
-            tma_load_4d(sbase + kOffQ + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G, mtile * nodes_per_tile,
-                        b);
-        if (!p.paged)
+            tma_load_4d(sbase + kOffQ + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G,
+                        mtile * nodes_per_tile, b);
+        if (!p.paged) {
             for (int i = 0; i < min(kStages, ntiles); ++i) load_kv(i);
+            for (int i = kStages; i < kStages + kPrefetchAhead; ++i) prefetch_kv(i);
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
@@ -328,8 +383,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
             asm volatile("cp.async.wait_group 0;" ::: "memory");  // nothing in flight when the warp leaves
         } else if (lane == 0) {
             for (int i = kStages; i < ntiles && ok; ++i) {
+                prefetch_kv(i + kPrefetchAhead);
                 ok &= mbar_wait(&bars[kBarKVEmpty + i % kStages], ((i / kStages) - 1) & 1, kTries);
-                load_kv(i);
+                if (ok) load_kv(i);
             }
         }
     } else if (warp == 1) {
@@ -337,136 +393,162 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         if (lane == 0) {
             constexpr uint32_t kIdescS = idesc_bf16(kM, kKt, 0);
             constexpr uint32_t kIdescO = idesc_bf16(kM, D, 1);
-            auto issue_pv = [&](int j) {
-                const int bj = j & 1, stj = j % kStages;
-                ok &= mbar_wait(&bars[kBarPFull + bj], (j >> 1) & 1, kTries);
-                tc_fence_after();
-                const uint32_t vaddr = sbase + kOffV + stj * kKVBytes;
-#pragma unroll
-                for (int ks = 0; ks < kKt / 16; ++ks)  // P: 16 keys = 8 columns of bf16 pairs per step
-                    umma_ts(tmem, tmem + kSCol + bj * kKt + ks * 8, sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024),
-                            kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
-                umma_commit(&bars[kBarPV + bj]);
-                umma_commit(&bars[kBarKVEmpty + stj]);
-            };
-            if (ntiles > 0) ok &= mbar_wait(&bars[kBarQ], 0, kTries);
-            for (int i = 0; i < ntiles && ok; ++i) {
-                const int st = i % kStages, bi = i & 1;
-                // S[bi] last held P(i-2), which the P V issued in the previous iteration consumed (tensor-core
-                // operations of this thread execute in order)
+            // S(i) = Q K_i^T into S buffer i % 2
+            auto issue_qk = [&](int i) {
+                const int st = i % kStages, sb = i & 1;
                 ok &= mbar_wait(&bars[kBarKVFull + st], (i / kStages) & 1, kTries);
                 tc_fence_after();
                 const uint32_t kaddr = sbase + kOffK + st * kKVBytes;
+                const uint32_t qaddr = sbase + kOffQ;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
                     const uint32_t qoff = (uint32_t)((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
                     const uint32_t koff = (uint32_t)((ks >> 2) * (kKVBytes / 2) + (ks & 3) * 32);
-                    umma(tmem + kSCol + bi * kKt, sdesc(sbase + kOffQ + qoff, 16, 1024), sdesc(kaddr + koff, 16, 1024),
-                         kIdescS, ks > 0);
+                    umma(tmem + kSCol + sb * kKt, sdesc(qaddr + qoff, 16, 1024), sdesc(kaddr + koff, 16, 1024), kIdescS,
+                         ks > 0);
                 }
-                umma_commit(&bars[kBarSFull + bi]);
-                if (i >= 1) issue_pv(i - 1);
+                umma_commit(&bars[kBarSFull + sb]);
+            };
+            // O += P(j) V_j once the softmax published P(j); the K/V stage is released when it completes
+            auto issue_pv = [&](int j) {
+                const int st = j % kStages, sb = j & 1;
+                ok &= mbar_wait(&bars[kBarPFull + sb], (j >> 1) & 1, kTries);
+                tc_fence_after();
+                const uint32_t vaddr = sbase + kOffV + st * kKVBytes;
+#pragma unroll
+                for (int ks = 0; ks < kKt / 16; ++ks)  // P: 16 keys = 8 columns of bf16 pairs per step
+                    umma_ts(tmem, tmem + kSCol + sb * kKt + ks * 8, sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024),
+                            kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                umma_commit(&bars[kBarPV + sb]);
+                umma_commit(&bars[kBarKVEmpty + st]);
+            };
+            if (ntiles > 0) ok &= mbar_wait(&bars[kBarQ], 0, kTries);
+            // scores of tile i while the softmax works on tile i - 1 (two S buffers); the stage of tile i - 1 is
+            // released when its P V completes.  S[i % 2] last held P(i - 2),
+            // which the P V issued in the previous iteration consumed (tensor-core operations of this thread
+            // execute in order).
+            for (int i = 0; i < ntiles && ok; ++i) {
+                issue_qk(i);
+                if (i >= 1 && ok) issue_pv(i - 1);
             }
             if (ntiles > 0 && ok) issue_pv(ntiles - 1);
         }
     } else {
         // ---------------------------------------------------------------- softmax warps
-        // warp w (2..17): TMEM lane quarter w % 4, key columns [32 part, 32 part + 32) of each 128-key tile with
+        // warp w: TMEM lane quarter w % 4, key columns [kCols part, kCols part + kCols) of each tile with
         // part = (w - 2) / 4; the kParts warps of a quarter exchange their row maxima (and at the end their row
-        // sums) through shared memory
+        // sums) through shared memory.
         const int quarter = warp & 3;
         const int part = (warp - 2) >> 2;
         const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
-        const int r = row0 + rt;             // packed row
-        const bool live = r < nrows;
-        const int node = live ? r / p.G : 0;
-        const uint64_t* anc_row = p.anc + ((size_t)(p.paged ? 0 : b) * p.n + node) * p.words;  // paged: shared
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [kParts][128 rows]
-        const int c_lo = part * 32;      // this warp's 32 of the tile's kKt key columns
+        constexpr int kCols = kKt / kParts, kChunks = kCols / 32;
+        const int c_lo = part * kCols;   // this warp's kCols of the tile's kKt key columns
         const int o_lo = part * kOCols;  // and its kOCols of O's 128 columns
         const float sc = p.scale_log2;
         float m_run = -INFINITY, l_run = 0.f;
         // a quarter whose 32 rows are all padding keeps only the barrier protocol: it leaves its TMEM rows as they
         // are, and the P V rows they feed (rows are independent in the MMA) are never stored
         const bool quarter_live = row0 + quarter * 32 < nrows;
-        for (int i = 0; i < ntiles; ++i) {
-            const int bi = i & 1;
+        for (int i = 0; i < ntiles && ok; ++i) {
             const int key0 = k_lo + i * kKt;
-            const uint32_t s_tm = tmem + lane_off + kSCol + bi * kKt;
-            ok &= mbar_wait(&bars[kBarSFull + bi], (i >> 1) & 1, kTries);
+            const int sb = i & 1;
+            const uint32_t s_tm = tmem + lane_off + kSCol + sb * kKt;
+            ok &= mbar_wait(&bars[kBarSFull + sb], (i >> 1) & 1, kTries);
             tc_fence_after();
             if (key0 + kKt > k_hi) {
-                // the tile runs past this split's keys: its rows from k_hi on hold whatever the caller's buffer
-                // has beyond the request's keys (any bits, NaN included).  Their P is 0, but 0 * NaN is NaN in the
-                // P V product, so those V rows are cleared before P is published (the tile landed before S(i) was
-                // computed, and P V (i) is issued only after every softmax warp has arrived below).  Each key row
-                // is 128 contiguous bytes per d-half, whatever the swizzle order of its 16-byte granules.
+                // the tile runs past this split's keys: its rows from k_hi on hold whatever the caller's buffer has
+                // beyond the request's keys (any bits, NaN included).  Their P is 0, but 0 * NaN is NaN in the P V
+                // product, so those V rows are cleared before P is published (the tile landed before S(i) was
+                // computed, and P V (i) is issued only after every softmax warp has arrived below).  Each key row is
+                // 128 contiguous bytes per d-half, whatever the swizzle order of its 16-byte granules.
                 const int r0 = k_hi > key0 ? k_hi - key0 : 0;
                 unsigned char* vt = smem + kOffV + (i % kStages) * kKVBytes;
                 for (int g = threadIdx.x - 64; g < (kKt - r0) * 16; g += kSoftmaxThreads) {
                     const int rr = r0 + (g >> 4), h = (g >> 3) & 1, c = g & 7;
                     *reinterpret_cast<uint4*>(vt + h * (kKVBytes / 2) + rr * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores' reads
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
             }
             if (!quarter_live) {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
-                if (!__all_sync(MFD_FULL_MASK, ok)) break;
+                if (lane == 0) mbar_arrive(&bars[kBarPFull + sb]);
+                ok = __all_sync(MFD_FULL_MASK, ok);
                 continue;
             }
-            float s[32];
-            tmem_ld32(s_tm + c_lo, s);
+            // this part's kCols scores of the row: kChunks TMEM loads in flight together
+            uint32_t sraw[kChunks][32];
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) tmem_ld32_issue(s_tm + c_lo + 32 * c, sraw[c]);
+            tmem_ld_wait(sraw);
+            float s[kChunks][32];
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) s[c][j] = __uint_as_float(sraw[c][j]);
             const bool fast = key0 + kKt <= prefix && key0 + kKt <= k_hi;
             if (!fast) {
-                // visibility of this thread's 32 keys as a bitmask: prefix keys, then the row's ancestor bits for
-                // the tree keys (two bitset words funnel-shifted into place), all cut at the split end
-                const int kb = key0 + c_lo;  // first key of this part
-                const int t0 = kb - prefix;  // its tree index (negative: prefix keys come first)
-                uint64_t vis;
-                if (t0 <= -64) {
-                    vis = ~0ull;
-                } else {
-                    const int w = t0 >> 6;  // floor division: word holding tree index t0 (t0 >= -63)
-                    const int sh = t0 & 63;
-                    const uint64_t lo = (w >= 0 && w < p.words) ? __ldg(anc_row + w) : 0ull;
-                    const uint64_t hi = (w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull;
-                    uint64_t tree = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;  // bit j: tree index t0 + j
-                    if (t0 < 0) {  // the first -t0 keys are prefix keys
-                        const int np = -t0;
-                        tree = hi << np;
-                        vis = tree | ((1ull << np) - 1ull);
-                    } else {
-                        vis = tree;
-                    }
-                }
-                const int live_keys = k_hi - kb;  // keys of this part before the split end
-                if (live_keys < 32) vis &= live_keys <= 0 ? 0ull : ((1ull << live_keys) - 1ull);
+                const int r = row0 + rt;  // packed row
+                const int node = r < nrows ? r / p.G : 0;
+                const uint64_t* anc_row = p.anc + ((size_t)(p.paged ? 0 : b) * p.n + node) * p.words;  // paged:
+                                                                                                       // shared
 #pragma unroll
-                for (int j = 0; j < 32; ++j) s[j] = ((vis >> j) & 1ull) ? s[j] : -INFINITY;
+                for (int c = 0; c < kChunks; ++c) {
+                    // visibility of 32 keys as a bitmask: prefix keys, then the row's ancestor bits for the
+                    // tree keys (two bitset words funnel-shifted into place), all cut at the split end
+                    const int kb = key0 + c_lo + 32 * c;  // first key of this chunk
+                    const int t0 = kb - prefix;             // its tree index (negative: prefix keys come first)
+                    uint64_t vis;
+                    if (t0 <= -64) {
+                        vis = ~0ull;
+                    } else {
+                        const int w = t0 >> 6;  // floor division: word holding tree index t0 (t0 >= -63)
+                        const int sh = t0 & 63;
+                        const uint64_t lo = (w >= 0 && w < p.words) ? __ldg(anc_row + w) : 0ull;
+                        const uint64_t hi = (w + 1 >= 0 && w + 1 < p.words) ? __ldg(anc_row + w + 1) : 0ull;
+                        uint64_t tree = sh ? ((lo >> sh) | (hi << (64 - sh))) : lo;  // bit j: tree index t0 + j
+                        if (t0 < 0) {  // the first -t0 keys are prefix keys
+                            const int np = -t0;
+                            tree = hi << np;
+                            vis = tree | ((1ull << np) - 1ull);
+                        } else {
+                            vis = tree;
+                        }
+                    }
+                    const int live_keys = k_hi - kb;  // keys of this chunk before the split end
+                    if (live_keys < 32) vis &= live_keys <= 0 ? 0ull : ((1ull << live_keys) - 1ull);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) s[c][j] = ((vis >> j) & 1ull) ? s[c][j] : -INFINITY;
+                }
             }
             float mx;
-            {  // the raw scores' maximum as a tree (scaling by sc > 0 keeps the order: max(s) * sc = max(s * sc))
-                float t[16];
+            {  // the raw scores' maximum as a tree (scaling by sc > 0 keeps the order: max(s) sc = max(s sc))
+                float u[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) t[j] = fmaxf(s[j], s[j + 16]);
+                for (int j = 0; j < 16; ++j) u[j] = fmaxf(s[0][j], s[0][j + 16]);
+#pragma unroll
+                for (int c = 1; c < kChunks; ++c)
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) u[j] = fmaxf(u[j], fmaxf(s[c][j], s[c][j + 16]));
 #pragma unroll
                 for (int h = 8; h > 0; h >>= 1)
 #pragma unroll
-                    for (int j = 0; j < h; ++j) t[j] = fmaxf(t[j], t[j + h]);
-                mx = t[0] * sc;
+                    for (int j = 0; j < h; ++j) u[j] = fmaxf(u[j], u[j + h]);
+                mx = u[0] * sc;
             }
-            // the row's max over the parts (every part has finished reading S[bi] after this barrier, so P may
-            // overwrite it)
-            xmax[part * kM + rt] = mx;
-            quarter_sync<kParts>(quarter);
+            if (kParts > 1) {
+                // the row's max over the parts (every part has finished reading S after this barrier, so P may
+                // overwrite it)
+                xmax[part * kM + rt] = mx;
+                quarter_sync<kParts>(quarter);
 #pragma unroll
-            for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[q * kM + rt]);
+                for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[q * kM + rt]);
+            }
             float alpha = 1.f;
             bool rescale = false;
-            if (mx > m_run + 8.f) {  // lazy: keep the running max unless the tile's exceeds it by more than 2^8
+            if (mx > m_run + 8.f) {  // lazy: keep the running max unless the tile's exceeds it by over 2^8
                 if (m_run != -INFINITY) {
                     alpha = fast_exp2(m_run - mx);
                     rescale = true;
@@ -474,22 +556,44 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 m_run = mx;
             }
             const float mref = m_run == -INFINITY ? 0.f : m_run;  // nothing visible yet: every p is 0
-            uint32_t pk[16];
-            float ps[4];  // independent partial row sums
+            // p = 2^(s sc - mref) with the products and sums on packed pairs; every kPolyEvery-th pair's
+            // exponentials on the FMA pipe (exp2_poly2), the others on the MUFU unit
+            const uint64_t sc2 = dup2(sc), nm2 = dup2(-mref);
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // independent partial row sums (pairs)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) ps[j] = 0.f;
+            for (int c = 0; c < kChunks; ++c) {
+                uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float p0 = fast_exp2(__fmaf_rn(s[j], sc, -mref));
-                const float p1 = fast_exp2(__fmaf_rn(s[j + 1], sc, -mref));
-                ps[(j >> 1) & 3] += p0 + p1;
-                pk[j >> 1] = pack_bf16(p0, p1);
+                for (int jp = 0; jp < 16; ++jp) {
+                    const uint64_t x = fma2(pk2(s[c][2 * jp], s[c][2 * jp + 1]), sc2, nm2);
+                    uint64_t e;
+                    if (jp % kPolyEvery == kPolyEvery - 1) {
+                        e = exp2_poly2(x);
+                    } else {
+                        float x0, x1;
+                        upk2(x, x0, x1);
+                        e = pk2(fast_exp2(x0), fast_exp2(x1));
+                    }
+                    acc[jp & 3] = add2(acc[jp & 3], e);
+                    float e0, e1;
+                    upk2(e, e0, e1);
+                    pk[jp] = pack_bf16(e0, e1);
+                }
+                // P as bf16 pairs over the first kKt / 2 columns of the S buffer: chunk c's 32 keys = 16 columns
+                tmem_st16u(s_tm + (c_lo >> 1) + 16 * c, pk);
             }
-            l_run = l_run * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
-            if (__any_sync(MFD_FULL_MASK, rescale)) {  // O must hold the P V of tile i-1; this part rescales O
-                                                       // columns [o_lo, o_lo + kOCols)
+            float l_add;
+            {
+                const uint64_t a2 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+                float a0, a1;
+                upk2(a2, a0, a1);
+                l_add = a0 + a1;
+            }
+            l_run = l_run * alpha + l_add;
+            if (__any_sync(MFD_FULL_MASK, rescale)) {  // O must hold the P V of key tile i - 1; this part
+                                                       // rescales O's columns [o_lo, o_lo + kOCols)
                 if (i >= 1) {
-                    ok &= mbar_wait(&bars[kBarPV + (bi ^ 1)], ((i - 1) >> 1) & 1, kTries);
+                    ok &= mbar_wait(&bars[kBarPV + ((i - 1) & 1)], ((i - 1) >> 1) & 1, kTries);
                     tc_fence_after();
                 }
 #pragma unroll
@@ -501,139 +605,141 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                     tmem_st32(tmem + lane_off + o_lo + oc, o);
                 }
             }
-            // P(i) as bf16 pairs over the first kKt / 2 columns of S[bi]: this part's 32 keys = 16 columns
-            tmem_st16u(s_tm + part * 16, pk);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[kBarPFull + bi]);
-            // the next tile's maxima may be written only after every part has read these; a failed wait anywhere
-            // in the quarter ends the loop for all its warps
+            if (lane == 0) mbar_arrive(&bars[kBarPFull + sb]);
+            // the next maxima may be written only after every part has read these; a failed wait anywhere in
+            // the quarter ends the loop for all its warps
             ok = quarter_sync_and<kParts>(quarter, ok);
-            if (!ok) break;
         }
-        if (ntiles > 0 && ok) {  // the last P V (every earlier one completed before it)
-            ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
-            tc_fence_after();
-        }
-        // ---- epilogue: the row sum over the parts, then this part's kOCols columns of O / l
-        quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
-        xmax[part * kM + rt] = l_run;
-        quarter_sync<kParts>(quarter);
-        float l_row = 0.f;
-#pragma unroll
-        for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
-        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
-        const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
         // staging of bf16 rows for coalesced stores: the K ring is free once the last P V completed
         unsigned char* stage = smem + kOffK;  // [128 rows][256 B]
-#pragma unroll
-        for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {
-            float o[32];
-            if (ntiles > 0 && quarter_live) {
-                tmem_ld32(tmem + lane_off + oc, o);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) o[j] = 0.f;
+        {
+            if (ntiles > 0 && ok) {  // O's last P V (every earlier one completed before it)
+                ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
+                tc_fence_after();
             }
-            if (p.splits == 1) {
+            // ---- epilogue: the row sum over the parts, then this part's kOCols columns of O / l
+            quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
+            xmax[part * kM + rt] = l_run;
+            quarter_sync<kParts>(quarter);
+            float l_row = 0.f;
 #pragma unroll
-                for (int j = 0; j < 32; j += 8)
-                    *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + j) * 2) =
-                        make_uint4(pack_bf16(o[j] * inv, o[j + 1] * inv), pack_bf16(o[j + 2] * inv, o[j + 3] * inv),
-                                   pack_bf16(o[j + 4] * inv, o[j + 5] * inv), pack_bf16(o[j + 6] * inv, o[j + 7] * inv));
-            } else {
-                // partials, chunk-major: float4 chunk c of row rt at [split][unit][c][rt] (a warp stores 512 B)
-                float4* dst = reinterpret_cast<float4*>(p.o_part) + ((size_t)split * units + unit) * (32 * kM);
+            for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
+            const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+            const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    dst[((oc + j) >> 2) * kM + rt] =
-                        make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
-            }
-        }
-        if (p.splits > 1) {
-            if (part == 0)
-                p.lse_part[((size_t)split * units + unit) * kM + rt] = l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
-            // the last split of this (request, KV head, M-tile) merges all of them
-            __threadfence();
-            softmax_sync<kParts>();
-            if (threadIdx.x == 64) {
-                unsigned int* tk = p.tickets + unit;
-                const unsigned int t = atomicAdd(tk, 1u);
-                const int last = t == (unsigned int)(p.splits - 1);
-                if (last) *tk = 0u;  // ready for the next launch
-                *shared_flag = last;
-            }
-            softmax_sync<kParts>();
-            if (*shared_flag) {
-                __threadfence();
-                const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
-                float m = -INFINITY;
-                for (int sp0 = 0; sp0 < p.splits; sp0 += 8) {  // eight splits' values per L2 round trip
-                    float l[8];
+            for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {
+                float o[32];
+                if (ntiles > 0 && quarter_live) {
+                    tmem_ld32(tmem + lane_off + oc, o);
+                } else {
 #pragma unroll
-                    for (int t = 0; t < 8; ++t)
-                        l[t] = sp0 + t < p.splits ? __ldcg(lse + (size_t)(sp0 + t) * units * kM) : -INFINITY;
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) m = fmaxf(m, l[t]);
+                    for (int j = 0; j < 32; ++j) o[j] = 0.f;
                 }
+                if (p.splits == 1) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8)
+                        *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + j) * 2) = make_uint4(
+                            pack_bf16(o[j] * inv, o[j + 1] * inv), pack_bf16(o[j + 2] * inv, o[j + 3] * inv),
+                            pack_bf16(o[j + 4] * inv, o[j + 5] * inv), pack_bf16(o[j + 6] * inv, o[j + 7] * inv));
+                } else {
+                    // partials, chunk-major: float4 chunk c of row rt at [split][unit][c][rt] (a warp stores 512 B)
+                    float4* dst = reinterpret_cast<float4*>(p.o_part) + ((size_t)split * units + unit) * (32 * kM);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        dst[((oc + j) >> 2) * kM + rt] =
+                            make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+                }
+            }
+            if (p.splits > 1) {
+                if (part == 0)
+                    p.lse_part[((size_t)split * units + unit) * kM + rt] =
+                        l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
+                // the last split of this (request, KV head, M-tile) merges all of them
+                __threadfence();
+                softmax_sync<kParts>();
+                if (threadIdx.x == 64) {
+                    unsigned int* tk = p.tickets + unit;
+                    const unsigned int tick = atomicAdd(tk, 1u);
+                    const int last = tick == (unsigned int)(p.splits - 1);
+                    if (last) *tk = 0u;  // ready for the next launch
+                    *shared_flag = last;
+                }
+                softmax_sync<kParts>();
+                if (*shared_flag) {
+                    __threadfence();
+                    const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
+                    float m = -INFINITY;
+                    for (int sp0 = 0; sp0 < p.splits; sp0 += 8) {  // eight splits' values per L2 round trip
+                        float l[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u)
+                            l[u] = sp0 + u < p.splits ? __ldcg(lse + (size_t)(sp0 + u) * units * kM) : -INFINITY;
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) m = fmaxf(m, l[u]);
+                    }
 #pragma unroll 1
-                for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {  // 32 columns (8 float4 chunks) at a time
-                    float acc[8][4];
+                    for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {  // 32 columns (8 float4 chunks) at a time
+                        float acc[8][4];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-                    float wsum = 0.f;
-                    if (m != -INFINITY) {
-                        // two splits' loads in flight at a time
-                        for (int sp = 0; sp < p.splits; sp += 2) {
-                            float4 v[2][8];
-                            float w[2];
+                        for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+                        float wsum = 0.f;
+                        if (m != -INFINITY) {
+                            // two splits' loads in flight at a time
+                            constexpr int kFly = 2;
+                            for (int sp = 0; sp < p.splits; sp += kFly) {
+                                float4 v[kFly][8];
+                                float w[kFly];
 #pragma unroll
-                            for (int t = 0; t < 2; ++t) {
-                                const int sq = sp + t < p.splits ? sp + t : sp;
-                                const float l = __ldcg(lse + (size_t)sq * units * kM);
-                                w[t] = (sp + t < p.splits && l != -INFINITY) ? fast_exp2(l - m) : 0.f;
-                                const float4* src = reinterpret_cast<const float4*>(p.o_part) +
-                                                    ((size_t)sq * units + unit) * (32 * kM);
+                                for (int u = 0; u < kFly; ++u) {
+                                    const int sq = sp + u < p.splits ? sp + u : sp;
+                                    const float l = __ldcg(lse + (size_t)sq * units * kM);
+                                    w[u] = (sp + u < p.splits && l != -INFINITY) ? fast_exp2(l - m) : 0.f;
+                                    const float4* src = reinterpret_cast<const float4*>(p.o_part) +
+                                                        ((size_t)sq * units + unit) * (32 * kM);
 #pragma unroll
-                                for (int c = 0; c < 8; ++c) v[t][c] = __ldcg(src + ((oc >> 2) + c) * kM + rt);
-                            }
+                                    for (int c = 0; c < 8; ++c) v[u][c] = __ldcg(src + ((oc >> 2) + c) * kM + rt);
+                                }
 #pragma unroll
-                            for (int t = 0; t < 2; ++t) {
-                                if (w[t] == 0.f) continue;  // (a split without visible keys holds zeros)
-                                wsum += w[t];
+                                for (int u = 0; u < kFly; ++u) {
+                                    if (w[u] == 0.f) continue;  // (a split without visible keys holds zeros)
+                                    wsum += w[u];
 #pragma unroll
-                                for (int c = 0; c < 8; ++c) {
-                                    acc[c][0] += w[t] * v[t][c].x;
-                                    acc[c][1] += w[t] * v[t][c].y;
-                                    acc[c][2] += w[t] * v[t][c].z;
-                                    acc[c][3] += w[t] * v[t][c].w;
+                                    for (int c = 0; c < 8; ++c) {
+                                        acc[c][0] += w[u] * v[u][c].x;
+                                        acc[c][1] += w[u] * v[u][c].y;
+                                        acc[c][2] += w[u] * v[u][c].z;
+                                        acc[c][3] += w[u] * v[u][c].w;
+                                    }
                                 }
                             }
                         }
-                    }
-                    const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
+                        const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-                    for (int c = 0; c < 8; c += 2)
-                        *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + c * 4) * 2) = make_uint4(
-                            pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
-                            pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
-                            pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+                        for (int c = 0; c < 8; c += 2)
+                            *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + c * 4) * 2) = make_uint4(
+                                pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
+                                pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
+                                pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+                    }
                 }
             }
-        }
-        // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
-        softmax_sync<kParts>();
-        if (p.splits == 1 || *shared_flag) {
-            const int ts = threadIdx.x - 64;
-            for (int e = ts; e < kM * 16; e += kSoftmaxThreads) {
-                const int rr = e >> 4, c = e & 15;
-                const int pr = row0 + rr;
-                if (pr >= nrows) continue;
-                __nv_bfloat16* orow = p.out + (size_t)b * p.so_b + (size_t)(pr / p.G) * p.so_n +
-                                      (size_t)(hk * p.G + pr % p.G) * p.so_h;
-                *reinterpret_cast<uint4*>(orow + c * 8) = *reinterpret_cast<const uint4*>(stage + rr * 256 + c * 16);
+            // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
+            softmax_sync<kParts>();
+            if (p.splits == 1 || *shared_flag) {
+                const int ts = threadIdx.x - 64;
+                for (int e = ts; e < kM * 16; e += kSoftmaxThreads) {
+                    const int rr = e >> 4, c = e & 15;
+                    const int pr = row0 + rr;
+                    if (pr >= nrows) continue;
+                    __nv_bfloat16* orow = p.out + (size_t)b * p.so_b + (size_t)(pr / p.G) * p.so_n +
+                                          (size_t)(hk * p.G + pr % p.G) * p.so_h;
+                    *reinterpret_cast<uint4*>(orow + c * 8) =
+                        *reinterpret_cast<const uint4*>(stage + rr * 256 + c * 16);
+                }
             }
         }
     }
@@ -707,7 +813,7 @@ static int launch_cfg(const Shape& sh, const Params& p, cudaStream_t stream) {
     return MFD_OK;
 }
 
-int launch(const Shape& sh, const Params& p, cudaStream_t stream) { return launch_cfg<CfgWide>(sh, p, stream); }
+int launch(const Shape& sh, const Params& p, cudaStream_t stream) { return launch_cfg<CfgRow>(sh, p, stream); }
 
 }  // namespace tca
 }  // namespace mfd

@@ -79,8 +79,7 @@ def paged_mode_block_attention(
         out = torch.empty((T, H, D), device=q.device, dtype=q.dtype)
     if bs == 0:
         return out
-    mtiles = (KL * (H // Hkv) + 127) // 128
-    splits = resolve_ctx_splits(num_ctx_splits, programs=bs * Hkv * mtiles, device=q.device)
+    splits = resolve_ctx_splits(num_ctx_splits, programs=ops.attention_ctas(bs, KL, H, Hkv), device=q.device)
     bits = block_bits(num_modes, block_size, q.device)
     return ops.paged_mode_attention(q, k_new, v_new, k_cache, v_cache, req_to_token, req_pool_indices, ctx_lens,
                                     bits, num_modes, block_size, scaling, splits, out=out)

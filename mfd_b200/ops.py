@@ -227,12 +227,17 @@ def compile_tree(root: torch.Tensor, tokens: torch.Tensor, depths: torch.Tensor,
 
 # ----------------------------------------------------------------------------------------------- attention
 
+def attention_ctas(bs: int, n: int, num_heads: int, num_kv_heads: int) -> int:
+    """CTAs of one key split of the verify attention: one per (request, KV head, 128-row M-tile of the packed rows
+    (node, query head of the group))."""
+    return bs * num_kv_heads * ((n * (num_heads // num_kv_heads) + 127) // 128)
+
+
 def default_splits(bs: int, n: int, num_heads: int, num_kv_heads: int, keys: int) -> int:
-    """Key splits of the attention: at most one wave of CTAs (one CTA per SM), each split at least 4 tiles of 64
-    keys (shorter splits would spend more on their partial (o, lse) records than on keys)."""
+    """Key splits of the attention: at most one wave of CTAs (one CTA per SM), each split at least 2 key tiles of
+    128 (shorter splits would spend more on their partial (o, lse) records than on keys)."""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    mtiles = (n * (num_heads // num_kv_heads) + 127) // 128
-    units = bs * num_kv_heads * mtiles
+    units = attention_ctas(bs, n, num_heads, num_kv_heads)
     want = max(1, sms // units)
     max_splits = max(1, (keys + 255) // 256)
     return int(min(want, max_splits))

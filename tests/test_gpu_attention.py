@@ -41,7 +41,8 @@ def test_verify_attention_vs_reference_fixture():
 
 
 @pytest.mark.parametrize("P,n,H,Hkv,splits", [(4096, 65, 32, 8, None), (100, 65, 32, 8, 3), (0, 17, 8, 8, 1),
-                                              (1000, 64, 32, 8, 7), (77, 257, 16, 4, 2)])
+                                              (1000, 64, 32, 8, 7), (77, 257, 16, 4, 2), (300, 100, 16, 8, 1),
+                                              (2500, 130, 8, 2, None), (129, 33, 32, 8, 1)])
 def test_tree_attention_vs_oracle(P, n, H, Hkv, splits):
     from mfd_b200 import ops
     g = torch.Generator().manual_seed(P + n + H)
@@ -169,3 +170,25 @@ def test_tree_attention_ignores_nan_beyond_each_requests_keys(splits):
     assert torch.isfinite(out1.float()).all()
     assert torch.equal(out1.cpu(), out[1:2].to(torch.bfloat16)) or \
         (out1.float().cpu() - out[1:2]).abs().max() <= TOL
+
+
+@pytest.mark.parametrize("n,splits", [(65, 1), (65, 3), (64, 2), (100, 1)])
+def test_tree_attention_rescales_on_growing_scores(n, splits):
+    """Scores that grow along the keys (K scaled by a ramp from 1 to 6) raise each row's running maximum by far
+    more than 2^8 several times, so every M-tile of a CTA (one or two per CTA) takes the O rescale path; the result
+    still matches the oracle."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(500 + n + splits)
+    P, H, Hkv, D = 1500, 32, 8, 128
+    parents = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)]
+    ramp = torch.linspace(1.0, 6.0, P + n).view(1, 1, P + n, 1)
+    q = (torch.randn(1, n, H, D, generator=g) * 2).to(torch.bfloat16)
+    k = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5 * ramp).to(torch.bfloat16)
+    v = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5).to(torch.bfloat16)
+    anc = anc_bits(parents, (n + 63) // 64)[None].to(DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, P, D ** -0.5, splits=splits)
+    kk = k[0].transpose(0, 1).float().numpy()
+    vv = v[0].transpose(0, 1).float().numpy()
+    ref = oracle.tree_attention(q[0].float().numpy(), kk[:P], vv[:P], kk[P:], vv[P:], parents, D ** -0.5)
+    assert np.abs(out[0].float().cpu().numpy() - ref).max() <= TOL
+    assert ops.tree_attention_status() == 0
