@@ -48,9 +48,9 @@ H, HKV, D = 32, 8, 128
 TOTAL_REQUESTS = 256     # 256 requests, partitioned 256/128/64/32 per GPU at 1/2/4/8 GPUs
 REQUESTS_PER_GPU = 32    # the --kernel / --config profiling cases
 # Logits-step DRAM traffic per row (read + write) from an ncu capture of 1024 rows x 151936 fp32, k = 64
-# (bench.py --kernel logits_step --requests-per-gpu 8): 626.81 MB read + 10.39 MB written.  Traffic grows with the
+# (bench.py --kernel logits_step --requests-per-gpu 8): 622.52 MB read + 4.65 MB written.  Traffic grows with the
 # rows, so a launch of R rows moves R times this.
-TOPK_TRAFFIC_PER_ROW = (626.812672e6 + 10.390272e6) / 1024
+TOPK_TRAFFIC_PER_ROW = (622.516224e6 + 4.645376e6) / 1024
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -766,6 +766,25 @@ def config_line(config: int, steps: int, warmup: int):
         line["uo_us"] = round(uo_us, 2)
         line["uo_roofline_us"] = round((2 * n * Hk * D * 2 + n * Hv * D * 2 + Hv * D * D * 4 + 2 * n * Hv * D * 4)
                                        / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
+        # the layer's input preparation (causal conv of kernel 4 over each node's window -- its root path after
+        # the conv state --, SiLU, l2 norms of q and k): tree_prep
+        KC = 4
+        cd = (2 * Hk + Hv) * D
+        x = torch.randn(n, cd, generator=g, device=dev).bfloat16()
+        conv_state = torch.randn(cd, KC, generator=g, device=dev).bfloat16()
+        conv_w = (torch.randn(cd, KC, generator=g, device=dev) * 0.5).bfloat16()
+        windows = []
+        for i in range(n):
+            path, j = [], i
+            while j >= 0:
+                path.append(KC + j)
+                j = parents[j]
+            windows.append((list(range(KC)) + path[::-1])[-KC:])
+        conv_index = torch.tensor(windows, dtype=torch.int32, device=dev)
+        prep_us = timed_us(lambda: ops.tree_prep(x, conv_state, conv_index, conv_w, Hk, Hv, D), steps, warmup, flush)
+        prep_bytes = n * cd * 2 + 2 * cd * KC * 2 + n * KC * 4 + (2 * n * Hk * D + n * Hv * D) * 2
+        line["prep_us"] = round(prep_us, 2)
+        line["prep_roofline_us"] = round(prep_bytes / (pk["hbm_gbs"] * 1e9) * 1e6, 2)
 
         def fn():
             ops.tree_gdn(q, k, v, G, beta, s0, anc, emit_states=True, out=(u, o, st))
