@@ -74,7 +74,7 @@ struct Cfg {
     static constexpr int kOffK = kOffQ + kQBytes;
     static constexpr int kOffV = kOffK + STAGES * kKVBytes;
     static constexpr int kOffX = kOffV + STAGES * kKVBytes;  // row maxima / sums exchanged by the parts of a row
-    static constexpr int kOffBar = kOffX + PARTS * kM * 4;
+    static constexpr int kOffBar = kOffX + 2 * PARTS * kM * 4;  // (two tiles' exchanges)
     static constexpr int kBarArea = 256;
     static constexpr int kSmemUsed = kOffBar + kBarArea;  // + barriers, TMEM address, flags
     static constexpr int kSmemCap = MINB == 1 ? kSmemMax : kSmemPerSm / MINB - 1024;
@@ -143,6 +143,11 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 // every kPolyEvery-th exponential pair of a row's keys goes to exp2_poly2, the rest to ex2.approx
 constexpr int kPolyEvery = 3;
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 // named barriers: 1 = the softmax threads, 2 + q = the PARTS warps of TMEM lane quarter q (one warp: a warp sync)
 template <int PARTS>
 __device__ __forceinline__ void softmax_sync() {
@@ -442,7 +447,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         const int part = (warp - 2) >> 2;
         const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-        float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [kParts][128 rows]
+        float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [2][kParts][128 rows]
         constexpr int kCols = kKt / kParts, kChunks = kCols / 32;
         const int c_lo = part * kCols;   // this warp's kCols of the tile's kKt key columns
         const int o_lo = part * kOCols;  // and its kOCols of O's 128 columns
@@ -451,7 +456,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         // a quarter whose 32 rows are all padding keeps only the barrier protocol: it leaves its TMEM rows as they
         // are, and the P V rows they feed (rows are independent in the MMA) are never stored
         const bool quarter_live = row0 + quarter * 32 < nrows;
-        for (int i = 0; i < ntiles && ok; ++i) {
+        // the loop ends for all warps of a quarter together: only at the max exchange, where their ok flags are
+        // AND-ed (a warp leaving alone would leave its partners waiting at a named barrier)
+        for (int i = 0; i < ntiles; ++i) {
             const int key0 = k_lo + i * kKt;
             const int sb = i & 1;
             const uint32_t s_tm = tmem + lane_off + kSCol + sb * kKt;
@@ -476,6 +483,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars[kBarPFull + sb]);
                 ok = __all_sync(MFD_FULL_MASK, ok);
+                if (!ok) break;
                 continue;
             }
             // this part's kCols scores of the row: kChunks TMEM loads in flight together
@@ -524,28 +532,29 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 }
             }
             float mx;
-            {  // the raw scores' maximum as a tree (scaling by sc > 0 keeps the order: max(s) sc = max(s sc))
+            {  // the raw scores' maximum as a tree of three-input maxima (scaling by sc > 0 keeps the order)
                 float u[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) u[j] = fmaxf(s[0][j], s[0][j + 16]);
 #pragma unroll
                 for (int c = 1; c < kChunks; ++c)
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) u[j] = fmaxf(u[j], fmaxf(s[c][j], s[c][j + 16]));
+                    for (int j = 0; j < 16; ++j) u[j] = fmax3(u[j], s[c][j], s[c][j + 16]);
 #pragma unroll
-                for (int h = 8; h > 0; h >>= 1)
-#pragma unroll
-                    for (int j = 0; j < h; ++j) u[j] = fmaxf(u[j], u[j + h]);
-                mx = u[0] * sc;
+                for (int j = 0; j < 5; ++j) u[j] = fmax3(u[3 * j], u[3 * j + 1], u[3 * j + 2]);
+                mx = fmaxf(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[15])) * sc;
             }
             if (kParts > 1) {
-                // the row's max over the parts (every part has finished reading S after this barrier, so P may
-                // overwrite it)
-                xmax[part * kM + rt] = mx;
-                quarter_sync<kParts>(quarter);
+                // the row's max over the parts, through a double-buffered exchange: after this barrier every part
+                // has finished reading S (so P may overwrite it), and a part can run at most one tile ahead
+                xmax[((i & 1) * kParts + part) * kM + rt] = mx;
+                ok = quarter_sync_and<kParts>(quarter, ok);
 #pragma unroll
-                for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[q * kM + rt]);
+                for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[((i & 1) * kParts + q) * kM + rt]);
+            } else {
+                ok = __all_sync(MFD_FULL_MASK, ok);
             }
+            if (!ok) break;
             float alpha = 1.f;
             bool rescale = false;
             if (mx > m_run + 8.f) {  // lazy: keep the running max unless the tile's exceeds it by over 2^8
@@ -609,9 +618,6 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars[kBarPFull + sb]);
-            // the next maxima may be written only after every part has read these; a failed wait anywhere in
-            // the quarter ends the loop for all its warps
-            ok = quarter_sync_and<kParts>(quarter, ok);
         }
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
         // staging of bf16 rows for coalesced stores: the K ring is free once the last P V completed
