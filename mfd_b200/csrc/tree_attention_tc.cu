@@ -56,22 +56,25 @@ constexpr int kSmemPerSm = 228 * 1024;  // per SM, of which 1 KB per resident bl
 // tile with the MMA warp alternating between them (2 stages) 2221 to 2561 us; separate K and V rings (a K stage
 // refilled as soon as its scores complete) 2146 us; Cfg<64, 2, 2, 2> (two CTAs per SM)
 // was slower still at 32 requests (348 against 280 us).
-template <int KT, int STAGES, int PARTS, int MINB>
+template <int KT, int STAGES, int PARTS, int MINB, int TILES = 1>
 struct Cfg {
     static constexpr int kKt = KT;
     static constexpr int kStages = STAGES;
     static constexpr int kParts = PARTS;
     static constexpr int kCtasPerSm = MINB;
+    static constexpr int kTiles = TILES;
     static constexpr int kOCols = D / PARTS;  // O columns each part rescales and stores
-    static constexpr int kSoftmaxThreads = 128 * PARTS;
+    static constexpr int kGroupThreads = 128 * PARTS;  // the softmax warps of one M-tile
+    static constexpr int kSoftmaxThreads = kGroupThreads * TILES;
     static constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, then the softmax warps
-    // S buffer b at column kSCol + KT b; P (bf16 pairs) over its first KT / 2 columns
-    static constexpr int kSCol = 128;
+    // O of M-tile t at column 128 t; S buffer b at column kSCol + KT b (TILES = 1: b = key tile parity; TILES = 2:
+    // b = M-tile); P (bf16 pairs) over its first KT / 2 columns
+    static constexpr int kSCol = 128 * TILES;
     static constexpr int kTmemCols = kSCol + 2 * KT <= 256 ? 256 : 512;
-    static constexpr int kQBytes = kM * D * 2;    // 32 KB: [2 d-halves][128 rows][128 B]
+    static constexpr int kQBytes = kM * D * 2;    // 32 KB per M-tile: [2 d-halves][128 rows][128 B]
     static constexpr int kKVBytes = KT * D * 2;   // [2 d-halves][KT keys][128 B]
     static constexpr int kOffQ = 0;
-    static constexpr int kOffK = kOffQ + kQBytes;
+    static constexpr int kOffK = kOffQ + TILES * kQBytes;
     static constexpr int kOffV = kOffK + STAGES * kKVBytes;
     static constexpr int kOffX = kOffV + STAGES * kKVBytes;  // row maxima / sums exchanged by the parts of a row
     static constexpr int kOffBar = kOffX + 2 * PARTS * kM * 4;  // (two tiles' exchanges)
@@ -91,13 +94,15 @@ struct Cfg {
     static constexpr int kBarPV = kBarPFull + 2;     // + S buffer: the P V that read it completes
     static constexpr int kNumBars = kBarPV + 2;
     static_assert(KT % (32 * PARTS) == 0, "each softmax warp takes a multiple of 32 key columns");
+    static_assert(TILES == 1 || (TILES == 2 && PARTS == 1 && kSCol + 2 * KT <= 512), "two M-tiles: one warp per row");
     static_assert(kOCols % 32 == 0, "O columns per part");
     static_assert(kSmemSlack >= 0 && kSmemBytes <= kSmemCap, "shared memory");
-    static_assert(STAGES * kKVBytes >= kM * 256, "the epilogue stages 128 bf16 rows in the K ring");
-    static_assert(8 * kNumBars + 8 <= kBarArea, "barrier area");
+    static_assert(STAGES * kKVBytes >= TILES * kM * 256, "the epilogue stages 128 bf16 rows per M-tile in the K ring");
+    static_assert(8 * kNumBars + 4 + 4 * TILES <= kBarArea, "barrier area");
     static_assert(MINB * kThreads <= 2048, "threads per SM");
 };
 using CfgRow = Cfg<128, 3, 2, 1>;
+using CfgPair = Cfg<128, 2, 1, 1, 2>;
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
 // K / V tiles are prefetched into L2 this many tiles before their load into the ring, so the ring's loads see L2
 // latency instead of DRAM latency (a stage is refilled less than one tile period before its scores are needed)
@@ -148,10 +153,11 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
-// named barriers: 1 = the softmax threads, 2 + q = the PARTS warps of TMEM lane quarter q (one warp: a warp sync)
-template <int PARTS>
-__device__ __forceinline__ void softmax_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(128 * PARTS) : "memory");
+// named barriers: 1 (and 6) = the softmax warps of M-tile 0 (and 1), 2 + q = the PARTS warps of TMEM lane quarter q
+// (one warp: a warp sync)
+template <int N>
+__device__ __forceinline__ void group_sync(int g) {  // the softmax warps of M-tile g: barrier 1 or 6
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + 5 * g), "n"(N) : "memory");
 }
 template <int PARTS>
 __device__ __forceinline__ void quarter_sync(int quarter) {
@@ -200,7 +206,8 @@ template <class C>
 __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const Params p) {
-    constexpr int kKt = C::kKt, kStages = C::kStages, kParts = C::kParts, kOCols = C::kOCols;
+    constexpr int kKt = C::kKt, kStages = C::kStages, kParts = C::kParts, kOCols = C::kOCols, kTiles = C::kTiles;
+    constexpr int kGroupThreads = C::kGroupThreads;
     constexpr int kSoftmaxThreads = C::kSoftmaxThreads, kTmemCols = C::kTmemCols, kSCol = C::kSCol;
     constexpr int kQBytes = C::kQBytes, kKVBytes = C::kKVBytes;
     constexpr int kOffQ = C::kOffQ, kOffK = C::kOffK, kOffV = C::kOffV, kOffX = C::kOffX, kOffBar = C::kOffBar;
@@ -218,16 +225,21 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     const uint32_t sbase = smem_addr(smem);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + 8 * kNumBars);
-    int* shared_flag = reinterpret_cast<int*>(smem + kOffBar + 8 * kNumBars + 4);
+    int* shared_flags = reinterpret_cast<int*>(smem + kOffBar + 8 * kNumBars + 4);  // one per M-tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    const int split = blockIdx.x / p.mtiles, mtile = blockIdx.x % p.mtiles;
+    // CTA x = split * ctiles + c: the CTA takes M-tiles mt0 .. mt0 + ntl - 1 of its (request, KV head)
+    const int ctiles = (p.mtiles + kTiles - 1) / kTiles;
+    const int split = blockIdx.x / ctiles;
+    const int mt0 = (blockIdx.x % ctiles) * kTiles;
+    const int ntl = min(kTiles, p.mtiles - mt0);
     const int hk = blockIdx.y;
     const int b = (!p.paged && p.prefix && p.bs > 1 && p.bs <= kMaxOrdered)
                       ? request_by_length_rank(p.prefix, p.bs, (int)blockIdx.z)
                       : (int)blockIdx.z;
     const int nrows = p.n * p.G;
-    const int row0 = mtile * kM;
+    // the phase of S buffer / P / P V barrier use i: one M-tile alternates two S buffers, two M-tiles have one each
+    auto sph = [](int i) { return (uint32_t)(kTiles == 1 ? ((i >> 1) & 1) : (i & 1)); };
     // keys [0, prefix) are visible to every row; keys [prefix, prefix + n) are the tree (block) keys, visible by the
     // ancestor bitsets.  Paged mode: the prefix is the request's context length, read on the device.
     int prefix;
@@ -252,7 +264,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNumBars; ++i)
             mbar_init(&bars[i], (i >= kBarPFull && i < kBarPV) ? (uint32_t)(4 * kParts) : 1u);
-        *shared_flag = 0;
+        for (int t = 0; t < kTiles; ++t) shared_flags[t] = 0;
         mbar_fence_init();
     }
     auto prefetch_kv = [&](int i) {
@@ -338,10 +350,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     };
     if (threadIdx.x == 0 && ntiles > 0) {  // (a split past the keys loads nothing: every issued copy is waited for)
         const int nodes_per_tile = kM / p.G;
-        mbar_expect_tx(&bars[kBarQ], kQBytes);
-        for (int h = 0; h < 2; ++h)
-            tma_load_4d(sbase + kOffQ + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G,
-                        mtile * nodes_per_tile, b);
+        mbar_expect_tx(&bars[kBarQ], ntl * kQBytes);
+        for (int t = 0; t < ntl; ++t)
+            for (int h = 0; h < 2; ++h)
+                tma_load_4d(sbase + kOffQ + t * kQBytes + h * (kQBytes / 2), &tmq, &bars[kBarQ], h * 64, hk * p.G,
+                            (mt0 + t) * nodes_per_tile, b);
         if (!p.paged) {
             for (int i = 0; i < min(kStages, ntiles); ++i) load_kv(i);
             for (int i = kStages; i < kStages + kPrefetchAhead; ++i) prefetch_kv(i);
@@ -398,13 +411,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         if (lane == 0) {
             constexpr uint32_t kIdescS = idesc_bf16(kM, kKt, 0);
             constexpr uint32_t kIdescO = idesc_bf16(kM, D, 1);
-            // S(i) = Q K_i^T into S buffer i % 2
-            auto issue_qk = [&](int i) {
-                const int st = i % kStages, sb = i & 1;
-                ok &= mbar_wait(&bars[kBarKVFull + st], (i / kStages) & 1, kTries);
-                tc_fence_after();
+            // S(t, i) = Q_t K_i^T into S buffer sb (key tile parity with one M-tile, the M-tile with two)
+            auto issue_qk = [&](int t, int i, int sb) {
+                const int st = i % kStages;
                 const uint32_t kaddr = sbase + kOffK + st * kKVBytes;
-                const uint32_t qaddr = sbase + kOffQ;
+                const uint32_t qaddr = sbase + kOffQ + t * kQBytes;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
                     const uint32_t qoff = (uint32_t)((ks >> 2) * (kQBytes / 2) + (ks & 3) * 32);
@@ -414,37 +425,72 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 }
                 umma_commit(&bars[kBarSFull + sb]);
             };
-            // O += P(j) V_j once the softmax published P(j); the K/V stage is released when it completes
-            auto issue_pv = [&](int j) {
-                const int st = j % kStages, sb = j & 1;
-                ok &= mbar_wait(&bars[kBarPFull + sb], (j >> 1) & 1, kTries);
+            // O_t += P(t, j) V_j once the softmax published P(t, j)
+            auto issue_pv = [&](int t, int j, int sb) {
+                const int st = j % kStages;
+                ok &= mbar_wait(&bars[kBarPFull + sb], sph(j), kTries);
                 tc_fence_after();
                 const uint32_t vaddr = sbase + kOffV + st * kKVBytes;
 #pragma unroll
                 for (int ks = 0; ks < kKt / 16; ++ks)  // P: 16 keys = 8 columns of bf16 pairs per step
-                    umma_ts(tmem, tmem + kSCol + sb * kKt + ks * 8, sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024),
-                            kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                    umma_ts(tmem + t * 128, tmem + kSCol + sb * kKt + ks * 8,
+                            sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
                 umma_commit(&bars[kBarPV + sb]);
-                umma_commit(&bars[kBarKVEmpty + st]);
+            };
+            auto wait_kv = [&](int i) {
+                ok &= mbar_wait(&bars[kBarKVFull + i % kStages], (i / kStages) & 1, kTries);
+                tc_fence_after();
             };
             if (ntiles > 0) ok &= mbar_wait(&bars[kBarQ], 0, kTries);
-            // scores of tile i while the softmax works on tile i - 1 (two S buffers); the stage of tile i - 1 is
-            // released when its P V completes.  S[i % 2] last held P(i - 2),
-            // which the P V issued in the previous iteration consumed (tensor-core operations of this thread
-            // execute in order).
-            for (int i = 0; i < ntiles && ok; ++i) {
-                issue_qk(i);
-                if (i >= 1 && ok) issue_pv(i - 1);
+            if (kTiles == 1) {
+                // scores of tile i while the softmax works on tile i - 1 (two S buffers); the stage of tile i - 1
+                // is released when its P V completes.  S[i % 2] last held P(i - 2), which the P V issued in the
+                // previous iteration consumed (tensor-core operations of this thread execute in order).
+                for (int i = 0; i < ntiles && ok; ++i) {
+                    wait_kv(i);
+                    issue_qk(0, i, i & 1);
+                    if (i >= 1 && ok) {
+                        issue_pv(0, i - 1, (i - 1) & 1);
+                        umma_commit(&bars[kBarKVEmpty + (i - 1) % kStages]);
+                    }
+                }
+                if (ntiles > 0 && ok) {
+                    issue_pv(0, ntiles - 1, (ntiles - 1) & 1);
+                    umma_commit(&bars[kBarKVEmpty + (ntiles - 1) % kStages]);
+                }
+            } else {
+                // two M-tiles, each with its own softmax warps and S buffer: P V of M-tile t for key tile i, then
+                // its scores for key tile i + 1 (into the buffer the P V just read), while the other M-tile's
+                // softmax runs; the stage of tile i is released after the last M-tile's P V
+                if (ntiles > 0 && ok) {
+                    wait_kv(0);
+                    for (int t = 0; t < ntl; ++t) issue_qk(t, 0, t);
+                }
+                for (int i = 0; i < ntiles && ok; ++i) {
+                    for (int t = 0; t < ntl && ok; ++t) {
+                        issue_pv(t, i, t);
+                        if (t == ntl - 1) umma_commit(&bars[kBarKVEmpty + i % kStages]);
+                        if (i + 1 < ntiles && ok) {
+                            if (t == 0) wait_kv(i + 1);
+                            issue_qk(t, i + 1, t);
+                        }
+                    }
+                }
             }
-            if (ntiles > 0 && ok) issue_pv(ntiles - 1);
         }
     } else {
         // ---------------------------------------------------------------- softmax warps
-        // warp w: TMEM lane quarter w % 4, key columns [kCols part, kCols part + kCols) of each tile with
-        // part = (w - 2) / 4; the kParts warps of a quarter exchange their row maxima (and at the end their row
-        // sums) through shared memory.
+        // warp w: M-tile t = (w - 2) / (4 kParts) of the CTA, TMEM lane quarter w % 4, key columns
+        // [kCols part, kCols part + kCols) of each tile with part = ((w - 2) mod 4 kParts) / 4; the kParts warps of
+        // a quarter exchange their row maxima (and at the end their row sums) through shared memory.  With two
+        // M-tiles each has its own warps, so one M-tile's softmax runs while the other's P V and scores do.
+        const int wg = warp - 2;
+        const int t = wg / (4 * kParts);
         const int quarter = warp & 3;
-        const int part = (warp - 2) >> 2;
+        const int part = (wg % (4 * kParts)) >> 2;
+        const int gtid = threadIdx.x - 64 - t * kGroupThreads;  // thread index among this M-tile's warps
+        const int row0 = (mt0 + t) * kM;
+        const int mtile = mt0 + t;
         const int rt = quarter * 32 + lane;  // row within the M-tile (TMEM lane)
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [2][kParts][128 rows]
@@ -456,23 +502,25 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         // a quarter whose 32 rows are all padding keeps only the barrier protocol: it leaves its TMEM rows as they
         // are, and the P V rows they feed (rows are independent in the MMA) are never stored
         const bool quarter_live = row0 + quarter * 32 < nrows;
+        const int loop_tiles = t < ntl ? ntiles : 0;  // (a CTA's last M-tile may have no second one)
         // the loop ends for all warps of a quarter together: only at the max exchange, where their ok flags are
         // AND-ed (a warp leaving alone would leave its partners waiting at a named barrier)
-        for (int i = 0; i < ntiles; ++i) {
+        for (int i = 0; i < loop_tiles; ++i) {
             const int key0 = k_lo + i * kKt;
-            const int sb = i & 1;
+            const int sb = kTiles == 1 ? (i & 1) : t;
             const uint32_t s_tm = tmem + lane_off + kSCol + sb * kKt;
-            ok &= mbar_wait(&bars[kBarSFull + sb], (i >> 1) & 1, kTries);
+            ok &= mbar_wait(&bars[kBarSFull + sb], sph(i), kTries);
             tc_fence_after();
             if (key0 + kKt > k_hi) {
                 // the tile runs past this split's keys: its rows from k_hi on hold whatever the caller's buffer has
                 // beyond the request's keys (any bits, NaN included).  Their P is 0, but 0 * NaN is NaN in the P V
                 // product, so those V rows are cleared before P is published (the tile landed before S(i) was
-                // computed, and P V (i) is issued only after every softmax warp has arrived below).  Each key row is
-                // 128 contiguous bytes per d-half, whatever the swizzle order of its 16-byte granules.
+                // computed, and an M-tile's P V (i) is issued only after all its softmax warps have arrived below;
+                // with two M-tiles each clears every such row itself, the other's stores writing the same zeros).
+                // Each key row is 128 contiguous bytes per d-half, whatever the swizzle order of its granules.
                 const int r0 = k_hi > key0 ? k_hi - key0 : 0;
                 unsigned char* vt = smem + kOffV + (i % kStages) * kKVBytes;
-                for (int g = threadIdx.x - 64; g < (kKt - r0) * 16; g += kSoftmaxThreads) {
+                for (int g = gtid; g < (kKt - r0) * 16; g += kGroupThreads) {
                     const int rr = r0 + (g >> 4), h = (g >> 3) & 1, c = g & 7;
                     *reinterpret_cast<uint4*>(vt + h * (kKVBytes / 2) + rr * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
                 }
@@ -602,16 +650,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
             if (__any_sync(MFD_FULL_MASK, rescale)) {  // O must hold the P V of key tile i - 1; this part
                                                        // rescales O's columns [o_lo, o_lo + kOCols)
                 if (i >= 1) {
-                    ok &= mbar_wait(&bars[kBarPV + ((i - 1) & 1)], ((i - 1) >> 1) & 1, kTries);
+                    ok &= mbar_wait(&bars[kBarPV + (kTiles == 1 ? ((i - 1) & 1) : t)], sph(i - 1), kTries);
                     tc_fence_after();
                 }
 #pragma unroll
                 for (int oc = 0; oc < kOCols; oc += 32) {
                     float o[32];
-                    tmem_ld32(tmem + lane_off + o_lo + oc, o);
+                    tmem_ld32(tmem + lane_off + t * 128 + o_lo + oc, o);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) o[j] *= alpha;
-                    tmem_st32(tmem + lane_off + o_lo + oc, o);
+                    tmem_st32(tmem + lane_off + t * 128 + o_lo + oc, o);
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -621,26 +669,29 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         }
         const size_t units = (size_t)p.bs * p.Hkv * p.mtiles;
         // staging of bf16 rows for coalesced stores: the K ring is free once the last P V completed
-        unsigned char* stage = smem + kOffK;  // [128 rows][256 B]
-        {
+        unsigned char* stage = smem + kOffK + t * (kM * 256);  // [128 rows][256 B] per M-tile
+        if (t < ntl) {
             if (ntiles > 0 && ok) {  // O's last P V (every earlier one completed before it)
-                ok &= mbar_wait(&bars[kBarPV + ((ntiles - 1) & 1)], ((ntiles - 1) >> 1) & 1, kTries);
+                ok &= mbar_wait(&bars[kBarPV + (kTiles == 1 ? ((ntiles - 1) & 1) : t)], sph(ntiles - 1), kTries);
                 tc_fence_after();
             }
             // ---- epilogue: the row sum over the parts, then this part's kOCols columns of O / l
-            quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
-            xmax[part * kM + rt] = l_run;
-            quarter_sync<kParts>(quarter);
-            float l_row = 0.f;
+            float l_row = l_run;
+            if (kParts > 1) {
+                quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
+                xmax[part * kM + rt] = l_run;
+                quarter_sync<kParts>(quarter);
+                l_row = 0.f;
 #pragma unroll
-            for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
+                for (int q = 0; q < kParts; ++q) l_row += xmax[q * kM + rt];
+            }
             const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
             const size_t unit = ((size_t)b * p.Hkv + hk) * p.mtiles + mtile;
 #pragma unroll
             for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {
                 float o[32];
                 if (ntiles > 0 && quarter_live) {
-                    tmem_ld32(tmem + lane_off + oc, o);
+                    tmem_ld32(tmem + lane_off + t * 128 + oc, o);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) o[j] = 0.f;
@@ -666,16 +717,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                         l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
                 // the last split of this (request, KV head, M-tile) merges all of them
                 __threadfence();
-                softmax_sync<kParts>();
-                if (threadIdx.x == 64) {
+                group_sync<kGroupThreads>(t);
+                if (gtid == 0) {
                     unsigned int* tk = p.tickets + unit;
                     const unsigned int tick = atomicAdd(tk, 1u);
                     const int last = tick == (unsigned int)(p.splits - 1);
                     if (last) *tk = 0u;  // ready for the next launch
-                    *shared_flag = last;
+                    shared_flags[t] = last;
                 }
-                softmax_sync<kParts>();
-                if (*shared_flag) {
+                group_sync<kGroupThreads>(t);
+                if (shared_flags[t]) {
                     __threadfence();
                     const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
                     float m = -INFINITY;
@@ -734,10 +785,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 }
             }
             // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
-            softmax_sync<kParts>();
-            if (p.splits == 1 || *shared_flag) {
-                const int ts = threadIdx.x - 64;
-                for (int e = ts; e < kM * 16; e += kSoftmaxThreads) {
+            group_sync<kGroupThreads>(t);
+            if (p.splits == 1 || shared_flags[t]) {
+                for (int e = gtid; e < kM * 16; e += kGroupThreads) {
                     const int rr = e >> 4, c = e & 15;
                     const int pr = row0 + rr;
                     if (pr >= nrows) continue;
@@ -813,13 +863,18 @@ static int launch_cfg(const Shape& sh, const Params& p, cudaStream_t stream) {
         set_error("%s: %s", who, cudaGetErrorString(e));
         return MFD_ERR_CUDA;
     }
-    dim3 grid((unsigned)(p.splits * p.mtiles), (unsigned)p.Hkv, (unsigned)p.bs);
+    dim3 grid((unsigned)(p.splits * ((p.mtiles + C::kTiles - 1) / C::kTiles)), (unsigned)p.Hkv, (unsigned)p.bs);
     tree_attn_tc_kernel<C><<<grid, C::kThreads, C::kSmemBytes, stream>>>(tq, tk, tv, p);
     MFD_CHECK_LAUNCH(who);
     return MFD_OK;
 }
 
-int launch(const Shape& sh, const Params& p, cudaStream_t stream) { return launch_cfg<CfgRow>(sh, p, stream); }
+// The paged gather (cp.async through req_to_token, issued by one warp) is the paged launch's bound, so pairs of its
+// M-tiles share each gathered K/V tile (SGLang mode attention, 32 requests: 926 -> 716 us).  The dense TMA path keeps
+// one M-tile per CTA: paired, its verify attention took 2324 against 2034 us at 256 requests.
+int launch(const Shape& sh, const Params& p, cudaStream_t stream) {
+    return (p.paged && p.mtiles >= 2) ? launch_cfg<CfgPair>(sh, p, stream) : launch_cfg<CfgRow>(sh, p, stream);
+}
 
 }  // namespace tca
 }  // namespace mfd

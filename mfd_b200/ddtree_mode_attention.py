@@ -37,7 +37,7 @@ def _sm_count(device) -> int:
 
 def resolve_ctx_splits(num_ctx_splits: int, *, programs: int, device) -> int:
     """num_ctx_splits > 0: that many key ranges per request; 0: one; < 0: auto, enough ranges for the
-    (request, KV head, M-tile) CTAs to cover the SMs once (at most 16)."""
+    (request, KV head, M-tile pair) CTAs to cover the SMs once (at most 16)."""
     if num_ctx_splits > 0:
         return int(num_ctx_splits)
     if num_ctx_splits == 0:
@@ -79,7 +79,7 @@ def paged_mode_block_attention(
         out = torch.empty((T, H, D), device=q.device, dtype=q.dtype)
     if bs == 0:
         return out
-    splits = resolve_ctx_splits(num_ctx_splits, programs=ops.attention_ctas(bs, KL, H, Hkv), device=q.device)
+    splits = resolve_ctx_splits(num_ctx_splits, programs=ops.attention_ctas(bs, KL, H, Hkv, paged=True), device=q.device)
     bits = block_bits(num_modes, block_size, q.device)
     return ops.paged_mode_attention(q, k_new, v_new, k_cache, v_cache, req_to_token, req_pool_indices, ctx_lens,
                                     bits, num_modes, block_size, scaling, splits, out=out)

@@ -227,10 +227,11 @@ def compile_tree(root: torch.Tensor, tokens: torch.Tensor, depths: torch.Tensor,
 
 # ----------------------------------------------------------------------------------------------- attention
 
-def attention_ctas(bs: int, n: int, num_heads: int, num_kv_heads: int) -> int:
-    """CTAs of one key split of the verify attention: one per (request, KV head, 128-row M-tile of the packed rows
-    (node, query head of the group))."""
-    return bs * num_kv_heads * ((n * (num_heads // num_kv_heads) + 127) // 128)
+def attention_ctas(bs: int, n: int, num_heads: int, num_kv_heads: int, paged: bool = False) -> int:
+    """CTAs of one key split of the attention kernel: one per (request, KV head, 128-row M-tile of the packed rows
+    (node, query head of the group)); the paged launch pairs its M-tiles (one when there is only one)."""
+    mtiles = (n * (num_heads // num_kv_heads) + 127) // 128
+    return bs * num_kv_heads * ((mtiles + 1) // 2 if paged and mtiles >= 2 else mtiles)
 
 
 def default_splits(bs: int, n: int, num_heads: int, num_kv_heads: int, keys: int) -> int:
