@@ -100,6 +100,18 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     return d;
 }
 __device__ __forceinline__ uint64_t dup2(float a) { return pk2(a, a); }
+// three-input maximum (one instruction; the maximum is exact, so any grouping gives the same value)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// the maximum over the 32 lanes of a full warp in one reduction
+__device__ __forceinline__ float warp_max_f32(float v) {
+    float d;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(d) : "f"(v));
+    return d;
+}
 
 // ------------------------------------------------------------------ warp helpers
 __device__ __forceinline__ uint64_t shfl_u64(uint64_t v, int src) {

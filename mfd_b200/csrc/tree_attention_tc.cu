@@ -148,11 +148,6 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
 // every kPolyEvery-th exponential pair of a row's keys goes to exp2_poly2, the rest to ex2.approx
 constexpr int kPolyEvery = 3;
 
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
 // named barriers: 1 (and 6) = the softmax warps of M-tile 0 (and 1), 2 + q = the PARTS warps of TMEM lane quarter q
 // (one warp: a warp sync)
 template <int N>

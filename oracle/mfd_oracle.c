@@ -370,7 +370,9 @@ static float bf16_to_f32(uint16_t h) {
 /*
  * exp(y) for y <= 0 in float32 by Cody-Waite range reduction (W. J. Cody and W. Waite,
  * "Software Manual for the Elementary Functions", 1980: ln 2 split as 0.693359375 - 2.12194440e-4)
- * and the degree-7 Taylor polynomial of exp on |r| <= ln2/2 evaluated by Horner's rule with fmaf.
+ * and the degree-5 polynomial 1 + c1 r + ... + c5 r^5 of exp on |r| <= ln2/2 (constant term fixed at 1;
+ * fitted for the least maximum relative error, 9.2e-8, by Lawson's iteratively reweighted least squares on
+ * 40001 points) evaluated by Horner's rule with fmaf.
  * Every step is a single correctly rounded IEEE operation, so the CUDA kernel, which performs the
  * same operations with __fmaf_rn / __fmul_rn / __fadd_rn, returns the same bits.
  */
@@ -379,13 +381,11 @@ static float mfd_exp32(float y) {
     float n = nearbyintf(y * 1.44269504088896341f); /* round half to even, as __float2int_rn */
     float r = fmaf(n, -0.693359375f, y);
     r = fmaf(n, 2.12194440e-4f, r);
-    float p = 1.0f / 5040.0f;
-    p = fmaf(p, r, 1.0f / 720.0f);
-    p = fmaf(p, r, 1.0f / 120.0f);
-    p = fmaf(p, r, 1.0f / 24.0f);
-    p = fmaf(p, r, 1.0f / 6.0f);
-    p = fmaf(p, r, 0.5f);
-    p = fmaf(p, r, 1.0f);
+    float p = 0.008290256f;
+    p = fmaf(p, r, 0.041897807f);
+    p = fmaf(p, r, 0.16667636f);
+    p = fmaf(p, r, 0.4999915f);
+    p = fmaf(p, r, 0.9999997f);
     p = fmaf(p, r, 1.0f);
     /* scale by 2^n by adding n to the exponent field: y > -87 gives n >= -126, and n = -126 only
        when r > 0.34, i.e. p > 1, so the result stays a normal number */
