@@ -67,9 +67,13 @@ struct Cfg {
     static constexpr int kGroupThreads = 128 * PARTS;  // the softmax warps of one M-tile
     static constexpr int kSoftmaxThreads = kGroupThreads * TILES;
     static constexpr int kThreads = 64 + kSoftmaxThreads;  // warp 0 producer, warp 1 MMA, then the softmax warps
-    // O of M-tile t at column 128 t; S buffer b at column kSCol + KT b (TILES = 1: b = key tile parity; TILES = 2:
-    // b = M-tile); P (bf16 pairs) over its first KT / 2 columns
-    static constexpr int kSCol = 128 * TILES;
+    // Two parts per row (one M-tile): each part keeps its own O accumulator, running max and sum for its half of
+    // every key tile's columns, so the parts never exchange maxima per tile; the epilogue merges the two.
+    static constexpr bool kDualO = TILES == 1 && PARTS == 2;
+    // O of M-tile t at column 128 t (dual: O of part p at 128 p); S buffer b at column kSCol + KT b (TILES = 1:
+    // b = key tile parity; TILES = 2: b = M-tile); P (bf16 pairs) over its first KT / 2 columns (dual: each part's
+    // P over the first half of its own KT / 2 columns)
+    static constexpr int kSCol = kDualO ? 256 : 128 * TILES;
     static constexpr int kTmemCols = kSCol + 2 * KT <= 256 ? 256 : 512;
     static constexpr int kQBytes = kM * D * 2;    // 32 KB per M-tile: [2 d-halves][128 rows][128 B]
     static constexpr int kKVBytes = KT * D * 2;   // [2 d-halves][KT keys][128 B]
@@ -130,7 +134,8 @@ __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, 
 // the constant term fixed at 1): 1.02e-4, far below the bf16 rounding (2^-9) P gets next.  2^n enters as n << 23
 // added to p's bits (the bits of the rounded sum are 0x4B400000 + n, and 0x4B400000 << 23 vanishes modulo 2^32).
 // x is first clamped to -127: there f = 0 and p = 1 exactly, so the bits are those of +0 -- masked scores (-inf)
-// and NaN give 0 as ex2.approx.ftz gives for -inf.
+// and NaN give 0 as ex2.approx.ftz gives for -inf.  (Arguments stay at or below 8: the lazy rescale keeps every
+// score within 2^8 of the running max.)
 constexpr float kExpC1 = 0.6932827234268188f, kExpC2 = 0.24220797419548035f, kExpC3 = 0.055007610470056534f;
 __device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
     float x0, x1;
@@ -203,6 +208,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                         const __grid_constant__ CUtensorMap tmv, const Params p) {
     constexpr int kKt = C::kKt, kStages = C::kStages, kParts = C::kParts, kOCols = C::kOCols, kTiles = C::kTiles;
     constexpr int kGroupThreads = C::kGroupThreads;
+    constexpr bool kDualO = C::kDualO;
     constexpr int kSoftmaxThreads = C::kSoftmaxThreads, kTmemCols = C::kTmemCols, kSCol = C::kSCol;
     constexpr int kQBytes = C::kQBytes, kKVBytes = C::kKVBytes;
     constexpr int kOffQ = C::kOffQ, kOffK = C::kOffK, kOffV = C::kOffV, kOffX = C::kOffX, kOffBar = C::kOffBar;
@@ -427,9 +433,17 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 tc_fence_after();
                 const uint32_t vaddr = sbase + kOffV + st * kKVBytes;
 #pragma unroll
-                for (int ks = 0; ks < kKt / 16; ++ks)  // P: 16 keys = 8 columns of bf16 pairs per step
-                    umma_ts(tmem + t * 128, tmem + kSCol + sb * kKt + ks * 8,
-                            sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                for (int ks = 0; ks < kKt / 16; ++ks) {  // P: 16 keys = 8 columns of bf16 pairs per step
+                    if (kDualO) {  // keys of the first half into O_0, of the second into O_1
+                        constexpr int kHalf = kKt / 32;  // steps per half
+                        const int hf = ks / kHalf, kk = ks % kHalf;
+                        umma_ts(tmem + hf * 128, tmem + kSCol + sb * kKt + hf * (kKt / 2) + kk * 8,
+                                sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        umma_ts(tmem + t * 128, tmem + kSCol + sb * kKt + ks * 8,
+                                sdesc(vaddr + ks * 2048, kKVBytes / 2, 1024), kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+                    }
+                }
                 umma_commit(&bars[kBarPV + sb]);
             };
             auto wait_kv = [&](int i) {
@@ -587,7 +601,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 for (int j = 0; j < 5; ++j) u[j] = fmax3(u[3 * j], u[3 * j + 1], u[3 * j + 2]);
                 mx = fmaxf(fmax3(u[0], u[1], u[2]), fmax3(u[3], u[4], u[15])) * sc;
             }
-            if (kParts > 1) {
+            if (kParts > 1 && !kDualO) {
                 // the row's max over the parts, through a double-buffered exchange: after this barrier every part
                 // has finished reading S (so P may overwrite it), and a part can run at most one tile ahead
                 xmax[((i & 1) * kParts + part) * kM + rt] = mx;
@@ -595,7 +609,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
 #pragma unroll
                 for (int q = 0; q < kParts; ++q) mx = fmaxf(mx, xmax[((i & 1) * kParts + q) * kM + rt]);
             } else {
-                ok = __all_sync(MFD_FULL_MASK, ok);
+                ok = __all_sync(MFD_FULL_MASK, ok);  // (dual: each part keeps its own running max)
             }
             if (!ok) break;
             float alpha = 1.f;
@@ -631,8 +645,9 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                     upk2(e, e0, e1);
                     pk[jp] = pack_bf16(e0, e1);
                 }
-                // P as bf16 pairs over the first kKt / 2 columns of the S buffer: chunk c's 32 keys = 16 columns
-                tmem_st16u(s_tm + (c_lo >> 1) + 16 * c, pk);
+                // P as bf16 pairs over the first kKt / 2 columns of the S buffer (dual: of this part's own
+                // columns): chunk c's 32 keys = 16 columns.  Every S value of the warp is in registers by now.
+                tmem_st16u(s_tm + (kDualO ? c_lo : (c_lo >> 1)) + 16 * c, pk);
             }
             float l_add;
             {
@@ -648,13 +663,16 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                     ok &= mbar_wait(&bars[kBarPV + (kTiles == 1 ? ((i - 1) & 1) : t)], sph(i - 1), kTries);
                     tc_fence_after();
                 }
+                // (dual: this part's own accumulator, all of its columns)
+                constexpr int kRescaleCols = kDualO ? D : kOCols;
+                const uint32_t obase = tmem + lane_off + (kDualO ? part * 128 : t * 128 + o_lo);
 #pragma unroll
-                for (int oc = 0; oc < kOCols; oc += 32) {
+                for (int oc = 0; oc < kRescaleCols; oc += 32) {
                     float o[32];
-                    tmem_ld32(tmem + lane_off + t * 128 + o_lo + oc, o);
+                    tmem_ld32(obase + oc, o);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) o[j] *= alpha;
-                    tmem_st32(tmem + lane_off + t * 128 + o_lo + oc, o);
+                    tmem_st32(obase + oc, o);
                 }
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -671,8 +689,19 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 tc_fence_after();
             }
             // ---- epilogue: the row sum over the parts, then this part's kOCols columns of O / l
-            float l_row = l_run;
-            if (kParts > 1) {
+            float l_row = l_run, m_fin = m_run;
+            float fself = 1.f, fother = 0.f;  // dual: weights of this part's and the other part's accumulator
+            if (kDualO) {
+                // merge the two parts' (max, sum): each O_p holds its half's sum of 2^(s - m_p) v
+                xmax[part * kM + rt] = m_run;
+                xmax[(2 + part) * kM + rt] = l_run;
+                quarter_sync<kParts>(quarter);
+                const float mo = xmax[(1 - part) * kM + rt], lo = xmax[(3 - part) * kM + rt];
+                m_fin = fmaxf(m_run, mo);
+                fself = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_fin);
+                fother = mo == -INFINITY ? 0.f : fast_exp2(mo - m_fin);
+                l_row = l_run * fself + lo * fother;
+            } else if (kParts > 1) {
                 quarter_sync<kParts>(quarter);  // every part is past its last use of xmax
                 xmax[part * kM + rt] = l_run;
                 quarter_sync<kParts>(quarter);
@@ -685,7 +714,13 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
 #pragma unroll
             for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {
                 float o[32];
-                if (ntiles > 0 && quarter_live) {
+                if (ntiles > 0 && quarter_live && kDualO) {
+                    float o2[32];
+                    tmem_ld32(tmem + lane_off + part * 128 + oc, o);
+                    tmem_ld32(tmem + lane_off + (1 - part) * 128 + oc, o2);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) o[j] = o[j] * fself + o2[j] * fother;
+                } else if (ntiles > 0 && quarter_live) {
                     tmem_ld32(tmem + lane_off + t * 128 + oc, o);
                 } else {
 #pragma unroll
@@ -709,7 +744,7 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
             if (p.splits > 1) {
                 if (part == 0)
                     p.lse_part[((size_t)split * units + unit) * kM + rt] =
-                        l_row > 0.f ? m_run + __log2f(l_row) : -INFINITY;
+                        l_row > 0.f ? m_fin + __log2f(l_row) : -INFINITY;
                 // the last split of this (request, KV head, M-tile) merges all of them
                 __threadfence();
                 group_sync<kGroupThreads>(t);

@@ -57,3 +57,4 @@ def test_exp2_poly_is_monotone_within_rounding():
     x = np.linspace(-20.0, 9.0, 100_001, dtype=np.float32)
     y = exp2_poly(x).astype(np.float64)
     assert np.all(np.diff(y) >= -BOUND * y[1:])
+

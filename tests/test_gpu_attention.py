@@ -192,3 +192,26 @@ def test_tree_attention_rescales_on_growing_scores(n, splits):
     ref = oracle.tree_attention(q[0].float().numpy(), kk[:P], vv[:P], kk[P:], vv[P:], parents, D ** -0.5)
     assert np.abs(out[0].float().cpu().numpy() - ref).max() <= TOL
     assert ops.tree_attention_status() == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2])
+def test_tree_attention_rescales_across_a_wide_score_range(splits):
+    """Scores whose base-2 exponent grows by hundreds along the keys (K scaled by a ramp from 1 to 40): the running
+    max is raised, and O rescaled in TMEM, on most key tiles, and the result is finite and matches the oracle."""
+    from mfd_b200 import ops
+    g = torch.Generator().manual_seed(700 + splits)
+    P, n, H, Hkv, D = 1500, 65, 32, 8, 128
+    parents = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)]
+    ramp = torch.linspace(1.0, 40.0, P + n).view(1, 1, P + n, 1)
+    q = (torch.randn(1, n, H, D, generator=g) * 2).to(torch.bfloat16)
+    k = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5 * ramp).to(torch.bfloat16)
+    v = (torch.randn(1, Hkv, P + n, D, generator=g) * 0.5).to(torch.bfloat16)
+    anc = anc_bits(parents, (n + 63) // 64)[None].to(DEV)
+    out = ops.tree_attention(q.to(DEV), k.to(DEV), v.to(DEV), anc, P, D ** -0.5, splits=splits)
+    kk = k[0].transpose(0, 1).float().numpy()
+    vv = v[0].transpose(0, 1).float().numpy()
+    ref = oracle.tree_attention(q[0].float().numpy(), kk[:P], vv[:P], kk[P:], vv[P:], parents, D ** -0.5)
+    got = out[0].float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= TOL
+    assert ops.tree_attention_status() == 0
