@@ -380,6 +380,7 @@ template <bool UNIT_T>  // temperature exactly 1 (then 1 / T is exactly 1)
 __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kernel(Params p) {
     __shared__ float blk_m[kMaxRounds * kSampleWarps];
     __shared__ float blk_s[kMaxRounds * kSampleWarps];
+    __shared__ double blk_w[kMaxRounds * kSampleWarps];  // block weights, written by the search warp
     __shared__ WalkStage stage;
     __shared__ int flag;
     __shared__ int64_t s_token;
@@ -432,8 +433,7 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
         const int nb = (int)((V + 255) / 256);
         float m = -INFINITY;
         for (int e = lane; e < nb; e += 32) m = fmaxf(m, blk_m[e]);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(MFD_FULL_MASK, m, o));
+        m = warp_max_f32(m);
         auto wblk = [&](int e) -> double {  // the block weight S_b * exp32((M_b - m) / T)
             const float mb = blk_m[e];
             if (mb == -INFINITY) return 0.0;
@@ -455,10 +455,18 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
             return -1;
         };
         const int per = (nb + 31) / 32;
+        // the run sums; each block weight is kept (shared memory) for the walk below.  The unrolled loop lets the
+        // exponentials of several blocks overlap while the sum keeps its left-to-right order.
         double run = 0.0;
-        for (int e = lane * per; e < (lane + 1) * per && e < nb; ++e) run = __dadd_rn(run, wblk(e));
+#pragma unroll 4
+        for (int e = lane * per; e < (lane + 1) * per && e < nb; ++e) {
+            const double w = wblk(e);
+            blk_w[e] = w;
+            run = __dadd_rn(run, w);
+        }
         // P_{L+1} = P_L + R_L in lane order (every lane computes the same sums); lane L keeps P_L
         double P = 0.0, myP = 0.0;
+#pragma unroll
         for (int L = 0; L < 32; ++L) {
             const double r = shfl_f64(run, L);
             if (lane == L) myP = P;
@@ -477,10 +485,11 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
                 // block of run Ls (lane Ls walks its run)
                 int bs = -1;
                 double t2 = 0.0;
+                __syncwarp();  // the block weights of lane Ls's run are in shared memory
                 if (lane == Ls) {
                     double Q = 0.0;
                     for (int e = Ls * per; e < (Ls + 1) * per && e < nb; ++e) {
-                        const double Qn = __dadd_rn(Q, wblk(e));
+                        const double Qn = __dadd_rn(Q, blk_w[e]);
                         if (Qn > t1) {
                             bs = e;
                             t2 = __dsub_rn(t1, Q);
@@ -497,10 +506,14 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
                     const float mb = blk_m[bs];
                     const double sc = (double)exp32_rule(__fmul_rn(__fsub_rn(mb, m), inv_t));
                     const int64_t i0 = 256 * (int64_t)bs + 8 * lane;
-                    auto wj = [&](int j) { return i0 + j < V ? __dmul_rn((double)weight(i0 + j, mb), sc) : 0.0; };
+                    double w8[8];  // this lane's 8 logit weights, each computed once
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) w8[j] = i0 + j < V ? __dmul_rn((double)weight(i0 + j, mb), sc) : 0.0;
                     double cl = 0.0;
-                    for (int j = 0; j < 8; ++j) cl = __dadd_rn(cl, wj(j));
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) cl = __dadd_rn(cl, w8[j]);
                     double B = 0.0, myB = 0.0;
+#pragma unroll
                     for (int l = 0; l < 32; ++l) {
                         const double c = shfl_f64(cl, l);
                         if (lane == l) myB = B;
@@ -515,8 +528,9 @@ __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kerne
                         int64_t hit = -1, lastpos = -1;
                         if (lane == ls) {
                             double a = 0.0;
+#pragma unroll
                             for (int j = 0; j < 8; ++j) {
-                                const double wv = wj(j);
+                                const double wv = w8[j];
                                 const double an = __dadd_rn(a, wv);
                                 if (wv > 0.0) lastpos = i0 + j;
                                 if (hit < 0 && an > t3 && wv > 0.0) hit = i0 + j;
