@@ -490,9 +490,11 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
     } else {
         // ---------------------------------------------------------------- softmax warps
         // warp w: M-tile t = (w - 2) / (4 kParts) of the CTA, TMEM lane quarter w % 4, key columns
-        // [kCols part, kCols part + kCols) of each tile with part = ((w - 2) mod 4 kParts) / 4; the kParts warps of
-        // a quarter exchange their row maxima (and at the end their row sums) through shared memory.  With two
-        // M-tiles each has its own warps, so one M-tile's softmax runs while the other's P V and scores do.
+        // [kCols part, kCols part + kCols) of each tile with part = ((w - 2) mod 4 kParts) / 4.  With two parts per
+        // row (the launched single-M-tile configuration) each part keeps its own O accumulator, running max and
+        // sum, merged with the other part's in the epilogue; with more parts they exchange their row maxima per
+        // tile (and their row sums at the end) through shared memory.  With two M-tiles each has its own warps, so
+        // one M-tile's softmax runs while the other's P V and scores do.
         const int wg = warp - 2;
         const int t = wg / (4 * kParts);
         const int quarter = warp & 3;
@@ -512,8 +514,8 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
         // are, and the P V rows they feed (rows are independent in the MMA) are never stored
         const bool quarter_live = row0 + quarter * 32 < nrows;
         const int loop_tiles = t < ntl ? ntiles : 0;  // (a CTA's last M-tile may have no second one)
-        // the loop ends for all warps of a quarter together: only at the max exchange, where their ok flags are
-        // AND-ed (a warp leaving alone would leave its partners waiting at a named barrier)
+        // with a per-tile max exchange the loop ends for all warps of a quarter together, at the exchange, where
+        // their ok flags are AND-ed (a warp leaving alone would leave its partners waiting at a named barrier)
         for (int i = 0; i < loop_tiles; ++i) {
             const int key0 = k_lo + i * kKt;
             const int sb = kTiles == 1 ? (i & 1) : t;
