@@ -17,7 +17,9 @@
 // reaches the floor (rare) appends those elements with shared atomics to the CTA's candidate buffer.  The floor
 // comes from the piece's first batch: each warp sorts its 32 lane maxima and the floor is the r-th largest over
 // the CTA, found by rank, with r chosen so that about 3.5 k elements of the whole piece are expected to pass (a
-// lower target sorts fewer candidates but fails the verification below more often, and a rescan costs more).
+// lower target sorts fewer candidates but fails the verification below more often, and a rescan costs more).  A
+// second, upper floor (about 2 k expected) is found by the same rank search: when more candidates than one per
+// thread were collected and at least k of them reach it, only those are sorted (one selection pass instead of two).
 // That floor is speculative and is verified at the end of the piece: if at least k candidates were collected
 // (and the buffer did not overflow), every element of the piece's top k is among them -- an element below the
 // floor has at least k collected elements above it.  Otherwise the piece is scanned again (an L2 hit) against a
@@ -148,9 +150,12 @@ struct Smem {
     float2 ms[kWarps];
     float wthr[kWarps];
     int count;
+    int count_hi;
     int flag;
     int spec;        // a speculative floor was found
     float floor_v;   // speculative floor (value)
+    int spec_hi;     // an upper speculative floor was found
+    float floor_hi;  // upper speculative floor (value)
     float logz;
 };
 
@@ -456,8 +461,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         {
             const int64_t sample = min(nvec, (int64_t)kBatch) * VE + (hb - c0) + (c1 - tb);
             const int64_t np = c1 - c0;
+            // two speculative floors: about 3.5 k and 2 k expected elements of the piece at or above them
             int r = (int)((7LL * k * sample + 2 * np - 1) / (2 * np));
             r = max(r, 1);
+            const int r_hi = max((int)((2LL * k * sample + np - 1) / np), 1);
             uint64_t r1[1] = {((uint64_t)ord_f32(lmax) << 32) | (uint64_t)(~(uint32_t)threadIdx.x)};
             warp_sort_desc<1>(r1);
             const int q = (k + kWarps - 1) / kWarps;
@@ -466,7 +473,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
             sm.cand[threadIdx.x] = r1[0];  // (the candidate buffer is free until the floors are known)
             if (threadIdx.x == 0) {
                 sm.spec = 0;
+                sm.spec_hi = 0;
                 sm.count = 0;
+                sm.count_hi = 0;
             }
             __syncthreads();
             if (r <= kThreads) {
@@ -477,6 +486,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
                 if (rank == r - 1) {
                     sm.floor_v = unord_f32((uint32_t)(r1[0] >> 32));
                     sm.spec = 1;
+                }
+                if (rank == r_hi - 1) {
+                    sm.floor_hi = unord_f32((uint32_t)(r1[0] >> 32));
+                    sm.spec_hi = 1;
                 }
             }
             __syncthreads();
@@ -595,9 +608,27 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) topk_logz_kernel(const P
         __syncthreads();
 
         // ---- verify the speculative floor; select the top KP
-        const int cnt = sm.count;
-        const int n = cnt < kCap ? cnt : kCap;
+        int cnt = sm.count;
+        const float fl_hi = sm.spec_hi ? fmaxf(fl, sm.floor_hi) : fl;
         __syncthreads();  // every thread has read the count before the selection may reset it
+        if (cnt > kWarps * 32 && cnt <= kCap / 2) {
+            // more candidates than one key per thread: when at least k of them reach the upper floor (about 2 k
+            // expected), those alone hold the top k (any other has k collected keys above it), and sorting them
+            // takes one pass of the selection instead of two.  They are compacted into the buffer's second half,
+            // then moved to its front.
+            for (int e = threadIdx.x; e < cnt; e += kThreads) {
+                const uint64_t key = sm.cand[e];
+                if (key_value(key) >= fl_hi) sm.cand[kCap / 2 + atomicAdd(&sm.count_hi, 1)] = key;
+            }
+            __syncthreads();
+            const int nh = sm.count_hi;
+            if (nh >= k && nh <= kWarps * 32) {
+                for (int e = threadIdx.x; e < nh; e += kThreads) sm.cand[e] = sm.cand[kCap / 2 + e];
+                cnt = nh;
+            }
+            __syncthreads();
+        }
+        const int n = cnt < kCap ? cnt : kCap;
         if (cnt > kCap || n < k) {
             rescan_select<KP, BF16>(sm, base, c0, c1, bv, k);
         } else {
