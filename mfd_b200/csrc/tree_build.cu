@@ -617,17 +617,19 @@ __global__ void __launch_bounds__(kThreads) mixture_heap1_kernel(Params p) {
 // order, and restricted to one mode it is the best-first enumeration of that mode alone -- except where two live
 // entries of one mode have equal keys (their order then depends on global node ids).  This kernel therefore:
 //   1. runs the K modes' enumerations at once, one warp per mode: the mode's live entries (one per open sibling
-//      group, at most B + 1) sit in registers, three per lane, and a pop is a warp-wide minimum (redux.sync), two
-//      ballots and the owner lane computing both successors.  Round 1 pops B / 4 entries per mode and merges them
+//      group, at most B + 1) sit in registers, three per lane, each with its two successors already computed, and a
+//      pop is a warp-wide minimum (redux.sync), one ballot and a hand-over of the first child to the lane of its new
+//      group; the successors of the two entries made live follow.  Round 1 pops B / 4 entries per mode and merges them
 //      (steps 2-4); the B-th distinct prefix found bounds the tree's last node, so round 2 pops only the modes
 //      whose next entry precedes that bound, up to it (or up to B entries when round 1 found fewer than B
 //      prefixes -- B per mode always suffice, since the first B distinct nodes contain at most B entries of any
 //      mode), and merges again;
 //   2. ranks every popped entry in the merged order (key, then mode) by fixed-step searches in the other modes'
 //      lists, run side by side;
-//   3. merges equal prefixes: every popped entry carries a hash of its token path, entries are grouped through a
-//      shared-memory hash table (atomicCAS / atomicMin give each group its least merged position), and every
-//      grouped entry is compared token by token with that first occurrence;
+//   3. merges equal prefixes: every popped entry gets a hash of its token path (summed up its parent chain by
+//      pointer jumping), entries are grouped through a shared-memory hash table (atomicCAS / atomicMin give each
+//      group its least merged position), and every grouped entry is compared token by token with that first
+//      occurrence;
 //   4. numbers the first occurrences in merged order by a block scan: the first B are the nodes, in the heap's
 //      pop order.
 // A mode whose warp minimum is not unique (an exact key tie), a successor with a smaller key than its generator
@@ -640,7 +642,7 @@ constexpr int kFastMaxB = 32 * kFastSlots - 1;
 
 struct FastSmem {
     uint32_t* ekey;   // [K][B] popped keys, in each mode's pop order (non-decreasing)
-    int32_t* etok;    // [K][B] token
+    int32_t* etok;    // [K][B] token (filled by the merge)
     int16_t* epl;     // [K][B] pop index of the parent entry in the same mode (-1: the root)
     uint8_t* edep;    // [K][B] depth
     int16_t* epos;    // [K][B] merged position
@@ -648,7 +650,9 @@ struct FastSmem {
     int16_t* eslot;   // [K][B] dedup hash slot
     int16_t* pnid;    // [K B] node id by merged position (0: not a node)
     int16_t* pent;    // [K B] entry (mode * B + pop index) by merged position
-    uint64_t* ehash;  // [K][B] hash of the entry's token path (root first)
+    uint16_t* eidx;   // [K][B] index of the entry in its mode's [L][k] table
+    uint64_t* ehash;  // [K][B] hash of the entry's token path (filled by the merge)
+    int16_t* ejmp;    // [K][B] pointer-jumping ancestor (merge scratch)
     uint64_t* dkey;   // [dcap] dedup keys (path hashes)
     int32_t* dval;    // [dcap] least merged position holding the key
 };
@@ -660,6 +664,8 @@ __device__ FastSmem carve_fast(const Params& p, unsigned char*& q, int dcap) {
     f.dval = (int32_t*)smem_take(q, 4 * (size_t)dcap);
     f.ehash = (uint64_t*)smem_take(q, 8 * KB);
     f.pent = (int16_t*)smem_take(q, 2 * KB);
+    f.eidx = (uint16_t*)smem_take(q, 2 * KB);
+    f.ejmp = (int16_t*)smem_take(q, 2 * KB);
     f.ekey = (uint32_t*)smem_take(q, 4 * KB);
     f.etok = (int32_t*)smem_take(q, 4 * KB);
     f.epl = (int16_t*)smem_take(q, 2 * KB);
@@ -673,7 +679,7 @@ __device__ FastSmem carve_fast(const Params& p, unsigned char*& q, int dcap) {
 static size_t fast_smem_bytes(int K, int B, int dcap) {
     auto r16 = [](size_t v) { return (v + 15) & ~(size_t)15; };
     const size_t KB = (size_t)K * B;
-    return r16(8 * (size_t)dcap) + r16(4 * (size_t)dcap) + r16(8 * KB) + r16(2 * KB) + 2 * r16(4 * KB) +
+    return r16(8 * (size_t)dcap) + r16(4 * (size_t)dcap) + r16(8 * KB) + 3 * r16(2 * KB) + 2 * r16(4 * KB) +
            5 * r16(2 * KB) + r16(KB);
 }
 __host__ __device__ inline int fast_dcap(int K, int B) {
@@ -682,17 +688,35 @@ __host__ __device__ inline int fast_dcap(int K, int B) {
     return d;
 }
 
-// Hash of a token path, extended one token at a time (splitmix64 finaliser of the previous hash and the token).
-// It only groups candidate duplicates: every grouped pair is compared token by token before it is trusted.
-constexpr uint64_t kRootPath = 0x243F6A8885A308D3ull;
-__device__ __forceinline__ uint64_t path_hash(uint64_t h, int32_t token) {
-    uint64_t z = h ^ ((uint64_t)(uint32_t)token * 0x9E3779B97F4A7C15ull);
+// Hash of a token path: the sum over its nodes of a splitmix64 finaliser of (token, depth), so that the merge can
+// form every entry's hash at once by pointer jumping, off the pop loop.  It only groups candidate duplicates: every
+// grouped pair is compared token by token before it is trusted.
+__device__ __forceinline__ uint64_t path_term(int32_t token, int depth) {
+    uint64_t z = (((uint64_t)(uint32_t)token << 5) | (uint64_t)depth) * 0x9E3779B97F4A7C15ull + 0x243F6A8885A308D3ull;
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    z ^= z >> 31;
-    return z == kEmptyHash ? z - 1 : z;
+    return z ^ (z >> 31);
 }
 
+// The successors of a live entry of rank r at depth d (1 <= d <= L) with log-weight w, in double as the reference
+// accumulates them (hf/tree_build_ext.py:190-199): the next sibling (w - lp[d][r]) + lp[d][r + 1] and the first
+// child w + lp[d + 1][0], with their mixture keys (kNoKey where there is none).  lpm is the mode's [L][k] table.
+// Indices are clamped, so lanes that evaluate it on state they then discard stay inside the table.
+__device__ __forceinline__ void fast_successors(const float* lpm, int k, int L, float pr, double w, int r, int d,
+                                                uint32_t& nk, double& nw, uint32_t& ck, double& cw) {
+    const int dc = min(max(d, 1), L), rc = min(max(r, 0), k - 1);
+    const float* row = lpm + (dc - 1) * k;
+    const float lr = row[rc], lr1 = row[min(rc + 1, k - 1)];
+    const float lc = lpm[min(dc, L - 1) * k];
+    nw = (w - (double)lr) + (double)lr1;
+    cw = w + (double)lc;
+    const uint32_t kn = mix_key(nw, pr), kc = mix_key(cw, pr);
+    nk = r + 1 < k ? kn : kNoKey;
+    ck = d < L ? kc : kNoKey;
+}
+
+// KMAX: 8 or 16, a bound on K that sizes the rank searches of the merge
+template <int KMAX>
 __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ int sh_cnt[16], sh_done[16];
@@ -711,18 +735,22 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
     if (threadIdx.x == 0) sh_bad = 0;
     __syncthreads();
 
-    // ---- 1. per-mode best-first enumeration, warp m = mode m.  Three live-entry slots per lane, as scalars (slot
-    // t of lane l holds group 32 t + l); the state persists across the two rounds.
+    // ---- 1. per-mode best-first enumeration, warp m = mode m.  Slot t of lane l holds group 32 t + l: the key of
+    // its live entry, the entry's meta ((parent pop index + 1) << 16 | depth << 11 | rank), and the entry's two
+    // successors, computed when it became live -- the next sibling (key n, log-weight v) and the first child (c, u).
+    // A pop then only moves precomputed values; the double-precision successors of the two entries it makes live
+    // come after.  The state persists across the two rounds.
     const int m = warp;
     const float pr = warp < K ? s.prior[m] : 0.f;
-    uint32_t k0 = kNoKey, k1 = kNoKey, k2 = kNoKey;
-    double w0 = 0.0, w1 = 0.0, w2 = 0.0;
-    int r0 = 0, r1 = 0, r2 = 0, d0 = 0, d1 = 0, d2 = 0, q0 = 0, q1 = 0, q2 = 0;
+    const float* lpm = s.lp + (size_t)(warp < K ? m : 0) * L * k;
+    uint32_t k0 = kNoKey, k1 = kNoKey, k2 = kNoKey, a0 = 0, a1 = 0, a2 = 0;
+    uint32_t n0 = kNoKey, n1 = kNoKey, n2 = kNoKey, c0 = kNoKey, c1 = kNoKey, c2 = kNoKey;
+    double v0 = 0.0, v1 = 0.0, v2 = 0.0, u0 = 0.0, u1 = 0.0, u2 = 0.0;
     if (warp < K && lane == 0) {  // group 0: the root's children, rank 0 first
-        w0 = (double)s.lp[(m * L) * k];
-        k0 = mix_key(w0, pr);
-        d0 = 1;
-        q0 = -1;
+        const double w = (double)lpm[0];
+        k0 = mix_key(w, pr);
+        a0 = 1u << 11;
+        fast_successors(lpm, k, L, pr, w, 0, 1, n0, v0, c0, u0);
     }
     int groups = 1, npop = 0, bad = 0;
     // pop while fewer than `limit` entries are out and the next entry precedes (ukey, umode) in the merged order
@@ -732,71 +760,59 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
             const int i = npop;
             const uint32_t wmin = __reduce_min_sync(MFD_FULL_MASK, min(k0, min(k1, k2)));
             if (wmin == kNoKey || wmin > ukey || (wmin == ukey && m > umode)) break;
-            const int mine = (k0 == wmin) + (k1 == wmin) + (k2 == wmin);
-            const uint32_t bal = __ballot_sync(MFD_FULL_MASK, mine > 0);
-            const uint32_t multi = __ballot_sync(MFD_FULL_MASK, mine > 1);
-            if ((bal & (bal - 1)) | multi) {  // an exact tie inside the mode
+            const bool h0 = k0 == wmin, h1 = k1 == wmin, h2 = k2 == wmin;
+            const uint32_t bal = __ballot_sync(MFD_FULL_MASK, h0 || h1 || h2);
+            if (bal & (bal - 1)) {  // an exact tie inside the mode
                 bad = 1;
                 break;
             }
             const int owner = __ffs(bal) - 1;
-            // the owner pops the entry and computes both successors: the sibling stays in its slot, the first child
-            // (a new group) goes to the lane and slot of group `groups`
-            uint32_t ck = kNoKey;
-            double cw = 0.0;
-            int cdep = 0, ptok = 0, ppar = 0, pd = 0;
-            if (lane == owner) {
-                const int sl = k0 == wmin ? 0 : (k1 == wmin ? 1 : 2);
-                const double w = sl == 0 ? w0 : (sl == 1 ? w1 : w2);
-                const int r = sl == 0 ? r0 : (sl == 1 ? r1 : r2);
-                const int d = sl == 0 ? d0 : (sl == 1 ? d1 : d2);
-                const int par = sl == 0 ? q0 : (sl == 1 ? q1 : q2);
-                const int row = (m * L + d - 1) * k;
-                const float lp_r = s.lp[row + r];
-                const float lp_r1 = r + 1 < k ? s.lp[row + r + 1] : 0.f;
-                const float lp_c = d < L ? s.lp[(m * L + d) * k] : 0.f;
-                const int32_t tok = s.ids[row + r];
-                uint32_t nk = kNoKey;
-                double nw = 0.0;
-                if (r + 1 < k) {  // the sibling: (logw - lp[rank]) + lp[rank + 1] in double
-                    nw = (w - (double)lp_r) + (double)lp_r1;
-                    nk = mix_key(nw, pr);
-                    if (nk < wmin) bad = 1;
-                }
-                if (d < L) {  // the first child: logw + lp[depth][0]
-                    cw = w + (double)lp_c;
-                    ck = mix_key(cw, pr);
-                    if (ck < wmin) bad = 1;
-                    cdep = d + 1;
-                }
-                if (sl == 0) { k0 = nk; w0 = nw; r0 = r + 1; }
-                else if (sl == 1) { k1 = nk; w1 = nw; r1 = r + 1; }
-                else { k2 = nk; w2 = nw; r2 = r + 1; }
-                ptok = tok;
-                ppar = par;
-                pd = d;
-            }
-            // hand the child over first (the next pop waits on it), then record the popped entry
-            cdep = __shfl_sync(MFD_FULL_MASK, cdep, owner);
-            if (cdep > 0) {
-                ck = __shfl_sync(MFD_FULL_MASK, ck, owner);
-                cw = __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(cw), owner));
-                const int g = groups++;
-                if (lane == (g & 31)) {
-                    const int sl = g >> 5;
-                    if (sl == 0) { k0 = ck; w0 = cw; r0 = 0; d0 = cdep; q0 = i; }
-                    else if (sl == 1) { k1 = ck; w1 = cw; r1 = 0; d1 = cdep; q1 = i; }
-                    else { k2 = ck; w2 = cw; r2 = 0; d2 = cdep; q2 = i; }
-                }
-            }
-            __syncwarp();  // the parent's path hash (an earlier pop, maybe by another lane) is visible
-            if (lane == owner) {
+            const bool own = lane == owner;
+            // the popped entry, as the owner holds it
+            const uint32_t a = h0 ? a0 : (h1 ? a1 : a2);
+            const uint32_t sk = h0 ? n0 : (h1 ? n1 : n2);
+            const double sw = h0 ? v0 : (h1 ? v1 : v2);
+            const uint32_t ck = h0 ? c0 : (h1 ? c1 : c2);
+            const double cw = h0 ? u0 : (h1 ? u1 : u2);
+            const int r = (int)(a & 2047u), d = (int)((a >> 11) & 31u);
+            // a second slot of the owner at the same key, or a successor that rounds below its generator
+            if (own && ((int)h0 + (int)h1 + (int)h2 > 1 || sk < wmin || ck < wmin)) bad = 1;
+            // the first child opens group `groups` (lane groups % 32, slot groups / 32)
+            const uint32_t hk = __shfl_sync(MFD_FULL_MASK, ck, owner);
+            const double hw = shfl_f64(cw, owner);
+            const int hd = __shfl_sync(MFD_FULL_MASK, d, owner);
+            if (own) {
                 ekey[i] = wmin;
-                f.etok[m * B + i] = ptok;
-                f.epl[m * B + i] = (int16_t)ppar;
-                f.edep[m * B + i] = (uint8_t)pd;
-                f.ehash[m * B + i] = path_hash(ppar < 0 ? kRootPath : f.ehash[m * B + ppar], ptok);
+                f.eidx[m * B + i] = (uint16_t)((d - 1) * k + r);
+                f.epl[m * B + i] = (int16_t)((int)(a >> 16) - 1);
+                f.edep[m * B + i] = (uint8_t)d;
             }
+            const int g = groups;
+            const bool child = hd < L;
+            groups += child ? 1 : 0;
+            const bool recv = child && lane == (g & 31);
+            const int rs = g >> 5;
+            // successors of the owner's new live entry (the sibling) and of the new group's first entry
+            uint32_t snk, sck, cnk, cck;
+            double snw, scw, cnw, ccw;
+            fast_successors(lpm, k, L, pr, sw, r + 1, d, snk, snw, sck, scw);
+            fast_successors(lpm, k, L, pr, hw, 0, hd + 1, cnk, cnw, cck, ccw);
+            const uint32_t sa = (a & ~2047u) | (uint32_t)(r + 1);
+            const uint32_t ca = ((uint32_t)(i + 1) << 16) | ((uint32_t)(hd + 1) << 11);
+#define MFD_SLOT_UPDATE(t, kt, at, nt, vt, ct, ut)                     \
+    {                                                                  \
+        const bool po = own && h##t, pr_ = recv && rs == t;            \
+        kt = po ? sk : (pr_ ? hk : kt);                                \
+        at = po ? sa : (pr_ ? ca : at);                                \
+        nt = po ? snk : (pr_ ? cnk : nt);                              \
+        vt = po ? snw : (pr_ ? cnw : vt);                              \
+        ct = po ? sck : (pr_ ? cck : ct);                              \
+        ut = po ? scw : (pr_ ? ccw : ut);                              \
+    }
+            MFD_SLOT_UPDATE(0, k0, a0, n0, v0, c0, u0)
+            MFD_SLOT_UPDATE(1, k1, a1, n1, v1, c1, u1)
+            MFD_SLOT_UPDATE(2, k2, a2, n2, v2, c2, u2)
+#undef MFD_SLOT_UPDATE
         }
         bad = __any_sync(MFD_FULL_MASK, bad);
         if (lane == 0) {
@@ -812,10 +828,9 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
     auto merged_pos = [&](int mm, int i, uint32_t kv) {
         int pos = i;
 #pragma unroll
-        for (int m2 = 0; m2 < 16; ++m2) {
-            if (m2 >= K || m2 == mm) continue;
+        for (int m2 = 0; m2 < KMAX; ++m2) {
+            const int cnt = (m2 < K && m2 != mm) ? sh_cnt[m2] : 0;
             const uint32_t* ek = f.ekey + m2 * B;
-            const int cnt = sh_cnt[m2];
             const uint64_t lim = (uint64_t)kv + (m2 < mm ? 1u : 0u);  // count keys < lim
             int base = 0;
 #pragma unroll
@@ -848,15 +863,58 @@ __global__ void __launch_bounds__(kFastThreads) mixture_fast_kernel(Params p) {
             sh_ukey = kNoKey;
             sh_umode = K;
         }
+        // tokens, and the path hashes by pointer jumping: an entry's sum starts as its own term and its pointer as
+        // its parent; each round adds the pointed-to entry's partial sum and moves the pointer to that entry's
+        // pointer, so ceil(log2(depth)) rounds reach the root
+        for (int x = threadIdx.x; x < KB; x += kFastThreads) {
+            const int mm = x / B, i = x - mm * B;
+            int jmp = -1;
+            if (i < sh_cnt[mm]) {
+                const int32_t tok = s.ids[(size_t)mm * L * k + f.eidx[x]];
+                f.etok[x] = tok;
+                f.ehash[x] = path_term(tok, f.edep[x]);
+                const int pl = f.epl[x];
+                jmp = pl < 0 ? -1 : mm * B + pl;
+            }
+            f.ejmp[x] = (int16_t)jmp;
+        }
         __syncthreads();
+        for (;;) {
+            constexpr int kPer = (16 * kFastMaxB + kFastThreads - 1) / kFastThreads;
+            uint64_t nh[kPer];
+            int na[kPer];
+            bool act[kPer];
+            int any = 0;
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int x = threadIdx.x + j * kFastThreads;
+                const int a = x < KB ? f.ejmp[x] : -1;
+                act[j] = a >= 0;
+                if (act[j]) {
+                    nh[j] = f.ehash[x] + f.ehash[a];
+                    na[j] = f.ejmp[a];
+                    any = 1;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int x = threadIdx.x + j * kFastThreads;
+                if (act[j]) {
+                    f.ehash[x] = nh[j];
+                    f.ejmp[x] = (int16_t)na[j];
+                }
+            }
+            if (!__syncthreads_or(any)) break;
+        }
         // positions, and each path's least position through the table of path hashes
         for (int x = threadIdx.x; x < KB; x += kFastThreads) {
             const int mm = x / B, i = x - mm * B;
             if (i >= sh_cnt[mm]) continue;
+            const uint64_t hk = f.ehash[x] == kEmptyHash ? kEmptyHash - 1 : f.ehash[x];
             const int pos = merged_pos(mm, i, f.ekey[x]);
             f.epos[x] = (int16_t)pos;
             f.pent[pos] = (int16_t)x;
-            const uint64_t hk = f.ehash[x];
             uint32_t h = (uint32_t)(hk >> 32) & (uint32_t)(dcap - 1);
             for (int t = 0; t < dcap; ++t) {
                 const unsigned long long prev =
@@ -1059,13 +1117,13 @@ extern "C" int mfd_build_trees(const float* top_logp, const void* top_ids, int i
         const int dcap = tree::fast_dcap((int)num_modes, (int)budget);
         const size_t fsmem = h1_smem + tree::fast_smem_bytes((int)num_modes, (int)budget, dcap);
         if (fsmem <= 220 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(tree::mixture_fast_kernel,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
+            auto kern = num_modes <= 8 ? tree::mixture_fast_kernel<8> : tree::mixture_fast_kernel<16>;
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
             if (e != cudaSuccess) {
                 set_error("mfd_build_trees: %s", cudaGetErrorString(e));
                 return MFD_ERR_CUDA;
             }
-            tree::mixture_fast_kernel<<<(unsigned)bs, tree::kFastThreads, fsmem, (cudaStream_t)stream>>>(p);
+            kern<<<(unsigned)bs, tree::kFastThreads, fsmem, (cudaStream_t)stream>>>(p);
             MFD_CHECK_LAUNCH("mfd_build_trees");
             return MFD_OK;
         }
