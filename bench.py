@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfd|reference] [--requests R]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU; the driver's launch)
     python bench.py --config C                             (one BASELINE config's kernels alone, C = 0..3)
+    python bench.py --north-star                           (the north-star step alone: batch 1, greedy)
     python bench.py --kernel K                             (one kernel alone, L2 flushed between launches: a kernel
                                                             of the batch step -- logits_step, tree_build, attention,
                                                             accept --, of the commit step -- commit_kv, gdn_commit --,
@@ -856,6 +857,7 @@ def main():
     ap.add_argument("--requests-per-gpu", type=int, default=REQUESTS_PER_GPU, help="--kernel lines only")
     ap.add_argument("--config", type=int, default=None, help="time one BASELINE config's kernels alone (1 GPU)")
     ap.add_argument("--no-extras", action="store_true", help="skip north_star / e2e / cpu_baseline")
+    ap.add_argument("--north-star", action="store_true", help="time only the north-star step (1 GPU)")
     ap.add_argument("--kernel", default=None,
                     choices=["logits_step", "tree_build", "attention", "accept", "commit_kv", "gdn_commit",
                              "paged_mode_attn"],
@@ -900,6 +902,10 @@ def main():
         print(json.dumps(fn(args.kernel, args.steps, args.warmup, args.requests_per_gpu)))
         return
 
+    if args.north_star:
+        torch.cuda.set_device(0)
+        print(json.dumps(north_star(torch.device("cuda", 0), args.steps, args.warmup)))
+        return
     if args.config is not None:
         torch.cuda.set_device(0)
         print(json.dumps(config_line(args.config, max(args.steps, 10), args.warmup)))
