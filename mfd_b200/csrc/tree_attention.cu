@@ -36,7 +36,7 @@ WsLayout ws_layout(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_head
 
 extern "C" int64_t mfd_tree_attention_tickets(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads) {
     if (bs <= 0 || n <= 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads) return 1;
-    return ws_layout(bs, n, num_heads, num_kv_heads, 1).units;
+    return 3 * ws_layout(bs, n, num_heads, num_kv_heads, 1).units;  // [arrived, claimed, finished] per unit
 }
 
 extern "C" size_t mfd_tree_attention_workspace(int64_t bs, int64_t n, int64_t num_heads, int64_t num_kv_heads,
@@ -82,8 +82,8 @@ extern "C" int mfd_tree_attention(const void* q, int64_t sq_b, int64_t sq_n, int
         set_error("mfd_tree_attention: workspace of %zu bytes needed", wl.total);
         return MFD_ERR_INVALID;
     }
-    if (splits > 1 && (!tickets || tickets_len < wl.units)) {
-        set_error("mfd_tree_attention: a zeroed ticket buffer of %lld words is needed", (long long)wl.units);
+    if (splits > 1 && (!tickets || tickets_len < 3 * wl.units)) {
+        set_error("mfd_tree_attention: a zeroed ticket buffer of %lld words is needed", (long long)(3 * wl.units));
         return MFD_ERR_INVALID;
     }
     // TMA: 16-byte aligned bases and strides
@@ -181,8 +181,9 @@ extern "C" int mfd_paged_mode_attention(const void* q, int64_t sq_t, int64_t sq_
         set_error("mfd_paged_mode_attention: workspace of %zu bytes needed", wl.total);
         return MFD_ERR_INVALID;
     }
-    if (splits > 1 && (!tickets || tickets_len < wl.units)) {
-        set_error("mfd_paged_mode_attention: a zeroed ticket buffer of %lld words is needed", (long long)wl.units);
+    if (splits > 1 && (!tickets || tickets_len < 3 * wl.units)) {
+        set_error("mfd_paged_mode_attention: a zeroed ticket buffer of %lld words is needed",
+                  (long long)(3 * wl.units));
         return MFD_ERR_INVALID;
     }
     char* ws = (char*)(((uintptr_t)workspace + 255) & ~(uintptr_t)255);

@@ -26,8 +26,10 @@
 //                TMEM only when a row's running max grows by more than 2^8.  A quarter whose 32 rows are all padding
 //                (the last M-tile holds 4 of 128 rows for 65 x 4) keeps only the barrier protocol.  Epilogue
 //                through a shared-memory stage so every store is coalesced.
-// Splits: each CTA writes (O / l, log2 lse) partials; the last CTA of a (request, KV head, M-tile) (a ticket)
-// merges all splits and writes bf16 out.  With one split the CTA writes out directly.
+// Splits: each CTA writes (O / l, log2 lse) partials; the splits of a (request, KV head, M-tile) then merge them
+// together, 32 output columns at a time, claimed by an atomic counter: the last split to arrive always takes part,
+// the others when they see every partial stored within a short bounded wait.  With one split the CTA writes out
+// directly.
 //
 // TMEM: O at columns [0, 128), S[0] and S[1] after it (one column per tile key each): 512 columns allocated.
 // Every mbarrier wait is bounded; when one gives up the CTA records a nonzero status, finishes without waiting
@@ -108,6 +110,16 @@ struct Cfg {
 using CfgRow = Cfg<128, 3, 2, 1>;
 using CfgPair = Cfg<128, 2, 1, 1, 2>;
 constexpr uint32_t kTries = 1u << 20;              // bounded mbarrier waits
+// The split merge: output column slices of 32 that the splits of a unit claim, and the bounded wait of a split for
+// the others' partials (32 polls, about 10-20 us; the splits of a unit normally run in one wave and arrive within a
+// microsecond or two of each other).
+constexpr int kMergeSlices = D / 32;
+constexpr int kMergeSpins = 32;
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* ptr) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
 // K / V tiles are prefetched into L2 this many tiles before their load into the ring, so the ring's loads see L2
 // latency instead of DRAM latency (a stage is refilled less than one tile period before its scores are needed)
 constexpr int kPrefetchAhead = 4;
@@ -747,18 +759,27 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                 if (part == 0)
                     p.lse_part[((size_t)split * units + unit) * kM + rt] =
                         l_row > 0.f ? m_fin + __log2f(l_row) : -INFINITY;
-                // the last split of this (request, KV head, M-tile) merges all of them
+                // The splits of this (request, KV head, M-tile) merge their partials together: counters
+                // [arrived, claimed, finished] per unit.  The last split to arrive knows every partial is stored; a
+                // split that sees the arrival count complete within a short bounded wait joins it.  Each takes slices
+                // of 32 output columns from the claim counter until none is left, so a split that gave up only
+                // leaves its share to the others.  The last split to finish resets the counters.
                 __threadfence();
                 group_sync<kGroupThreads>(t);
+                unsigned int* tk = p.tickets + 3 * unit;
                 if (gtid == 0) {
-                    unsigned int* tk = p.tickets + unit;
                     const unsigned int tick = atomicAdd(tk, 1u);
-                    const int last = tick == (unsigned int)(p.splits - 1);
-                    if (last) *tk = 0u;  // ready for the next launch
-                    shared_flags[t] = last;
+                    int go = tick == (unsigned int)(p.splits - 1);
+                    for (int it = 0; !go && it < kMergeSpins; ++it) {
+                        __nanosleep(256);
+                        go = ld_acquire_u32(tk) >= (unsigned int)p.splits;
+                    }
+                    shared_flags[t] = go;
                 }
                 group_sync<kGroupThreads>(t);
-                if (shared_flags[t]) {
+                const bool go = shared_flags[t] != 0;
+                group_sync<kGroupThreads>(t);  // every thread has read the flag before the slot carries slices
+                if (go) {
                     __threadfence();
                     const float* lse = p.lse_part + unit * kM + rt;  // split sp at lse[sp * units * kM]
                     float m = -INFINITY;
@@ -770,17 +791,22 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
 #pragma unroll
                         for (int u = 0; u < 8; ++u) m = fmaxf(m, l[u]);
                     }
-#pragma unroll 1
-                    for (int oc = o_lo; oc < o_lo + kOCols; oc += 32) {  // 32 columns (8 float4 chunks) at a time
-                        float acc[8][4];
+                    // a slice: this thread's row rt, columns [32 sl + kSliceCols part, + kSliceCols)
+                    constexpr int kSliceCols = 32 / kParts, kSliceChunks = kSliceCols / 4;
+                    constexpr int kFly = 16 / kSliceChunks;  // splits' loads in flight: 16 float4 a thread
+                    for (;;) {
+                        if (gtid == 0) shared_flags[t] = (int)atomicAdd(tk + 1, 1u);
+                        group_sync<kGroupThreads>(t);
+                        const int sl = shared_flags[t];
+                        if (sl >= kMergeSlices) break;  // (the same value for the whole group)
+                        const int c0 = 32 * sl + kSliceCols * part;
+                        float acc[kSliceChunks][4];
 #pragma unroll
-                        for (int c = 0; c < 8; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
+                        for (int c = 0; c < kSliceChunks; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
                         float wsum = 0.f;
                         if (m != -INFINITY) {
-                            // two splits' loads in flight at a time
-                            constexpr int kFly = 2;
                             for (int sp = 0; sp < p.splits; sp += kFly) {
-                                float4 v[kFly][8];
+                                float4 v[kFly][kSliceChunks];
                                 float w[kFly];
 #pragma unroll
                                 for (int u = 0; u < kFly; ++u) {
@@ -790,14 +816,15 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                                     const float4* src = reinterpret_cast<const float4*>(p.o_part) +
                                                         ((size_t)sq * units + unit) * (32 * kM);
 #pragma unroll
-                                    for (int c = 0; c < 8; ++c) v[u][c] = __ldcg(src + ((oc >> 2) + c) * kM + rt);
+                                    for (int c = 0; c < kSliceChunks; ++c)
+                                        v[u][c] = __ldcg(src + ((c0 >> 2) + c) * kM + rt);
                                 }
 #pragma unroll
                                 for (int u = 0; u < kFly; ++u) {
                                     if (w[u] == 0.f) continue;  // (a split without visible keys holds zeros)
                                     wsum += w[u];
 #pragma unroll
-                                    for (int c = 0; c < 8; ++c) {
+                                    for (int c = 0; c < kSliceChunks; ++c) {
                                         acc[c][0] += w[u] * v[u][c].x;
                                         acc[c][1] += w[u] * v[u][c].y;
                                         acc[c][2] += w[u] * v[u][c].z;
@@ -808,17 +835,37 @@ __global__ void __launch_bounds__(C::kThreads, C::kCtasPerSm)
                         }
                         const float wi = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
-                        for (int c = 0; c < 8; c += 2)
-                            *reinterpret_cast<uint4*>(stage + rt * 256 + (oc + c * 4) * 2) = make_uint4(
+                        for (int c = 0; c < kSliceChunks; c += 2)
+                            *reinterpret_cast<uint4*>(stage + rt * 256 + (c0 + c * 4) * 2) = make_uint4(
                                 pack_bf16(acc[c][0] * wi, acc[c][1] * wi), pack_bf16(acc[c][2] * wi, acc[c][3] * wi),
                                 pack_bf16(acc[c + 1][0] * wi, acc[c + 1][1] * wi),
                                 pack_bf16(acc[c + 1][2] * wi, acc[c + 1][3] * wi));
+                        group_sync<kGroupThreads>(t);
+                        // coalesced copy of the slice's 64 bytes of every row
+                        for (int e = gtid; e < kM * 4; e += kGroupThreads) {
+                            const int rr = e >> 2, c = 4 * sl + (e & 3);
+                            const int pr = row0 + rr;
+                            if (pr >= nrows) continue;
+                            __nv_bfloat16* orow = p.out + (size_t)b * p.so_b + (size_t)(pr / p.G) * p.so_n +
+                                                  (size_t)(hk * p.G + pr % p.G) * p.so_h;
+                            *reinterpret_cast<uint4*>(orow + c * 8) =
+                                *reinterpret_cast<const uint4*>(stage + rr * 256 + c * 16);
+                        }
+                    }
+                }
+                group_sync<kGroupThreads>(t);
+                if (gtid == 0) {
+                    __threadfence();  // this split's claims come before its finish
+                    if (atomicAdd(tk + 2, 1u) == (unsigned int)(p.splits - 1)) {
+                        tk[0] = 0u;  // every split is past its last use of the counters: ready for the next launch
+                        tk[1] = 0u;
+                        tk[2] = 0u;
                     }
                 }
             }
-            // coalesced copy of the staged bf16 rows to out (one split, or the merging CTA)
+            // coalesced copy of the staged bf16 rows to out (one split)
             group_sync<kGroupThreads>(t);
-            if (p.splits == 1 || shared_flags[t]) {
+            if (p.splits == 1) {
                 for (int e = gtid; e < kM * 16; e += kGroupThreads) {
                     const int rr = e >> 4, c = e & 15;
                     const int pr = row0 + rr;
