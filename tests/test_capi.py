@@ -35,3 +35,13 @@ def test_error_path_without_gpu_reports_status():
     assert rc == 2 and b"limits" in lib.mfd_last_error()
     ws = lib.mfd_topk_logz_workspace(128, 151936, 64)
     assert ws > 0
+
+
+def test_attention_ticket_words_cover_the_merge_counters():
+    """mfd_tree_attention_tickets: three counters (arrived, claimed, finished) per (request, KV head, M-tile) of
+    128 packed rows (node x query head of the KV head's group), a host-only computation."""
+    lib = _lib.load()
+    for bs, n, H, Hkv in [(1, 65, 32, 8), (256, 65, 32, 8), (3, 17, 16, 16), (2, 129, 8, 2)]:
+        G = H // Hkv
+        mtiles = (n * G + 127) // 128
+        assert lib.mfd_tree_attention_tickets(bs, n, H, Hkv) == 3 * bs * Hkv * mtiles
