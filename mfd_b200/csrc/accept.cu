@@ -343,10 +343,10 @@ __global__ void __launch_bounds__(kGreedyThreads) greedy_kernel(Params p) {
     if (threadIdx.x == 0) p.tickets[b] = 0u;
 }
 
-constexpr int kSampleThreads = 512;
-constexpr int kSampleCtasPerSm = 3;  // (40 registers a thread)
+constexpr int kSampleThreads = 256;
+constexpr int kSampleCtasPerSm = 6;  // (40 registers a thread)
 constexpr int kSampleWarps = kSampleThreads / 32;
-constexpr int kMaxRounds = 96;  // rows up to 96 rounds x 512 threads x 8 logits = 393216 logits
+constexpr int kMaxRounds = 192;  // rows up to 192 rounds x 256 threads x 8 logits = 393216 logits
 constexpr int kUnroll = 4;      // rounds whose loads are in flight together
 
 // the 8 logits of vector v (elements 8v .. 8v+7 of the row); absent elements read as -inf
@@ -370,11 +370,12 @@ __device__ __forceinline__ double shfl_f64(double v, int src) {
     return __longlong_as_double((long long)shfl_u64((uint64_t)__double_as_longlong(v), src));
 }
 
-// stochastic: one 512-thread CTA per row (three resident per SM, so a CTA's serial search holds a third of an SM's
-// warps).  One pass over the logits: in round r warp w reduces block e = 16 r + w (vector 32 e + lane per lane,
-// so every load is coalesced): the block maximum by
-// warp shuffles, the lane sums of the weights against it, and their butterfly sum; lane 0 keeps (M_b, S_b) in
-// shared memory.  Warp 0 then forms the block weights, the run sums and Z in the rule's order and locates the
+// stochastic: one 256-thread CTA per row (six resident per SM, so a CTA's serial search holds a sixth of an SM's
+// warps; 512-thread CTAs, three per SM, measured 2% slower).  One pass over the logits: in round r warp w reduces
+// block e = 8 r + w (vector 32 e + lane per lane, so every load is coalesced): the block maximum by warp
+// shuffles, the lane sums of the weights against it, and their butterfly sum; lane 0 keeps (M_b, S_b) in shared
+// memory.  A block's arithmetic does not depend on which warp reduces it, so the CTA size leaves the rule's bits
+// unchanged.  Warp 0 then forms the block weights, the run sums and Z in the rule's order and locates the
 // target run -> block -> lane -> logit (re-reading one block of 256 logits).
 template <bool UNIT_T>  // temperature exactly 1 (then 1 / T is exactly 1)
 __global__ void __launch_bounds__(kSampleThreads, kSampleCtasPerSm) sample_kernel(Params p) {
