@@ -9,7 +9,7 @@ compiles each with torch.utils.cpp_extension.load_inline into oracle/_ref/, exac
 reference's own tests build them (tests/test_sglang_tree_builder.py:28-48).  The resulting .so files are
 git-ignored but travel to the GPU box, where `load()` imports them without the reference mounted.
 
-    python oracle/build_ref.py            # needs /root/reference; no-op if it is absent
+    python oracle/build_ref.py            # needs the reference checkout (MFD_REFERENCE_ROOT); no-op without it
 """
 
 from __future__ import annotations

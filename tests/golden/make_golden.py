@@ -1,6 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container where the reference is mounted (default /root/reference, or MFD_REFERENCE_ROOT):
+Run in a container where the reference checkout is mounted (its root in MFD_REFERENCE_ROOT, else the mount
+point the build container uses):
 
     python tests/golden/make_golden.py
 
